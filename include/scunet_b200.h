@@ -1,0 +1,141 @@
+/*
+ * scunet_b200 — B200 (sm_100a) SCUNet forward pass behind a C ABI.
+ *
+ * This is the device side of the reference's `Backend` trait
+ * (scunet-rs src/backend.rs:19-56) for the CUDA backend that `Cuda::new` /
+ * `Cuda::forward` (src/cuda.rs:192-241, 1606-1848) implement today. A Rust
+ * `impl Backend for B200` (or any other host) binds these symbols; nothing here
+ * takes a torch, Rust or C++ type: plain pointers, sizes and status codes.
+ *
+ * Conventions
+ *  - Every function returning int returns 0 on success and a negative SCB_E*
+ *    code on failure; the message is then available from scb_last_error().
+ *    Nothing here aborts the process (the reference panics on a device OOM,
+ *    src/cuda.rs:346-360, and on a missing weight, src/weights.rs:309-314).
+ *  - One context owns one device's weights, streams and scratch arena. A context
+ *    is used by one host thread at a time (the reference serialises on a mutex,
+ *    tests/device_lock.rs:7-14). Independent contexts on different devices run
+ *    concurrently (batch sharding: one context per GPU).
+ *  - Images are NCHW float32 in [0,1] (or uint8 where stated); the network's
+ *    arithmetic is fp16 tensor-core operands with fp32 accumulation and an fp32
+ *    residual stream.
+ */
+#ifndef SCUNET_B200_H
+#define SCUNET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct scb_ctx scb_ctx;
+
+/* One named weight tensor, C-order float32, as `Weights::t(name)` hands it out
+ * (src/weights.rs:312-314). Names and shapes: src/weights.rs:207-263. */
+typedef struct {
+  const char* name;
+  const float* data;
+  int ndim;
+  int64_t shape[4];
+} scb_tensor;
+
+enum {
+  SCB_OK = 0,
+  SCB_EINVAL = -1,    /* bad argument, shape or geometry */
+  SCB_ENOWEIGHT = -2, /* a required tensor is missing */
+  SCB_ECUDA = -3,     /* CUDA runtime / driver error */
+  SCB_ENOMEM = -4,    /* device allocation refused (admission, scb_need_bytes) */
+  SCB_EDEVICE = -5    /* a kernel reported a failure through the device error word */
+};
+
+enum { SCB_F32 = 0, SCB_U8 = 1 };
+
+/* Validate, repack (fp16 K-major tiles) and upload every weight once.
+ * Replaces `Cuda::new(&Weights)` (src/cuda.rs:192-241). `config` is the seven
+ * per-stage block counts ([4]*7 for every published checkpoint); dim 64,
+ * head_dim 32, window 8 are the only supported values (src/weights.rs:204-280).
+ * On failure *out is NULL and the message is in scb_last_error(NULL). */
+int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int head_dim, int window,
+               const int config[7], int device, scb_ctx** out);
+
+/* `Backend::forward` (src/backend.rs:19-25; src/cuda.rs:1606-1848): x is the
+ * already replicate-padded [c][hp][wp] float32 host plane (hp, wp multiples of
+ * 64), y receives the same shape. Synchronous. */
+int scb_forward(scb_ctx* ctx, const float* x_nchw, int c, int hp, int wp, float* y_nchw);
+
+/* Batched device-pointer forward with the pad and crop fused
+ * (`backend::run`, src/backend.rs:63-105, for n images at once): x is
+ * [n][c][h][w] (x_dtype SCB_U8 or SCB_F32) and y is [n][c][h][w] (y_dtype
+ * SCB_F32, or SCB_U8 quantised as clamp(v,0,1)*255+0.5 truncated,
+ * src/image.rs:60-63). Both are device pointers. Asynchronous on `stream`
+ * (a cudaStream_t; NULL = the context's own stream). */
+int scb_forward_dev(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype,
+                    void* stream);
+
+/* Same as scb_forward_dev with host pointers: copies in, runs, copies out,
+ * synchronises (the end-to-end call a host application makes). */
+int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype);
+
+/* Device bytes a forward of n images of hp x wp needs beyond the weights
+ * (`memguard::device_need`, src/memguard.rs:66-74). Pure arithmetic. */
+int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes);
+
+/* `Backend::footprint` (src/backend.rs:27-31): device bytes held now. */
+void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_bytes);
+
+/* `Backend::release_scratch` (src/backend.rs:46-55): drop the arena. */
+void scb_release_scratch(scb_ctx* ctx);
+
+/* Message of the last failure on ctx (or of the last failed scb_create when ctx
+ * is NULL); "" when the last call succeeded. */
+const char* scb_last_error(const scb_ctx* ctx);
+
+void scb_destroy(scb_ctx* ctx);
+
+/* ---- single-op probes: the device ops one at a time on caller-owned device
+ * buffers, for parity tests (the reference's `op_probe`, `linear_probe`,
+ * `attention_kernel_probe` and `block_dump`, src/cuda.rs:1246-1468). All
+ * pointers are device pointers; activations are NHWC (pixel-major). ---- */
+
+/* out[m][n] = act(sum_k a[m][k] * b[n][k] + bias[n]) (+ res16[m][n]); fp16 a, b,
+ * res16, out16; fp32 bias, out32 (either output may be NULL). act 0/1/2 =
+ * none/ReLU/GELU-erf. K, N multiples of 32 / 16. */
+int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16, int N, const float* bias, int act,
+                   const void* res16, void* out16, float* out32);
+
+/* 3x3 stride-1 zero-pad-1 conv, no bias: x16 [n][H][W][cin] -> [n][H][W][cout];
+ * w16 [cout][ky][kx][cin]. act as above; res16 added after act when non-NULL. */
+int scb_probe_conv3x3(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin, const void* w16, int cout,
+                      int act, const void* res16, void* out16);
+
+/* 2x2 stride-2 conv: x16 [n][H][W][cin] -> out32/out16 [n][H/2][W/2][cout];
+ * w16 [cout][dy][dx][cin]. */
+int scb_probe_down2(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin, const void* w16, int cout,
+                    float* out32, void* out16);
+
+/* 2x2 stride-2 transposed conv: x16 [n][h][w][cin] -> [n][2h][2w][cout];
+ * w16 [(dy, dx, cout)][cin]. */
+int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, const void* w16, int cout,
+                  float* out32, void* out16);
+
+/* Window attention: qkv16 [n][H][W][3t] (q | k | v column blocks) ->
+ * out16 [n][H][W][t]; rp float32 [t/32][15][15]; shift 0 (W) or 4 (SW). */
+int scb_probe_attention(scb_ctx* ctx, const void* qkv16, int n, int H, int W, int t, int shift, const float* rp,
+                        void* out16);
+
+/* One ConvTransBlock with the context's weights: `stage` 0..6 (down1, down2,
+ * down3, body, up3, up2, up1), `index` 0..3 within the stage; x32 [n][H][W][c]
+ * float32 is read and y32 written (may alias). shift follows the block index
+ * (odd = SW), as the reference walker does (src/cuda.rs:1702, 1775, 1811-1817). */
+int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n, int H, int W, float* y32);
+
+/* Number of kernel launches the last forward issued (for launch accounting). */
+int scb_last_launch_count(const scb_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCUNET_B200_H */

@@ -1,0 +1,209 @@
+"""Host-side mirror of the reference's `Backend` boundary over the C ABI.
+
+`B200` is the device backend behind `include/scunet_b200.h`, shaped like the
+reference's `trait Backend` (scunet-rs `src/backend.rs:19-56`): `name()`,
+`forward(x, plan)` on an already padded `[c][hp][wp]` plane, `footprint()`,
+`release_scratch()`. `run()` is `backend::run` (`src/backend.rs:63-105`): size
+check, admission against free device memory, replicate pad, forward, length check,
+crop. Errors are `BackendError` carrying the library's message (the reference's
+`Result<_, String>`).
+
+There is no CPU fallback: constructing `B200` without the built library, or on a
+machine without a B200, raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+from . import plan as _plan
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libscunet_b200.so"
+
+SCB_F32, SCB_U8 = 0, 1
+SYMBOLS = [
+    "scb_create", "scb_forward", "scb_forward_dev", "scb_forward_host", "scb_need_bytes", "scb_footprint",
+    "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
+    "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
+]
+
+
+class BackendError(RuntimeError):
+    pass
+
+
+class ScbTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", ctypes.POINTER(ctypes.c_float)), ("ndim", ctypes.c_int),
+                ("shape", ctypes.c_int64 * 4)]
+
+
+_lib = None
+
+
+def load_library(path=None):
+    """dlopen the C-ABI library and declare every entry point's signature."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise BackendError(f"{p} is not built (python scunet-rs_b200/build.py)")
+    lib = ctypes.CDLL(str(p))
+    vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    fp = ctypes.POINTER(ctypes.c_float)
+    lib.scb_create.argtypes = [ctypes.POINTER(ScbTensor), i, i, i, i, i, ctypes.POINTER(ctypes.c_int), i,
+                               ctypes.POINTER(vp)]
+    lib.scb_forward.argtypes = [vp, fp, i, i, i, fp]
+    lib.scb_forward_dev.argtypes = [vp, vp, i, i, i, i, i, vp, i, vp]
+    lib.scb_forward_host.argtypes = [vp, vp, i, i, i, i, i, vp, i]
+    lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
+    lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
+    lib.scb_footprint.restype = None
+    lib.scb_release_scratch.argtypes = [vp]
+    lib.scb_release_scratch.restype = None
+    lib.scb_last_error.argtypes = [vp]
+    lib.scb_last_error.restype = ctypes.c_char_p
+    lib.scb_destroy.argtypes = [vp]
+    lib.scb_destroy.restype = None
+    lib.scb_last_launch_count.argtypes = [vp]
+    lib.scb_probe_gemm.argtypes = [vp, vp, i, i, vp, i, vp, i, vp, vp, vp]
+    lib.scb_probe_conv3x3.argtypes = [vp, vp, i, i, i, i, vp, i, i, vp, vp]
+    lib.scb_probe_down2.argtypes = [vp, vp, i, i, i, i, vp, i, vp, vp]
+    lib.scb_probe_up2.argtypes = [vp, vp, i, i, i, i, vp, i, vp, vp]
+    lib.scb_probe_attention.argtypes = [vp, vp, i, i, i, i, i, vp, vp]
+    lib.scb_probe_block.argtypes = [vp, i, i, vp, i, i, i, vp]
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def need_bytes(n, in_nc, hp, wp):
+    """`memguard::device_need` (`src/memguard.rs:66-74`) for the B200 arena."""
+    lib = load_library()
+    out = ctypes.c_size_t(0)
+    if lib.scb_need_bytes(n, in_nc, hp, wp, ctypes.byref(out)) != 0:
+        raise BackendError(f"no arena for {n} x {hp}x{wp}")
+    return out.value
+
+
+class B200:
+    """The B200 device backend (`impl Backend`, `src/backend.rs:19-56`)."""
+
+    def __init__(self, weights, device=0):
+        self.lib = load_library()
+        self.weights = weights
+        self.in_nc = weights.in_nc
+        self.device = device
+        names, self._keep = [], []
+        arr = (ScbTensor * len(weights.tensors))()
+        for k, (name, a) in enumerate(weights.tensors.items()):
+            a = np.ascontiguousarray(a, np.float32)
+            self._keep.append(a)
+            nm = name.encode()
+            names.append(nm)
+            arr[k].name = nm
+            arr[k].data = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            arr[k].ndim = a.ndim
+            for d in range(4):
+                arr[k].shape[d] = a.shape[d] if d < a.ndim else 0
+        cfg = (ctypes.c_int * 7)(*weights.config)
+        ctx = ctypes.c_void_p()
+        rc = self.lib.scb_create(arr, len(weights.tensors), weights.in_nc, weights.dim, weights.head_dim,
+                                 weights.window, cfg, device, ctypes.byref(ctx))
+        self._names = names
+        if rc != 0:
+            raise BackendError(f"scb_create: {self.lib.scb_last_error(None).decode()}")
+        self.ctx = ctx
+        self._keep = None  # weights are on the device now
+
+    # -- the trait ------------------------------------------------------------
+    def name(self):
+        return "b200"
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise BackendError(f"{what}: {self.lib.scb_last_error(self.ctx).decode()}")
+
+    def forward(self, x, plan):
+        """`Backend::forward`: padded [c][hp][wp] float32 -> same shape (host arrays)."""
+        x = np.ascontiguousarray(x, np.float32).reshape(self.in_nc, plan.hp, plan.wp)
+        y = np.empty_like(x)
+        fp = ctypes.POINTER(ctypes.c_float)
+        self._check(self.lib.scb_forward(self.ctx, x.ctypes.data_as(fp), self.in_nc, plan.hp, plan.wp,
+                                         y.ctypes.data_as(fp)), "scb_forward")
+        return y
+
+    def footprint(self):
+        w, s = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        self.lib.scb_footprint(self.ctx, ctypes.byref(w), ctypes.byref(s))
+        return w.value, s.value
+
+    def release_scratch(self):
+        self.lib.scb_release_scratch(self.ctx)
+
+    # -- batched paths ----------------------------------------------------------
+    def forward_host(self, x):
+        """[n][c][h][w] uint8 or float32 host array -> float32 [n][c][h][w] (pad and
+        crop fused on the device)."""
+        x = np.ascontiguousarray(x)
+        n, c, h, w = x.shape
+        xd = SCB_U8 if x.dtype == np.uint8 else SCB_F32
+        if xd == SCB_F32:
+            x = x.astype(np.float32, copy=False)
+        y = np.empty((n, c, h, w), np.float32)
+        self._check(self.lib.scb_forward_host(self.ctx, x.ctypes.data, xd, n, c, h, w, y.ctypes.data, SCB_F32),
+                    "scb_forward_host")
+        return y
+
+    def forward_dev(self, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream=0):
+        """Device pointers (e.g. torch tensors' data_ptr()); asynchronous."""
+        self._check(self.lib.scb_forward_dev(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream or None),
+                    "scb_forward_dev")
+
+    def last_launch_count(self):
+        return self.lib.scb_last_launch_count(self.ctx)
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.lib.scb_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def run(be, x, c, h, w, wt):
+    """`backend::run` (`src/backend.rs:63-105`): min-size check, admission, replicate
+    pad, forward, length check, crop. x is [c][h][w] float32 in [0,1]."""
+    p = _plan.Plan.new(h, w, wt.window)
+    _plan.check_min_size(h, w, wt.window)
+    if be.name() == "b200":
+        check_b200(be, p)
+    padded = _plan.pad_replicate(x, c, h, w, p.hp, p.wp)
+    y = be.forward(padded, p)
+    if y.size != c * p.plane():
+        raise BackendError(f"{be.name()}: the backend returned {y.size} floats for a {p.hp}x{p.wp} plane of {c} "
+                           f"channels")
+    return _plan.crop(y, c, h, w, p.hp, p.wp)
+
+
+def check_b200(be, p, n=1):
+    """`memguard::check_cuda` (`src/memguard.rs:262-285`): refuse before allocating
+    when the arena would not fit in free device memory; fail open when the free
+    figure cannot be read."""
+    need = need_bytes(n, be.in_nc, p.hp, p.wp)
+    try:
+        import torch
+        free, _ = torch.cuda.mem_get_info(be.device)
+    except Exception:
+        return
+    have_arena = be.footprint()[1]
+    if need > free + have_arena:
+        raise BackendError(f"{p.h}x{p.w} needs {need / 2**30:.2f} GiB of device scratch, "
+                           f"{(free + have_arena) / 2**30:.2f} GiB available")

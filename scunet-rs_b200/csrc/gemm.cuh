@@ -1,0 +1,371 @@
+// The tensor-core workhorse: D[M x N] = A[M x K] * B[N x K]^T on tcgen05 with the
+// accumulator in TMEM, A and B fp16 K-major tiles landed by TMA (128B/64B
+// swizzle), fp32 accumulate, and a fused epilogue (bias, ReLU/GELU, fp16/fp32
+// residual, fp32 skip add, LayerNorm of a column range, fp16/fp32 stores).
+//
+// One kernel covers every channel-mixing op of the network; only how A's tiles
+// are addressed (GEO_*) and where the epilogue stores a row differ:
+//
+//   GEO_FLAT  1x1 convs and linears: row m = pixel m of an NHWC plane.
+//   GEO_CONV3 3x3 / stride 1 / zero pad 1 conv as an implicit GEMM: an M tile is a
+//             TH x TW block of output pixels of one image; the K loop walks the 9
+//             taps (ky, kx) x channel chunks, each tap a TMA box of the NHWC input
+//             at offset (y+ky-1, x+kx-1). Out-of-range boxes are zero-filled by the
+//             TMA unit, which IS the zero padding.
+//   GEO_DOWN2 2x2 / stride 2 conv: the input viewed as 5-D (C, dx, W/2, dy, rows/2);
+//             tap (dy, dx) of a TH x TW output block is one TMA box.
+//   GEO_UP2   2x2 / stride 2 transposed conv: a plain GEMM over input pixels with
+//             N ordered (dy, dx, c_out); the epilogue scatters each N tile to the
+//             output pixel (2y+dy, 2x+dx) (pixel shuffle).
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
+// UMMA issuer (one elected lane), warps 2..5 = epilogue (thread = accumulator row).
+// The grid is persistent; tiles are strided over CTAs and the two TMEM
+// accumulator buffers let tile i's epilogue overlap tile i+1's main loop.
+#pragma once
+#include <cuda.h>
+#include "ptx.cuh"
+
+namespace scb {
+
+enum Geo : int { GEO_FLAT = 0, GEO_CONV3 = 1, GEO_DOWN2 = 2, GEO_UP2 = 3 };
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
+
+struct GemmGeom {
+  int M;            // rows of A (FLAT/UP2: pixels; CONV3/DOWN2: output pixels, for bounds)
+  int n_total;      // N
+  int num_kb;       // K / BK
+  int kb_per_tap;   // CONV3/DOWN2: channel chunks per tap
+  int m_tiles, n_tiles;
+  // CONV3: per-image plane H x W; DOWN2: stacked output rows H (= n*Ho) x W (= Wo)
+  int H, W, TH, TW, tiles_x, tiles_y;
+  // UP2: input width and c_out
+  int up_w, up_cout;
+};
+
+struct GemmEpi {
+  const float* bias;    // [N] or null
+  int act;              // Act
+  const __half* res16;  // residual, fp16, element (pixel, col) at res16[p*res16_ld + col]
+  long res16_ld;
+  const float* res32;   // residual, fp32
+  long res32_ld;
+  const float* skip32;  // if set, the fp16 store holds (v + skip) and the fp32 store v
+  long skip_ld;
+  __half* out16;
+  long out16_ld;
+  float* out32;
+  long out32_ld;
+  // LayerNorm over global columns [ln_lo, ln_lo + ln_n) of the final value v,
+  // written as fp16 to ln_out[p*ln_ld + (col - ln_lo)].
+  const float* ln_g;
+  const float* ln_b;
+  __half* ln_out;
+  long ln_ld;
+  int ln_lo, ln_n;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+template <int BN, int BK, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + tmem slot + alignment slack
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+};
+
+// Where accumulator row `r` of M tile `mt` lives: returns the output pixel index
+// (or -1 when the row is outside the plane) for a given N-tile base `n0`, and the
+// output column of the tile's first column.
+template <int GEO>
+__device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int n0, int& col0) {
+  col0 = n0;
+  if (GEO == GEO_FLAT) {
+    const long p = (long)mt * 128 + r;
+    return p < g.M ? p : -1;
+  } else if (GEO == GEO_CONV3) {
+    const int per_img = g.tiles_y * g.tiles_x;
+    const int img = mt / per_img;
+    const int rem = mt - img * per_img;
+    const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
+    const int y = ty * g.TH + r / g.TW, x = tx * g.TW + r % g.TW;
+    if (x >= g.W || y >= g.H) return -1;
+    return ((long)img * g.H + y) * g.W + x;
+  } else if (GEO == GEO_DOWN2) {
+    const int ty = mt / g.tiles_x, tx = mt - ty * g.tiles_x;
+    const int y = ty * g.TH + r / g.TW, x = tx * g.TW + r % g.TW;
+    if (x >= g.W || y >= g.H) return -1;
+    return (long)y * g.W + x;
+  } else {  // GEO_UP2
+    const long p = (long)mt * 128 + r;
+    if (p >= g.M) return -1;
+    const long R = p / g.up_w;
+    const int x = (int)(p - R * g.up_w);
+    const int d = n0 / g.up_cout;
+    col0 = n0 - d * g.up_cout;
+    return (2 * R + (d >> 1)) * (2L * g.up_w) + 2 * x + (d & 1);
+  }
+}
+
+template <int BN, int BK, int STAGES, int GEO>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
+               const GemmEpi e) {
+  using L = GemmSmem<BN, BK, STAGES>;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(BK == 64 || BK == 32, "BK is one 128B or 64B swizzle row of fp16");
+  constexpr uint32_t ROWB = BK * 2;
+  constexpr uint32_t SWZ = (BK == 64) ? SW_128B : SW_64B;
+  constexpr uint32_t IDESC = make_idesc_f16(128, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_tiles = g.m_tiles * g.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_fence_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
+        const int n0 = nt * BN;
+        int img = 0, y0 = 0, x0 = 0;
+        if (GEO == GEO_CONV3) {
+          const int per_img = g.tiles_y * g.tiles_x;
+          img = mt / per_img;
+          const int rem = mt - img * per_img;
+          const int ty = rem / g.tiles_x;
+          y0 = ty * g.TH;
+          x0 = (rem - ty * g.tiles_x) * g.TW;
+        } else if (GEO == GEO_DOWN2) {
+          const int ty = mt / g.tiles_x;
+          y0 = ty * g.TH;
+          x0 = (mt - ty * g.tiles_x) * g.TW;
+        }
+        for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
+          uint8_t* sa = smem + s * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          if (GEO == GEO_FLAT || GEO == GEO_UP2) {
+            tma_load_2d(sa, &tmA, &full[s], kb * BK, mt * 128);
+          } else if (GEO == GEO_CONV3) {
+            const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
+            const int ky = tap / 3, kx = tap - ky * 3;
+            tma_load_4d(sa, &tmA, &full[s], ch * BK, x0 + kx - 1, y0 + ky - 1, img);
+          } else {  // GEO_DOWN2
+            const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
+            tma_load_5d(sa, &tmA, &full[s], ch * BK, tap & 1, x0, tap >> 1, y0);
+          }
+          tma_load_2d(sb, &tmB, &full[s], kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t) {
+        const uint32_t a = t & 1, aph = (t >> 1) & 1;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1, SCB_ERR_WAIT_ACC_FREE)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, SCB_ERR_WAIT_FULL)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_f16(d_tmem, make_sdesc(sa + k * 32, ROWB, SWZ), make_sdesc(sb + k * 32, ROWB, SWZ), IDESC,
+                     (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[a]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, thread = accumulator row ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    uint32_t t = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
+      const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
+      const int n0 = nt * BN;
+      const uint32_t a = t & 1, aph = (t >> 1) & 1;
+      if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
+      tc_fence_after();
+      int col0;
+      const long p = row_pixel<GEO>(g, mt, r, n0, col0);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+      const bool do_ln = e.ln_out != nullptr && e.ln_lo >= n0 && e.ln_lo < n0 + BN;
+      float ln_sum = 0.f, ln_sq = 0.f, ln_shift = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tbase + c, v);
+        const int n = n0 + c;       // global GEMM column
+        const int oc = col0 + c;    // output column
+        if (e.bias) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += __ldg(e.bias + n + j);
+        }
+        if (e.act == ACT_RELU) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
+        } else if (e.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
+        }
+        if (p >= 0) {
+          if (e.res16) {
+            const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + oc);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint4 u = __ldg(src + h);
+              const __half2* hp = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float2 f = __half22float2(hp[j]);
+                v[h * 8 + 2 * j] += f.x;
+                v[h * 8 + 2 * j + 1] += f.y;
+              }
+            }
+          }
+          if (e.res32) {
+            const float4* src = reinterpret_cast<const float4*>(e.res32 + p * e.res32_ld + oc);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              float4 f = __ldg(src + h);
+              v[4 * h] += f.x; v[4 * h + 1] += f.y; v[4 * h + 2] += f.z; v[4 * h + 3] += f.w;
+            }
+          }
+          if (e.out32) {
+            float4* dst = reinterpret_cast<float4*>(e.out32 + p * e.out32_ld + oc);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) dst[h] = make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+          }
+          if (e.out16) {
+            float s[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s[j] = v[j];
+            if (e.skip32) {
+              const float4* sk = reinterpret_cast<const float4*>(e.skip32 + p * e.skip_ld + oc);
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                float4 f = __ldg(sk + h);
+                s[4 * h] += f.x; s[4 * h + 1] += f.y; s[4 * h + 2] += f.z; s[4 * h + 3] += f.w;
+              }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(e.out16 + p * e.out16_ld + oc);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              dst[h] = make_uint4(pack_half2(s[8 * h], s[8 * h + 1]), pack_half2(s[8 * h + 2], s[8 * h + 3]),
+                                  pack_half2(s[8 * h + 4], s[8 * h + 5]), pack_half2(s[8 * h + 6], s[8 * h + 7]));
+          }
+        }
+        if (do_ln && n >= e.ln_lo && n < e.ln_lo + e.ln_n) {
+          if (n == e.ln_lo) ln_shift = v[0];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float d = v[j] - ln_shift;
+            ln_sum += d;
+            ln_sq += d * d;
+          }
+        }
+      }
+      if (do_ln) {
+        // Second pass over the LN columns: recompute v exactly as above and normalise.
+        const float inv_n = 1.f / (float)e.ln_n;
+        const float md = ln_sum * inv_n;
+        const float var = fmaxf(ln_sq * inv_n - md * md, 0.f);
+        const float mean = ln_shift + md;
+        const float rstd = rsqrtf(var + 1e-5f);
+#pragma unroll 1
+        for (int c = e.ln_lo - n0; c < e.ln_lo - n0 + e.ln_n; c += 16) {
+          float v[16];
+          tmem_ld16(tbase + c, v);
+          const int n = n0 + c;
+          const int oc = col0 + c;
+          if (e.bias) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += __ldg(e.bias + n + j);
+          }
+          if (p >= 0) {
+            if (e.res16) {
+              const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + oc);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint4 u = __ldg(src + h);
+                const __half2* hp = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  float2 f = __half22float2(hp[j]);
+                  v[h * 8 + 2 * j] += f.x;
+                  v[h * 8 + 2 * j + 1] += f.y;
+                }
+              }
+            }
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int k = n + j - e.ln_lo;
+              o[j] = (v[j] - mean) * rstd * __ldg(e.ln_g + k) + __ldg(e.ln_b + k);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(e.ln_out + p * e.ln_ld + (n - e.ln_lo));
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              dst[h] = make_uint4(pack_half2(o[8 * h], o[8 * h + 1]), pack_half2(o[8 * h + 2], o[8 * h + 3]),
+                                  pack_half2(o[8 * h + 4], o[8 * h + 5]), pack_half2(o[8 * h + 6], o[8 * h + 7]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace scb

@@ -1,0 +1,1120 @@
+// scunet_b200: the C-ABI (include/scunet_b200.h), weight repack, the per-geometry
+// arena and op plan, and the U-Net walker that replaces `Cuda::forward`
+// (scunet-rs src/cuda.rs:1606-1848) with the same stage order:
+//
+//   x1 = head(pad(x))                                   (tools/network_scunet.py:247)
+//   x2 = down1(x1), x3 = down2(x2), x4 = down3(x3)      4 blocks + 2x2 s2 conv each
+//   b  = body(x4)                                       4 blocks
+//   y  = up3(b + x4), up2(y + x3), up1(y + x2)          2x2 transposed conv + 4 blocks
+//   out = crop(tail(y + x1))
+//
+// Activations live in HBM as NHWC: the residual stream and the four U-Net skips in
+// fp32, every other intermediate in fp16 (it is only ever a tensor-core operand).
+// Each GEMM epilogue that produces the residual stream also writes its fp16
+// "shadow" - the A operand of the next GEMM - and the last block of body/up3/up2/
+// up1 writes the shadow of (x + skip) directly, which is the skip add that
+// upstream performs before each up conv and before the tail.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/scunet_b200.h"
+#include "attn.cuh"
+#include "gemm.cuh"
+#include "io_kernels.cuh"
+
+using namespace scb;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+// --------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched through the runtime, so the library
+// links no libcuda and loads on a machine without a driver).
+// --------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn(std::string& err) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn) return fn;
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
+    err = "cuTensorMapEncodeTiled is not available from the driver";
+    return nullptr;
+  }
+  fn = reinterpret_cast<EncodeTiledFn>(p);
+  return fn;
+}
+
+bool encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                const uint32_t* box, int bk, std::string& err) {
+  EncodeTiledFn fn = encode_fn(err);
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) s[i] = strides[i];
+  }
+  const CUtensorMapSwizzle swz = bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), d, s, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d), rank %d, dims %llu x %llu", (int)r, rank,
+             (unsigned long long)dims[0], (unsigned long long)dims[1]);
+    err = buf;
+    return false;
+  }
+  return true;
+}
+
+// --------------------------------------------------------------------------
+// GEMM op: tiles, maps, dispatch over the compiled (BN, BK, GEO) variants
+// --------------------------------------------------------------------------
+constexpr int stages_for(int bn, int bk) {
+  return (196608 / ((128 + bn) * bk * 2)) > 8 ? 8 : (196608 / ((128 + bn) * bk * 2));
+}
+
+struct GemmOp {
+  int geo = GEO_FLAT, bn = 64, bk = 64;
+  CUtensorMap ta, tb;
+  GemmGeom g{};
+  GemmEpi e{};
+};
+
+template <int BN, int BK, int GEO>
+cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
+  constexpr int S = stages_for(BN, BK);
+  using L = GemmSmem<BN, BK, S>;
+  auto kfn = gemm_tc_kernel<BN, BK, S, GEO>;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = op.g.m_tiles * op.g.n_tiles;
+  const int grid = std::max(1, std::min(tiles, sms));
+  kfn<<<grid, 192, L::TOTAL, st>>>(op.ta, op.tb, op.g, op.e);
+  return cudaGetLastError();
+}
+
+#define SCB_GEMM_CASE(BN, BK, GEO) \
+  if (op.bn == BN && op.bk == BK && op.geo == GEO) return launch_t<BN, BK, GEO>(op, sms, st);
+
+cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
+  SCB_GEMM_CASE(32, 32, GEO_FLAT)
+  SCB_GEMM_CASE(32, 64, GEO_FLAT)
+  SCB_GEMM_CASE(64, 64, GEO_FLAT)
+  SCB_GEMM_CASE(96, 32, GEO_FLAT)
+  SCB_GEMM_CASE(128, 32, GEO_FLAT)
+  SCB_GEMM_CASE(128, 64, GEO_FLAT)
+  SCB_GEMM_CASE(192, 64, GEO_FLAT)
+  SCB_GEMM_CASE(256, 64, GEO_FLAT)
+  SCB_GEMM_CASE(64, 64, GEO_UP2)
+  SCB_GEMM_CASE(128, 64, GEO_UP2)
+  SCB_GEMM_CASE(256, 64, GEO_UP2)
+  SCB_GEMM_CASE(32, 32, GEO_CONV3)
+  SCB_GEMM_CASE(64, 64, GEO_CONV3)
+  SCB_GEMM_CASE(128, 64, GEO_CONV3)
+  SCB_GEMM_CASE(256, 64, GEO_CONV3)
+  SCB_GEMM_CASE(128, 64, GEO_DOWN2)
+  SCB_GEMM_CASE(256, 64, GEO_DOWN2)
+  return cudaErrorInvalidConfiguration;
+}
+
+bool gemm_supported(int geo, int bn, int bk) {
+  static const int tab[][3] = {{32, 32, GEO_FLAT},   {32, 64, GEO_FLAT},   {64, 64, GEO_FLAT},   {96, 32, GEO_FLAT},
+                               {128, 32, GEO_FLAT},  {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
+                               {64, 64, GEO_UP2},    {128, 64, GEO_UP2},   {256, 64, GEO_UP2},   {32, 32, GEO_CONV3},
+                               {64, 64, GEO_CONV3},  {128, 64, GEO_CONV3}, {256, 64, GEO_CONV3}, {128, 64, GEO_DOWN2},
+                               {256, 64, GEO_DOWN2}};
+  for (auto& r : tab)
+    if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
+  return false;
+}
+
+int pick_bn(int N) {
+  if (N <= 256 && (N == 32 || N == 64 || N == 96 || N == 128 || N == 192 || N == 256)) return N;
+  if (N % 256 == 0) return 256;
+  if (N % 192 == 0) return 192;
+  if (N % 128 == 0) return 128;
+  if (N % 64 == 0) return 64;
+  return 32;
+}
+
+// Output-block tile for the spatial GEMMs: TW x TH = 128 pixels, TW the widest
+// power of two <= 128 that divides W (16 with edge masking otherwise).
+void pick_tile(int W, int& TW, int& TH) {
+  TW = 16;
+  for (int c : {128, 64, 32, 16})
+    if (W % c == 0) {
+      TW = c;
+      break;
+    }
+  TH = 128 / TW;
+}
+
+struct Maker {
+  std::string* err;
+  bool ok = true;
+
+  bool mapB(GemmOp& op, const __half* w, int N, int K) {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t str[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {(uint32_t)op.bk, (uint32_t)op.bn};
+    return encode_map(&op.tb, w, 2, dims, str, box, op.bk, *err);
+  }
+
+  // Plain GEMM over M rows of an fp16 [M][lda] matrix (first K columns).
+  bool flat(GemmOp& op, const __half* a, long M, int K, long lda, const __half* w, int N, int geo = GEO_FLAT) {
+    op.geo = geo;
+    op.bk = (K % 64 == 0) ? 64 : 32;
+    op.bn = pick_bn(N);
+    if (geo == GEO_UP2) op.bn = std::min(op.bn, op.g.up_cout);
+    if (!gemm_supported(op.geo, op.bn, op.bk) || K % 32 || N % op.bn) {
+      *err = "no GEMM variant for N=" + std::to_string(N) + " K=" + std::to_string(K);
+      return false;
+    }
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t str[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {(uint32_t)op.bk, 128};
+    if (!encode_map(&op.ta, a, 2, dims, str, box, op.bk, *err)) return false;
+    if (!mapB(op, w, N, K)) return false;
+    op.g.M = (int)M;
+    op.g.n_total = N;
+    op.g.num_kb = K / op.bk;
+    op.g.kb_per_tap = op.g.num_kb;
+    op.g.m_tiles = (int)((M + 127) / 128);
+    op.g.n_tiles = N / op.bn;
+    return true;
+  }
+
+  // 3x3 implicit GEMM over n images of H x W, input channels [0, cin) of an fp16
+  // NHWC buffer whose pixel stride is pix_ld elements.
+  bool conv3(GemmOp& op, const __half* x, int n, int H, int W, int cin, long pix_ld, const __half* w, int cout) {
+    op.geo = GEO_CONV3;
+    op.bk = (cin % 64 == 0) ? 64 : 32;
+    op.bn = cout;
+    if (!gemm_supported(op.geo, op.bn, op.bk) || cin % 32) {
+      *err = "no conv3x3 variant for cin=" + std::to_string(cin) + " cout=" + std::to_string(cout);
+      return false;
+    }
+    int TW, TH;
+    pick_tile(W, TW, TH);
+    const uint64_t dims[4] = {(uint64_t)cin, (uint64_t)W, (uint64_t)H, (uint64_t)n};
+    const uint64_t str[3] = {(uint64_t)pix_ld * 2, (uint64_t)W * pix_ld * 2, (uint64_t)H * W * pix_ld * 2};
+    const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)TH, 1};
+    if (!encode_map(&op.ta, x, 4, dims, str, box, op.bk, *err)) return false;
+    if (!mapB(op, w, cout, 9 * cin)) return false;
+    op.g.M = n * H * W;
+    op.g.n_total = cout;
+    op.g.kb_per_tap = cin / op.bk;
+    op.g.num_kb = 9 * op.g.kb_per_tap;
+    op.g.H = H;
+    op.g.W = W;
+    op.g.TH = TH;
+    op.g.TW = TW;
+    op.g.tiles_x = (W + TW - 1) / TW;
+    op.g.tiles_y = H / TH;
+    op.g.m_tiles = n * op.g.tiles_y * op.g.tiles_x;
+    op.g.n_tiles = 1;
+    return true;
+  }
+
+  // 2x2 stride-2 conv of an fp16 NHWC [n*H][W][cin] plane (contiguous).
+  bool down2(GemmOp& op, const __half* x, int n, int H, int W, int cin, const __half* w, int cout) {
+    op.geo = GEO_DOWN2;
+    op.bk = 64;
+    op.bn = pick_bn(cout);
+    if (!gemm_supported(op.geo, op.bn, op.bk) || cin % 64) {
+      *err = "no down-conv variant for cin=" + std::to_string(cin);
+      return false;
+    }
+    const int Ho = H / 2, Wo = W / 2, rows = n * Ho;
+    int TW, TH;
+    pick_tile(Wo, TW, TH);
+    const uint64_t dims[5] = {(uint64_t)cin, 2, (uint64_t)Wo, 2, (uint64_t)rows};
+    const uint64_t str[4] = {(uint64_t)cin * 2, (uint64_t)cin * 4, (uint64_t)W * cin * 2, (uint64_t)W * cin * 4};
+    const uint32_t box[5] = {(uint32_t)op.bk, 1, (uint32_t)TW, 1, (uint32_t)TH};
+    if (!encode_map(&op.ta, x, 5, dims, str, box, op.bk, *err)) return false;
+    if (!mapB(op, w, cout, 4 * cin)) return false;
+    op.g.M = rows * Wo;
+    op.g.n_total = cout;
+    op.g.kb_per_tap = cin / op.bk;
+    op.g.num_kb = 4 * op.g.kb_per_tap;
+    op.g.H = rows;
+    op.g.W = Wo;
+    op.g.TH = TH;
+    op.g.TW = TW;
+    op.g.tiles_x = (Wo + TW - 1) / TW;
+    op.g.tiles_y = (rows + TH - 1) / TH;
+    op.g.m_tiles = op.g.tiles_y * op.g.tiles_x;
+    op.g.n_tiles = cout / op.bn;
+    return true;
+  }
+
+  bool up2(GemmOp& op, const __half* x, int n, int h, int w, int cin, const __half* wt, int cout) {
+    op.g.up_w = w;
+    op.g.up_cout = cout;
+    return flat(op, x, (long)n * h * w, cin, cin, wt, 4 * cout, GEO_UP2);
+  }
+};
+
+// --------------------------------------------------------------------------
+// Weights on the device
+// --------------------------------------------------------------------------
+struct BlockW {
+  int c = 0;
+  __half *w11, *w12, *wc0, *wc2, *wqkv, *wproj, *w0, *w2;
+  float *b11, *b12, *bqkv, *bproj, *b0, *b2, *ln1g, *ln1b, *ln2g, *ln2b, *rp;
+};
+
+const char* kStageName[7] = {"down1", "down2", "down3", "body", "up3", "up2", "up1"};
+const int kStageLevel[7] = {0, 1, 2, 3, 2, 1, 0};
+
+struct Op {
+  enum Kind { GEMM, ATTN, HEAD, TAIL } kind;
+  GemmOp gemm;
+  AttnGeom attn{};
+  const __half* attn_in = nullptr;
+  __half* attn_out = nullptr;
+  const float* attn_rp = nullptr;
+};
+
+struct Arena {
+  int n = 0, hp = 0, wp = 0;
+  char* base = nullptr;
+  size_t bytes = 0;
+  float* skip[4] = {};
+  __half* xs[4] = {};
+  float* xw = nullptr;
+  __half *y = nullptr, *hc = nullptr, *z = nullptr, *a = nullptr, *o = nullptr, *qh = nullptr;
+  float* io_in = nullptr;  // staging for host-pointer forwards
+  float* io_out = nullptr;
+  std::vector<Op> ops;     // head .. tail
+};
+
+size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A) {
+  const size_t P = (size_t)n * hp * wp;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 1023) & ~size_t(1023);
+    return o;
+  };
+  size_t o_skip[4], o_xs[4];
+  for (int s = 0; s < 4; ++s) o_skip[s] = take(P * 256 >> s);
+  for (int s = 0; s < 4; ++s) o_xs[s] = take(P * 128 >> s);
+  size_t o_xw = take(P * 256), o_y = take(P * 128), o_hc = take(P * 64), o_z = take(P * 128), o_a = take(P * 64),
+         o_o = take(P * 64), o_qh = take(P * 256);
+  size_t o_in = take(P * in_nc * 4), o_out = take(P * in_nc * 4);
+  if (A) {
+    char* b = A->base;
+    for (int s = 0; s < 4; ++s) {
+      A->skip[s] = reinterpret_cast<float*>(b + o_skip[s]);
+      A->xs[s] = reinterpret_cast<__half*>(b + o_xs[s]);
+    }
+    A->xw = reinterpret_cast<float*>(b + o_xw);
+    A->y = reinterpret_cast<__half*>(b + o_y);
+    A->hc = reinterpret_cast<__half*>(b + o_hc);
+    A->z = reinterpret_cast<__half*>(b + o_z);
+    A->a = reinterpret_cast<__half*>(b + o_a);
+    A->o = reinterpret_cast<__half*>(b + o_o);
+    A->qh = reinterpret_cast<__half*>(b + o_qh);
+    A->io_in = reinterpret_cast<float*>(b + o_in);
+    A->io_out = reinterpret_cast<float*>(b + o_out);
+  }
+  return off;
+}
+
+}  // namespace
+
+struct scb_ctx {
+  int device = 0, in_nc = 3, dim = 64, sms = 148;
+  int config[7] = {4, 4, 4, 4, 4, 4, 4};
+  cudaStream_t stream = nullptr;
+  std::string err;
+  char* wblob = nullptr;
+  size_t wbytes = 0;
+  std::vector<BlockW> blocks[7];
+  __half* wdown[3] = {};
+  __half* wup[3] = {};
+  float* whead = nullptr;
+  float* wtail = nullptr;
+  Arena arena;
+  int last_launches = 0;
+};
+
+namespace {
+
+int fail(scb_ctx* ctx, int code, const std::string& msg) {
+  if (ctx)
+    ctx->err = msg;
+  else
+    g_create_error = msg;
+  return code;
+}
+
+int cuda_fail(scb_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, SCB_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define CKC(ctx, x, what)                           \
+  do {                                              \
+    cudaError_t _e = (x);                           \
+    if (_e != cudaSuccess) return cuda_fail(ctx, _e, what); \
+  } while (0)
+
+// Host-side weight table lookup with shape check.
+struct Table {
+  std::map<std::string, const scb_tensor*> by_name;
+  std::string err;
+  const float* get(const std::string& name, std::initializer_list<int64_t> shape) {
+    auto it = by_name.find(name);
+    if (it == by_name.end()) {
+      err = "missing tensor " + name;
+      return nullptr;
+    }
+    const scb_tensor* t = it->second;
+    if ((size_t)t->ndim != shape.size()) {
+      err = name + ": rank " + std::to_string(t->ndim) + ", expected " + std::to_string(shape.size());
+      return nullptr;
+    }
+    int i = 0;
+    for (int64_t s : shape) {
+      if (t->shape[i] != s) {
+        err = name + ": dim " + std::to_string(i) + " is " + std::to_string(t->shape[i]) + ", expected " +
+              std::to_string(s);
+        return nullptr;
+      }
+      ++i;
+    }
+    if (!t->data) {
+      err = name + ": null data";
+      return nullptr;
+    }
+    return t->data;
+  }
+};
+
+// Host staging for the weight blob: appends converted arrays, 256-byte aligned.
+struct Blob {
+  std::vector<char> host;
+  size_t put(const void* p, size_t bytes) {
+    size_t off = (host.size() + 255) & ~size_t(255);
+    host.resize(off + bytes);
+    memcpy(host.data() + off, p, bytes);
+    return off;
+  }
+  size_t half(const std::vector<float>& v) {
+    std::vector<__half> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = __float2half_rn(v[i]);
+    return put(h.data(), h.size() * 2);
+  }
+  size_t f32(const float* p, size_t n) { return put(p, n * 4); }
+};
+
+cudaError_t launch_attn(const Op& op, cudaStream_t st) {
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(window_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const unsigned grid = (unsigned)((op.attn.n_windows + 1) / 2);
+  window_attn_kernel<<<grid, 128, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
+  return cudaGetLastError();
+}
+
+// Run the ops of the arena's plan on `st`, with the image pointers of this call.
+int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w, cudaStream_t st) {
+  Arena& A = ctx->arena;
+  int launches = 0;
+  for (const Op& op : A.ops) {
+    cudaError_t e = cudaSuccess;
+    switch (op.kind) {
+      case Op::HEAD: {
+        HeadGeom g{A.n, c, h, w, A.hp, A.wp, x_u8};
+        const long threads = (long)A.n * A.hp * A.wp * 4;
+        head_conv_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, ctx->whead, A.skip[0], A.xs[0], g);
+        e = cudaGetLastError();
+        break;
+      }
+      case Op::TAIL: {
+        TailGeom g{A.n, c, h, w, A.hp, A.wp, y_u8};
+        const long threads = (long)A.n * h * w;
+        tail_conv_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(A.xs[0], ctx->wtail, y, g);
+        e = cudaGetLastError();
+        break;
+      }
+      case Op::GEMM:
+        e = launch_gemm(op.gemm, ctx->sms, st);
+        break;
+      case Op::ATTN:
+        e = launch_attn(op, st);
+        break;
+    }
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
+    ++launches;
+  }
+  ctx->last_launches = launches;
+  return SCB_OK;
+}
+
+// The ops of one ConvTransBlock at stage plane (n, H, W) with c channels.
+//   xin (fp32, shadow already in xs) -> xout (fp32, may alias xin; may be null
+//   when `skip` is given: then only the fp16 shadow of (x + skip) is written).
+bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena& A, int n, int H, int W,
+               const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err) {
+  const int c = bw.c, t = c / 2, cc = c / 2, heads = t / 32;
+  const long P = (long)n * H * W;
+  Maker mk{&err};
+  Op op{};
+  op.kind = Op::GEMM;
+  // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
+  {
+    GemmOp g{};
+    if (!mk.flat(g, xs, P, c, c, bw.w11, c)) return false;
+    g.e.bias = bw.b11;
+    g.e.out16 = A.y;
+    g.e.out16_ld = c;
+    g.e.ln_g = bw.ln1g;
+    g.e.ln_b = bw.ln1b;
+    g.e.ln_out = A.a;
+    g.e.ln_ld = t;
+    g.e.ln_lo = cc;
+    g.e.ln_n = t;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 2. h = relu(conv3x3(y_c))
+  {
+    GemmOp g{};
+    if (!mk.conv3(g, A.y, n, H, W, cc, c, bw.wc0, cc)) return false;
+    g.e.act = ACT_RELU;
+    g.e.out16 = A.hc;
+    g.e.out16_ld = cc;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 3. z[:, :cc] = conv3x3(h) + y_c
+  {
+    GemmOp g{};
+    if (!mk.conv3(g, A.hc, n, H, W, cc, cc, bw.wc2, cc)) return false;
+    g.e.res16 = A.y;
+    g.e.res16_ld = c;
+    g.e.out16 = A.z;
+    g.e.out16_ld = c;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 4. qkv = LN1(y_t) W^T + b
+  {
+    GemmOp g{};
+    if (!mk.flat(g, A.a, P, t, t, bw.wqkv, 3 * t)) return false;
+    g.e.bias = bw.bqkv;
+    g.e.out16 = A.qh;
+    g.e.out16_ld = 3 * t;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 5. window attention
+  {
+    Op at{};
+    at.kind = Op::ATTN;
+    at.attn = AttnGeom{n, H, W, t, heads, shifted ? 4 : 0, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
+    at.attn_in = A.qh;
+    at.attn_out = A.o;
+    at.attn_rp = bw.rp;
+    ops.push_back(at);
+  }
+  // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
+  {
+    GemmOp g{};
+    if (!mk.flat(g, A.o, P, t, t, bw.wproj, t)) return false;
+    g.e.bias = bw.bproj;
+    g.e.res16 = A.y + cc;
+    g.e.res16_ld = c;
+    g.e.out16 = A.z + cc;
+    g.e.out16_ld = c;
+    g.e.ln_g = bw.ln2g;
+    g.e.ln_b = bw.ln2b;
+    g.e.ln_out = A.a;
+    g.e.ln_ld = t;
+    g.e.ln_lo = 0;
+    g.e.ln_n = t;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 7. hid = gelu(LN2 W0^T + b0)
+  {
+    GemmOp g{};
+    if (!mk.flat(g, A.a, P, t, t, bw.w0, 4 * t)) return false;
+    g.e.bias = bw.b0;
+    g.e.act = ACT_GELU;
+    g.e.out16 = A.qh;
+    g.e.out16_ld = 4 * t;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 8. z[:, cc:] = hid W2^T + b2 + x1t
+  {
+    GemmOp g{};
+    if (!mk.flat(g, A.qh, P, 4 * t, 4 * t, bw.w2, t)) return false;
+    g.e.bias = bw.b2;
+    g.e.res16 = A.z + cc;
+    g.e.res16_ld = c;
+    g.e.out16 = A.z + cc;
+    g.e.out16_ld = c;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  // 9. x = x + conv1_2(z) + b  (fp32) and its shadow (or the shadow of x + skip)
+  {
+    GemmOp g{};
+    if (!mk.flat(g, A.z, P, c, c, bw.w12, c)) return false;
+    g.e.bias = bw.b12;
+    g.e.res32 = xin;
+    g.e.res32_ld = c;
+    g.e.out32 = xout;
+    g.e.out32_ld = c;
+    g.e.out16 = xs;
+    g.e.out16_ld = c;
+    g.e.skip32 = skip;
+    g.e.skip_ld = c;
+    op.gemm = g;
+    ops.push_back(op);
+  }
+  (void)ctx;
+  return true;
+}
+
+int build_plan(scb_ctx* ctx) {
+  Arena& A = ctx->arena;
+  std::string err;
+  std::vector<Op>& ops = A.ops;
+  ops.clear();
+  const int n = A.n;
+  auto H = [&](int lvl) { return A.hp >> lvl; };
+  auto W = [&](int lvl) { return A.wp >> lvl; };
+  Op head{};
+  head.kind = Op::HEAD;
+  ops.push_back(head);
+  for (int s = 0; s < 7; ++s) {
+    const int lvl = kStageLevel[s];
+    const int c = 64 << lvl;
+    const bool up = s >= 4;
+    if (up) {
+      // m_up{k}.0 : transposed conv from level lvl+1 (shadow already holds x + skip)
+      Op op{};
+      op.kind = Op::GEMM;
+      Maker mk{&err};
+      GemmOp g{};
+      if (!mk.up2(g, A.xs[lvl + 1], n, H(lvl + 1), W(lvl + 1), 2 * c, ctx->wup[s - 4], c)) return fail(ctx, SCB_EINVAL, err);
+      g.e.out32 = A.xw;
+      g.e.out32_ld = c;
+      g.e.out16 = A.xs[lvl];
+      g.e.out16_ld = c;
+      op.gemm = g;
+      ops.push_back(op);
+    }
+    const int nb = ctx->config[s];
+    for (int i = 0; i < nb; ++i) {
+      const float* xin = (!up && i == 0) ? A.skip[lvl] : A.xw;
+      const bool last = i == nb - 1;
+      const float* skip = nullptr;
+      float* xout = A.xw;
+      if (last && s >= 3) {  // body, up3, up2, up1: shadow of (x + skip) only
+        skip = A.skip[lvl];
+        xout = nullptr;
+      }
+      if (!block_ops(ctx, ops, ctx->blocks[s][i], A, n, H(lvl), W(lvl), xin, xout, A.xs[lvl], skip, (i % 2) == 1, err))
+        return fail(ctx, SCB_EINVAL, err);
+    }
+    if (s < 3) {
+      // m_down{k}.4 : 2x2 stride-2 conv -> the next level's skip (fp32) + shadow
+      Op op{};
+      op.kind = Op::GEMM;
+      Maker mk{&err};
+      GemmOp g{};
+      if (!mk.down2(g, A.xs[lvl], n, H(lvl), W(lvl), c, ctx->wdown[s], 2 * c)) return fail(ctx, SCB_EINVAL, err);
+      g.e.out32 = A.skip[lvl + 1];
+      g.e.out32_ld = 2 * c;
+      g.e.out16 = A.xs[lvl + 1];
+      g.e.out16_ld = 2 * c;
+      op.gemm = g;
+      ops.push_back(op);
+    }
+  }
+  Op tail{};
+  tail.kind = Op::TAIL;
+  ops.push_back(tail);
+  return SCB_OK;
+}
+
+int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
+  Arena& A = ctx->arena;
+  if (A.base && A.n == n && A.hp == hp && A.wp == wp) return SCB_OK;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr);
+  if (A.base && A.bytes < need) {
+    cudaFree(A.base);
+    A.base = nullptr;
+    A.bytes = 0;
+  }
+  if (!A.base) {
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    if (need > free_b) {
+      char buf[256];
+      snprintf(buf, sizeof buf, "%d x %dx%d needs %.2f GiB of device scratch, %.2f GiB free", n, hp, wp,
+               need / 1073741824.0, free_b / 1073741824.0);
+      return fail(ctx, SCB_ENOMEM, buf);
+    }
+    cudaError_t e = cudaMalloc(&A.base, need);
+    if (e != cudaSuccess) {
+      A.base = nullptr;
+      return fail(ctx, SCB_ENOMEM, std::string("arena allocation refused: ") + cudaGetErrorString(e));
+    }
+    A.bytes = need;
+  }
+  A.n = n;
+  A.hp = hp;
+  A.wp = wp;
+  arena_layout(n, ctx->in_nc, hp, wp, &A);
+  return build_plan(ctx);
+}
+
+int check_device_error(scb_ctx* ctx) {
+  unsigned v = 0;
+  CKC(ctx, cudaMemcpyFromSymbol(&v, scb::g_device_error, sizeof v), "read device error word");
+  if (v) {
+    unsigned z = 0;
+    cudaMemcpyToSymbol(scb::g_device_error, &z, sizeof z);
+    return fail(ctx, SCB_EDEVICE, "a kernel gave up on a bounded wait (device error code " + std::to_string(v) + ")");
+  }
+  return SCB_OK;
+}
+
+bool geom_ok(scb_ctx* ctx, int n, int c, int h, int w) {
+  if (n <= 0 || h <= 0 || w <= 0) {
+    fail(ctx, SCB_EINVAL, "empty image");
+    return false;
+  }
+  if (c != ctx->in_nc) {
+    fail(ctx, SCB_EINVAL, "the image has " + std::to_string(c) + " channels, the weights take " + std::to_string(ctx->in_nc));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int head_dim, int window,
+               const int config[7], int device, scb_ctx** out) {
+  if (!out) return fail(nullptr, SCB_EINVAL, "out is NULL");
+  *out = nullptr;
+  if (in_nc != 1 && in_nc != 3) return fail(nullptr, SCB_EINVAL, "in_nc must be 1 or 3");
+  if (dim != 64 || head_dim != 32 || window != 8)
+    return fail(nullptr, SCB_EINVAL, "only dim 64, head_dim 32, window 8 exist (src/weights.rs:204-280)");
+  if (!tensors || n_tensors <= 0) return fail(nullptr, SCB_ENOWEIGHT, "no tensors");
+  int cfg[7];
+  for (int i = 0; i < 7; ++i) {
+    cfg[i] = config ? config[i] : 4;
+    if (cfg[i] < 1 || cfg[i] > 16) return fail(nullptr, SCB_EINVAL, "config entries must be 1..16");
+  }
+  Table tab;
+  for (int i = 0; i < n_tensors; ++i) {
+    if (!tensors[i].name) return fail(nullptr, SCB_EINVAL, "tensor with NULL name");
+    tab.by_name[tensors[i].name] = &tensors[i];
+  }
+  Blob blob;
+  struct Pending {
+    size_t w11, w12, wc0, wc2, wqkv, wproj, w0, w2, b11, b12, bqkv, bproj, b0, b2, l1g, l1b, l2g, l2b, rp;
+    int c;
+  };
+  std::vector<Pending> pend[7];
+  size_t o_down[3], o_up[3], o_head, o_tail;
+
+  auto need = [&](const std::string& nm, std::initializer_list<int64_t> sh) -> const float* {
+    const float* p = tab.get(nm, sh);
+    return p;
+  };
+  // m_head / m_tail stay fp32 (SIMT kernels)
+  const float* p = need("m_head.0.weight", {dim, in_nc, 3, 3});
+  if (!p) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+  o_head = blob.f32(p, (size_t)dim * in_nc * 9);
+  p = need("m_tail.0.weight", {in_nc, dim, 3, 3});
+  if (!p) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+  o_tail = blob.f32(p, (size_t)in_nc * dim * 9);
+
+  for (int s = 0; s < 7; ++s) {
+    const int c = dim << kStageLevel[s], t = c / 2, heads = t / 32;
+    const int first = s >= 4 ? 1 : 0;
+    for (int i = 0; i < cfg[s]; ++i) {
+      const std::string pre = std::string("m_") + kStageName[s] + "." + std::to_string(first + i);
+      const std::string tb = pre + ".trans_block";
+      Pending pd{};
+      pd.c = c;
+      auto half_of = [&](const std::string& nm, std::initializer_list<int64_t> sh, size_t& off) {
+        const float* q = need(nm, sh);
+        if (!q) return false;
+        size_t cnt = 1;
+        for (auto d : sh) cnt *= (size_t)d;
+        off = blob.half(std::vector<float>(q, q + cnt));
+        return true;
+      };
+      auto f32_of = [&](const std::string& nm, std::initializer_list<int64_t> sh, size_t& off) {
+        const float* q = need(nm, sh);
+        if (!q) return false;
+        size_t cnt = 1;
+        for (auto d : sh) cnt *= (size_t)d;
+        off = blob.f32(q, cnt);
+        return true;
+      };
+      // 3x3 conv weights: [co][ci][ky][kx] -> [co][ky][kx][ci]
+      auto conv3_of = [&](const std::string& nm, size_t& off) {
+        const float* q = need(nm, {t, t, 3, 3});
+        if (!q) return false;
+        std::vector<float> r((size_t)t * t * 9);
+        for (int co = 0; co < t; ++co)
+          for (int ci = 0; ci < t; ++ci)
+            for (int k = 0; k < 9; ++k) r[((size_t)co * 9 + k) * t + ci] = q[((size_t)co * t + ci) * 9 + k];
+        off = blob.half(r);
+        return true;
+      };
+      bool ok = half_of(pre + ".conv1_1.weight", {c, c, 1, 1}, pd.w11) && f32_of(pre + ".conv1_1.bias", {c}, pd.b11) &&
+                half_of(pre + ".conv1_2.weight", {c, c, 1, 1}, pd.w12) && f32_of(pre + ".conv1_2.bias", {c}, pd.b12) &&
+                conv3_of(pre + ".conv_block.0.weight", pd.wc0) && conv3_of(pre + ".conv_block.2.weight", pd.wc2) &&
+                f32_of(tb + ".ln1.weight", {t}, pd.l1g) && f32_of(tb + ".ln1.bias", {t}, pd.l1b) &&
+                f32_of(tb + ".ln2.weight", {t}, pd.l2g) && f32_of(tb + ".ln2.bias", {t}, pd.l2b) &&
+                half_of(tb + ".msa.embedding_layer.weight", {3 * t, t}, pd.wqkv) &&
+                f32_of(tb + ".msa.embedding_layer.bias", {3 * t}, pd.bqkv) &&
+                half_of(tb + ".msa.linear.weight", {t, t}, pd.wproj) && f32_of(tb + ".msa.linear.bias", {t}, pd.bproj) &&
+                f32_of(tb + ".msa.relative_position_params", {heads, 15, 15}, pd.rp) &&
+                half_of(tb + ".mlp.0.weight", {4 * t, t}, pd.w0) && f32_of(tb + ".mlp.0.bias", {4 * t}, pd.b0) &&
+                half_of(tb + ".mlp.2.weight", {t, 4 * t}, pd.w2) && f32_of(tb + ".mlp.2.bias", {t}, pd.b2);
+      if (!ok) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+      pend[s].push_back(pd);
+    }
+    if (s < 3) {  // m_down{k}.{cfg}: [2c][c][2][2] -> [co][dy][dx][ci]
+      const std::string nm = std::string("m_") + kStageName[s] + "." + std::to_string(cfg[s]) + ".weight";
+      const float* q = need(nm, {2 * c, c, 2, 2});
+      if (!q) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+      std::vector<float> r((size_t)2 * c * c * 4);
+      for (int co = 0; co < 2 * c; ++co)
+        for (int ci = 0; ci < c; ++ci)
+          for (int k = 0; k < 4; ++k) r[((size_t)co * 4 + k) * c + ci] = q[((size_t)co * c + ci) * 4 + k];
+      o_down[s] = blob.half(r);
+    }
+    if (s >= 4) {  // m_up{k}.0: [ci=2c][co=c][2][2] -> [(dy,dx,co)][ci]
+      const std::string nm = std::string("m_") + kStageName[s] + ".0.weight";
+      const float* q = need(nm, {2 * c, c, 2, 2});
+      if (!q) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+      std::vector<float> r((size_t)2 * c * c * 4);
+      for (int ci = 0; ci < 2 * c; ++ci)
+        for (int co = 0; co < c; ++co)
+          for (int k = 0; k < 4; ++k) r[((size_t)k * c + co) * (2 * c) + ci] = q[((size_t)ci * c + co) * 4 + k];
+      o_up[s - 4] = blob.half(r);
+    }
+  }
+
+  scb_ctx* ctx = new scb_ctx();
+  ctx->device = device;
+  ctx->in_nc = in_nc;
+  ctx->dim = dim;
+  memcpy(ctx->config, cfg, sizeof cfg);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return fail(nullptr, SCB_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+  }
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10) {
+    delete ctx;
+    return fail(nullptr, SCB_ECUDA, "this library is built for sm_100a (B200); device has compute capability " +
+                                        std::to_string(major) + "." + std::to_string(minor));
+  }
+  cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device);
+  e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->wblob, blob.host.size());
+  if (e == cudaSuccess) e = cudaMemcpy(ctx->wblob, blob.host.data(), blob.host.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    std::string m = std::string("weight upload: ") + cudaGetErrorString(e);
+    scb_destroy(ctx);
+    return fail(nullptr, SCB_ECUDA, m);
+  }
+  ctx->wbytes = blob.host.size();
+  char* b = ctx->wblob;
+  auto H16 = [&](size_t o) { return reinterpret_cast<__half*>(b + o); };
+  auto F = [&](size_t o) { return reinterpret_cast<float*>(b + o); };
+  ctx->whead = F(o_head);
+  ctx->wtail = F(o_tail);
+  for (int s = 0; s < 3; ++s) ctx->wdown[s] = H16(o_down[s]);
+  for (int s = 0; s < 3; ++s) ctx->wup[s] = H16(o_up[s]);
+  for (int s = 0; s < 7; ++s)
+    for (auto& pd : pend[s]) {
+      BlockW bw;
+      bw.c = pd.c;
+      bw.w11 = H16(pd.w11); bw.w12 = H16(pd.w12); bw.wc0 = H16(pd.wc0); bw.wc2 = H16(pd.wc2);
+      bw.wqkv = H16(pd.wqkv); bw.wproj = H16(pd.wproj); bw.w0 = H16(pd.w0); bw.w2 = H16(pd.w2);
+      bw.b11 = F(pd.b11); bw.b12 = F(pd.b12); bw.bqkv = F(pd.bqkv); bw.bproj = F(pd.bproj);
+      bw.b0 = F(pd.b0); bw.b2 = F(pd.b2); bw.ln1g = F(pd.l1g); bw.ln1b = F(pd.l1b);
+      bw.ln2g = F(pd.l2g); bw.ln2b = F(pd.l2b); bw.rp = F(pd.rp);
+      ctx->blocks[s].push_back(bw);
+    }
+  g_create_error.clear();
+  *out = ctx;
+  return SCB_OK;
+}
+
+int scb_forward_dev(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype,
+                    void* stream) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
+  if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  int r = ensure_arena(ctx, n, hp, wp);
+  if (r) return r;
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  r = run_ops(ctx, x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w, st);
+  if (r) return r;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
+  if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  int r = ensure_arena(ctx, n, hp, wp);
+  if (r) return r;
+  Arena& A = ctx->arena;
+  const size_t in_b = (size_t)n * c * h * w * (x_dtype == SCB_U8 ? 1 : 4);
+  const size_t out_b = (size_t)n * c * h * w * (y_dtype == SCB_U8 ? 1 : 4);
+  CKC(ctx, cudaMemcpyAsync(A.io_in, x, in_b, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+  r = run_ops(ctx, A.io_in, x_dtype == SCB_U8, A.io_out, y_dtype == SCB_U8, c, h, w, ctx->stream);
+  if (r) return r;
+  CKC(ctx, cudaMemcpyAsync(y, A.io_out, out_b, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+  CKC(ctx, cudaStreamSynchronize(ctx->stream), "forward");
+  r = check_device_error(ctx);
+  if (r) return r;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_forward(scb_ctx* ctx, const float* x_nchw, int c, int hp, int wp, float* y_nchw) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (hp % 64 || wp % 64) return fail(ctx, SCB_EINVAL, "scb_forward takes a plane already padded to a multiple of 64");
+  return scb_forward_host(ctx, x_nchw, SCB_F32, 1, c, hp, wp, y_nchw, SCB_F32);
+}
+
+int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes) {
+  if (!bytes || n <= 0 || hp <= 0 || wp <= 0 || hp % 64 || wp % 64 || (in_nc != 1 && in_nc != 3)) return SCB_EINVAL;
+  *bytes = arena_layout(n, in_nc, hp, wp, nullptr);
+  return SCB_OK;
+}
+
+void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_bytes) {
+  if (weights_bytes) *weights_bytes = ctx ? ctx->wbytes : 0;
+  if (scratch_bytes) *scratch_bytes = ctx ? ctx->arena.bytes : 0;
+}
+
+void scb_release_scratch(scb_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->arena.base) cudaFree(ctx->arena.base);
+  ctx->arena = Arena{};
+}
+
+const char* scb_last_error(const scb_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_error.c_str(); }
+
+int scb_last_launch_count(const scb_ctx* ctx) { return ctx ? ctx->last_launches : 0; }
+
+void scb_destroy(scb_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  scb_release_scratch(ctx);
+  if (ctx->wblob) cudaFree(ctx->wblob);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+// ---------------------------------------------------------------------------- probes
+static int probe_finish(scb_ctx* ctx, cudaError_t e) {
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "probe launch");
+  CKC(ctx, cudaStreamSynchronize(ctx->stream), "probe");
+  int r = check_device_error(ctx);
+  if (r) return r;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16, int N, const float* bias, int act,
+                   const void* res16, void* out16, float* out32) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  std::string err;
+  Maker mk{&err};
+  GemmOp g{};
+  if (!mk.flat(g, static_cast<const __half*>(a16), M, K, K, static_cast<const __half*>(b16), N))
+    return fail(ctx, SCB_EINVAL, err);
+  g.e.bias = bias;
+  g.e.act = act;
+  g.e.res16 = static_cast<const __half*>(res16);
+  g.e.res16_ld = N;
+  g.e.out16 = static_cast<__half*>(out16);
+  g.e.out16_ld = N;
+  g.e.out32 = out32;
+  g.e.out32_ld = N;
+  return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
+}
+
+int scb_probe_conv3x3(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin, const void* w16, int cout, int act,
+                      const void* res16, void* out16) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  std::string err;
+  Maker mk{&err};
+  GemmOp g{};
+  if (!mk.conv3(g, static_cast<const __half*>(x16), n, H, W, cin, cin, static_cast<const __half*>(w16), cout))
+    return fail(ctx, SCB_EINVAL, err);
+  g.e.act = act;
+  g.e.res16 = static_cast<const __half*>(res16);
+  g.e.res16_ld = cout;
+  g.e.out16 = static_cast<__half*>(out16);
+  g.e.out16_ld = cout;
+  return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
+}
+
+int scb_probe_down2(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin, const void* w16, int cout,
+                    float* out32, void* out16) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  std::string err;
+  Maker mk{&err};
+  GemmOp g{};
+  if (!mk.down2(g, static_cast<const __half*>(x16), n, H, W, cin, static_cast<const __half*>(w16), cout))
+    return fail(ctx, SCB_EINVAL, err);
+  g.e.out32 = out32;
+  g.e.out32_ld = cout;
+  g.e.out16 = static_cast<__half*>(out16);
+  g.e.out16_ld = cout;
+  return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
+}
+
+int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, const void* w16, int cout,
+                  float* out32, void* out16) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  std::string err;
+  Maker mk{&err};
+  GemmOp g{};
+  if (!mk.up2(g, static_cast<const __half*>(x16), n, h, w, cin, static_cast<const __half*>(w16), cout))
+    return fail(ctx, SCB_EINVAL, err);
+  g.e.out32 = out32;
+  g.e.out32_ld = cout;
+  g.e.out16 = static_cast<__half*>(out16);
+  g.e.out16_ld = cout;
+  return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
+}
+
+int scb_probe_attention(scb_ctx* ctx, const void* qkv16, int n, int H, int W, int t, int shift, const float* rp,
+                        void* out16) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (t % 32 || t / 32 > 8 || H % 8 || W % 8 || (shift != 0 && shift != 4)) return fail(ctx, SCB_EINVAL, "attention geometry");
+  Op op{};
+  op.kind = Op::ATTN;
+  op.attn = AttnGeom{n, H, W, t, t / 32, shift, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
+  op.attn_in = static_cast<const __half*>(qkv16);
+  op.attn_out = static_cast<__half*>(out16);
+  op.attn_rp = rp;
+  return probe_finish(ctx, launch_attn(op, ctx->stream));
+}
+
+int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n, int H, int W, float* y32) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (stage < 0 || stage > 6 || index < 0 || index >= ctx->config[stage]) return fail(ctx, SCB_EINVAL, "block index");
+  if (H % 8 || W % 8 || n <= 0) return fail(ctx, SCB_EINVAL, "block plane must be a multiple of 8");
+  const BlockW& bw = ctx->blocks[stage][index];
+  const int c = bw.c;
+  // A private arena sized as a full-resolution plane of n*H*W pixels is more than enough.
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  Arena tmp;
+  const long P = (long)n * H * W;
+  const size_t bytes = (size_t)P * (c * 2 /*xs*/ + c * 2 /*y*/ + c /*hc*/ + c * 2 /*z*/ + c /*a*/ + c /*o*/ + c * 4 /*qh*/) + 16 * 1024;
+  char* base = nullptr;
+  CKC(ctx, cudaMalloc(&base, bytes), "probe scratch");
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    char* p = base + off;
+    off += (b + 1023) & ~size_t(1023);
+    return p;
+  };
+  __half* xs = reinterpret_cast<__half*>(take((size_t)P * c * 2));
+  tmp.y = reinterpret_cast<__half*>(take((size_t)P * c * 2));
+  tmp.hc = reinterpret_cast<__half*>(take((size_t)P * c));
+  tmp.z = reinterpret_cast<__half*>(take((size_t)P * c * 2));
+  tmp.a = reinterpret_cast<__half*>(take((size_t)P * c));
+  tmp.o = reinterpret_cast<__half*>(take((size_t)P * c));
+  tmp.qh = reinterpret_cast<__half*>(take((size_t)P * c * 4));
+  // shadow of x: a one-off conversion on the device
+  std::vector<float> hx((size_t)P * c);
+  cudaError_t e = cudaMemcpy(hx.data(), x32, hx.size() * 4, cudaMemcpyDeviceToHost);
+  std::vector<__half> hs(hx.size());
+  for (size_t i = 0; i < hx.size(); ++i) hs[i] = __float2half_rn(hx[i]);
+  if (e == cudaSuccess) e = cudaMemcpy(xs, hs.data(), hs.size() * 2, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    return cuda_fail(ctx, e, "probe staging");
+  }
+  std::vector<Op> ops;
+  std::string err;
+  if (!block_ops(ctx, ops, bw, tmp, n, H, W, x32, y32, xs, nullptr, (index % 2) == 1, err)) {
+    cudaFree(base);
+    return fail(ctx, SCB_EINVAL, err);
+  }
+  int r = SCB_OK;
+  for (const Op& op : ops) {
+    if (op.kind == Op::GEMM) {
+      e = launch_gemm(op.gemm, ctx->sms, ctx->stream);
+    } else {
+      e = launch_attn(op, ctx->stream);
+    }
+    if (e != cudaSuccess) break;
+  }
+  r = probe_finish(ctx, e);
+  cudaFree(base);
+  return r;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+"""End to end on the device: the golden fixtures (upstream torch FP32 on seeded
+weights), batched vs single, and bit-identical repeats (the reference's race
+detector, tests/cuda_ops.rs:217-251)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3       # north-star bar on the [0,1] output before quantisation
+LEVEL_FRAC = 0.999   # >= 99.9 % of values within 1 8-bit level
+
+
+def _gpu():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+
+
+def check_parity(oracle, what, want, got):
+    rep = oracle.parity_report(want, got)
+    print(f"{what}: {rep}")
+    assert rep["max_abs"] <= MAX_ABS, f"{what}: {rep}"
+    assert 1.0 - rep["frac_level_gt1"] >= LEVEL_FRAC, f"{what}: {rep}"
+    return rep
+
+
+@pytest.mark.parametrize("stem", ["color_64x64", "color_80x64", "color_72x40", "gray_64x64", "color_128x128"])
+def test_forward_matches_golden(stem, goldens, oracle, scb, be1, be3):
+    _gpu()
+    g = goldens[stem]
+    be = be3 if g["c"] == 3 else be1
+    wt = be.weights
+    got = scb.run(be, g["x"][0], g["c"], g["h"], g["w"], wt)
+    check_parity(oracle, stem, g["y"][0], got)
+
+
+def test_forward_host_batched_uint8(scb, oracle, be3, weights3):
+    """uint8 in, the pad/crop fused on the device, two different images in one
+    call; each must match the oracle."""
+    _gpu()
+    x = np.concatenate([scb.synth.noisy_image(s, 3, 72, 136, 25 / 255)[None] for s in (1, 2)])
+    y = be3.forward_host(x)
+    want = oracle.forward(x.astype(np.float32) / 255.0, weights3.tensors)
+    for i in range(2):
+        check_parity(oracle, f"batched {i}", want[i], y[i])
+
+
+def test_repeats_are_bit_identical(scb, be3):
+    _gpu()
+    x = scb.synth.noisy_image(5, 3, 256, 192, 25 / 255)[None]
+    first = be3.forward_host(x)
+    for r in range(5):
+        again = be3.forward_host(x)
+        assert np.array_equal(first, again), f"run {r + 1} differs: max {np.abs(first - again).max():.3e}"
+
+
+def test_footprint_and_release(scb, be3):
+    _gpu()
+    be3.forward_host(scb.synth.noisy_image(3, 3, 64, 64, 0.1)[None])
+    wb, sb = be3.footprint()
+    assert wb > 30e6 and sb > 0
+    be3.release_scratch()
+    assert be3.footprint()[1] == 0

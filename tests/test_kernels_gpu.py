@@ -1,0 +1,180 @@
+"""Each device op against a float32 reference computed on the same fp16 operands,
+called through the C ABI probes (the reference's `op_probe` / `linear_probe` /
+`attention_kernel_probe` / `block_dump` pattern, tests/cuda_ops.rs:254-585)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch
+
+
+def close(what, want, got, tol):
+    """Worst |diff| scaled by the data's magnitude (tests/cuda_ops.rs:49-73)."""
+    want = np.asarray(want, np.float64)
+    got = np.asarray(got, np.float64)
+    scale = max(np.abs(want).max(), 1e-6)
+    d = np.abs(want - got)
+    i = int(d.argmax())
+    assert d.max() <= tol * scale, f"{what}: worst |diff| {d.max():.3e} at {i} (scale {scale:.3e}, tol {tol:.1e})"
+    return d.max() / scale
+
+
+def h16(rng, shape, scale=1.0):
+    return (rng.standard_normal(shape) * scale).astype(np.float16)
+
+
+@pytest.mark.parametrize("M,K,N,act,res", [
+    (300, 64, 64, 1, True), (256, 32, 32, 0, False), (200, 32, 96, 0, False), (128, 32, 128, 2, False),
+    (384, 64, 128, 0, True), (130, 64, 192, 0, False), (1000, 64, 256, 0, True), (257, 128, 512, 0, False),
+    (129, 256, 768, 0, False), (5000, 128, 32, 0, True), (64, 64, 64, 0, False), (20000, 64, 64, 0, True),
+])
+def test_gemm(be3, M, K, N, act, res):
+    torch = _torch()
+    rng = np.random.default_rng(M + K + N)
+    a, b = h16(rng, (M, K)), h16(rng, (N, K), K ** -0.5)
+    bias = rng.standard_normal(N).astype(np.float32)
+    r16 = h16(rng, (M, N)) if res else None
+    ref = a.astype(np.float32) @ b.astype(np.float32).T + bias
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = np.asarray(torch.nn.functional.gelu(torch.from_numpy(ref)))
+    if res:
+        ref = ref + r16.astype(np.float32)
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    tbias = torch.from_numpy(bias).cuda()
+    tr = torch.from_numpy(r16).cuda() if res else None
+    o16 = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    o32 = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    rc = be3.lib.scb_probe_gemm(be3.ctx, ta.data_ptr(), M, K, tb.data_ptr(), N, tbias.data_ptr(), act,
+                                tr.data_ptr() if res else None, o16.data_ptr(), o32.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    close(f"gemm {M}x{K}x{N} f32", ref, o32.cpu().numpy(), 1e-5)
+    close(f"gemm {M}x{K}x{N} f16", ref, o16.float().cpu().numpy(), 2e-3)
+
+
+def conv3_ref(torch, x16, w, act, r16):
+    """x16 [n][H][W][ci] fp16, w [co][ci][3][3] float (fp16 values)."""
+    x = torch.from_numpy(x16.astype(np.float32)).permute(0, 3, 1, 2)
+    y = torch.nn.functional.conv2d(x.double(), torch.from_numpy(w).double(), padding=1)
+    if act == 1:
+        y = torch.relu(y)
+    y = y.permute(0, 2, 3, 1).numpy()
+    if r16 is not None:
+        y = y + r16.astype(np.float64)
+    return y
+
+
+@pytest.mark.parametrize("n,H,W,cin,act,res", [
+    (2, 16, 24, 32, 1, False), (1, 8, 8, 64, 0, True), (1, 16, 32, 128, 1, False), (1, 8, 16, 256, 0, True),
+    (2, 64, 64, 32, 0, True), (1, 8, 136, 64, 1, False),
+])
+def test_conv3x3(be3, n, H, W, cin, act, res):
+    torch = _torch()
+    rng = np.random.default_rng(n * H * W + cin)
+    x = h16(rng, (n, H, W, cin))
+    w = h16(rng, (cin, cin, 3, 3), (9 * cin) ** -0.5).astype(np.float32)
+    wk = np.ascontiguousarray(w.transpose(0, 2, 3, 1)).astype(np.float16)  # [co][ky][kx][ci]
+    r16 = h16(rng, (n, H, W, cin)) if res else None
+    ref = conv3_ref(torch, x, w, act, r16)
+    tx, tw = torch.from_numpy(x).cuda(), torch.from_numpy(wk).cuda()
+    tr = torch.from_numpy(r16).cuda() if res else None
+    out = torch.empty((n, H, W, cin), dtype=torch.float16, device="cuda")
+    rc = be3.lib.scb_probe_conv3x3(be3.ctx, tx.data_ptr(), n, H, W, cin, tw.data_ptr(), cin, act,
+                                   tr.data_ptr() if res else None, out.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    close(f"conv3x3 {n}x{H}x{W}x{cin}", ref, out.float().cpu().numpy(), 2e-3)
+
+
+@pytest.mark.parametrize("n,H,W,cin", [(2, 16, 32, 64), (1, 16, 16, 128), (1, 16, 16, 256), (3, 8, 24, 64)])
+def test_down2(be3, n, H, W, cin):
+    torch = _torch()
+    rng = np.random.default_rng(H * W + cin)
+    cout = 2 * cin
+    x = h16(rng, (n, H, W, cin))
+    w = h16(rng, (cout, cin, 2, 2), (4 * cin) ** -0.5).astype(np.float32)
+    wk = np.ascontiguousarray(w.transpose(0, 2, 3, 1)).astype(np.float16)
+    xt = torch.from_numpy(x.astype(np.float64)).permute(0, 3, 1, 2)
+    ref = torch.nn.functional.conv2d(xt, torch.from_numpy(w).double(), stride=2).permute(0, 2, 3, 1).numpy()
+    tx, tw = torch.from_numpy(x).cuda(), torch.from_numpy(wk).cuda()
+    o32 = torch.empty((n, H // 2, W // 2, cout), dtype=torch.float32, device="cuda")
+    o16 = torch.empty((n, H // 2, W // 2, cout), dtype=torch.float16, device="cuda")
+    rc = be3.lib.scb_probe_down2(be3.ctx, tx.data_ptr(), n, H, W, cin, tw.data_ptr(), cout, o32.data_ptr(),
+                                 o16.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    close("down2 f32", ref, o32.cpu().numpy(), 1e-5)
+    close("down2 f16", ref, o16.float().cpu().numpy(), 2e-3)
+
+
+@pytest.mark.parametrize("n,h,w,cin", [(2, 8, 8, 128), (1, 8, 16, 256), (1, 4, 8, 512), (2, 16, 24, 128)])
+def test_up2(be3, n, h, w, cin):
+    torch = _torch()
+    rng = np.random.default_rng(h * w + cin)
+    cout = cin // 2
+    x = h16(rng, (n, h, w, cin))
+    wt = h16(rng, (cin, cout, 2, 2), (4 * cout) ** -0.5).astype(np.float32)  # ConvTranspose layout
+    wk = np.ascontiguousarray(wt.transpose(2, 3, 1, 0).reshape(4 * cout, cin)).astype(np.float16)
+    xt = torch.from_numpy(x.astype(np.float64)).permute(0, 3, 1, 2)
+    ref = torch.nn.functional.conv_transpose2d(xt, torch.from_numpy(wt).double(), stride=2).permute(0, 2, 3, 1).numpy()
+    tx, tw = torch.from_numpy(x).cuda(), torch.from_numpy(wk).cuda()
+    o32 = torch.empty((n, 2 * h, 2 * w, cout), dtype=torch.float32, device="cuda")
+    o16 = torch.empty((n, 2 * h, 2 * w, cout), dtype=torch.float16, device="cuda")
+    rc = be3.lib.scb_probe_up2(be3.ctx, tx.data_ptr(), n, h, w, cin, tw.data_ptr(), cout, o32.data_ptr(),
+                               o16.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    close("up2 f32", ref, o32.cpu().numpy(), 1e-5)
+    close("up2 f16", ref, o16.float().cpu().numpy(), 2e-3)
+
+
+@pytest.mark.parametrize("n,H,W,t,shift", [
+    (1, 8, 8, 32, 0), (2, 16, 24, 32, 4), (1, 24, 16, 64, 4), (1, 16, 16, 128, 0), (1, 16, 16, 256, 4),
+    (1, 8, 8, 256, 4), (3, 8, 16, 32, 4), (1, 64, 64, 32, 4),
+])
+def test_attention(be3, oracle, n, H, W, t, shift):
+    torch = _torch()
+    rng = np.random.default_rng(H * W * t + shift)
+    heads = t // 32
+    qkv = h16(rng, (n, H, W, 3 * t))
+    rp = (rng.standard_normal((heads, 15, 15)) * 0.5).astype(np.float32)
+    want = np.empty((n, H, W, t), np.float32)
+    for i in range(n):
+        tok = oracle.window_tokens(qkv[i].astype(np.float32), shift)
+        o = oracle.attention_core(tok, rp, H // 8, W // 8, shift > 0)
+        want[i] = oracle.window_untokens(o, H, W, shift)
+    tq, trp = torch.from_numpy(qkv).cuda(), torch.from_numpy(rp).cuda()
+    out = torch.empty((n, H, W, t), dtype=torch.float16, device="cuda")
+    rc = be3.lib.scb_probe_attention(be3.ctx, tq.data_ptr(), n, H, W, t, shift, trp.data_ptr(), out.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    close(f"attention {n}x{H}x{W} t{t} s{shift}", want, out.float().cpu().numpy(), 4e-3)
+
+
+STAGES = ["down1", "down2", "down3", "body", "up3", "up2", "up1"]
+
+
+@pytest.mark.parametrize("stage,index,n,H,W", [
+    (0, 0, 1, 16, 16), (0, 1, 2, 16, 24), (1, 1, 1, 16, 16), (2, 0, 1, 8, 16), (3, 1, 1, 8, 8), (3, 0, 1, 16, 16),
+    (4, 1, 1, 16, 16), (6, 3, 1, 24, 16),
+])
+def test_block(be3, weights3, oracle, stage, index, n, H, W):
+    """One ConvTransBlock against the oracle at several geometries, W and SW
+    (tests/cuda_ops.rs:130-158)."""
+    torch = _torch()
+    c = 64 << [0, 1, 2, 3, 2, 1, 0][stage]
+    rng = np.random.default_rng(stage * 10 + index)
+    x = (rng.standard_normal((n, H, W, c)) * 0.5).astype(np.float32)
+    first = 1 if stage >= 4 else 0
+    prefix = f"m_{STAGES[stage]}.{first + index}"
+    w = weights3.tensors
+    want = np.stack([oracle.conv_trans_block(x[i], w, prefix, index % 2 == 1) for i in range(n)])
+    tx = torch.from_numpy(x).cuda()
+    ty = torch.empty_like(tx)
+    rc = be3.lib.scb_probe_block(be3.ctx, stage, index, tx.data_ptr(), n, H, W, ty.data_ptr())
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    r = close(f"block {prefix} {n}x{H}x{W}", want, ty.cpu().numpy(), 1e-2)
+    print(f"block {prefix}: rel err {r:.2e}")
