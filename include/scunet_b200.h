@@ -134,6 +134,17 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
 /* Number of kernel launches the last forward issued (for launch accounting). */
 int scb_last_launch_count(const scb_ctx* ctx);
 
+/* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,
+ * 263-273): while on, every launch of a forward is bracketed by CUDA events on the
+ * launch stream. */
+int scb_set_profiling(scb_ctx* ctx, int on);
+
+/* For the last profiled forward: per launch, its op class (0 head, 1 tail,
+ * 2 conv1x1, 3 conv3x3, 4 qkv, 5 attention, 6 proj, 7 mlp0, 8 mlp2, 9 down,
+ * 10 up), its algorithmic FLOPs and its device time in ms (waits for the
+ * events). Returns the number of entries written (<= max). */
+int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,7 +28,9 @@ SYMBOLS = [
     "scb_create", "scb_forward", "scb_forward_dev", "scb_forward_host", "scb_need_bytes", "scb_footprint",
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
+    "scb_set_profiling", "scb_profile_read",
 ]
+OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up"]
 
 
 class BackendError(RuntimeError):
@@ -75,6 +77,9 @@ def load_library(path=None):
     lib.scb_probe_up2.argtypes = [vp, vp, i, i, i, i, vp, i, vp, vp]
     lib.scb_probe_attention.argtypes = [vp, vp, i, i, i, i, i, vp, vp]
     lib.scb_probe_block.argtypes = [vp, i, i, vp, i, i, i, vp]
+    lib.scb_set_profiling.argtypes = [vp, i]
+    lib.scb_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double),
+                                     ctypes.POINTER(ctypes.c_float), i]
     if path is None:
         _lib = lib
     return lib
@@ -162,6 +167,17 @@ class B200:
         """Device pointers (e.g. torch tensors' data_ptr()); asynchronous."""
         self._check(self.lib.scb_forward_dev(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream or None),
                     "scb_forward_dev")
+
+    def set_profiling(self, on):
+        self._check(self.lib.scb_set_profiling(self.ctx, int(bool(on))), "scb_set_profiling")
+
+    def profile(self, max_ops=4096):
+        """[(class, flops, ms)] for every launch of the last profiled forward."""
+        tags = (ctypes.c_int * max_ops)()
+        flops = (ctypes.c_double * max_ops)()
+        ms = (ctypes.c_float * max_ops)()
+        n = self.lib.scb_profile_read(self.ctx, tags, flops, ms, max_ops)
+        return [(OP_CLASSES[tags[k]], flops[k], ms[k]) for k in range(n)]
 
     def last_launch_count(self):
         return self.lib.scb_last_launch_count(self.ctx)

@@ -292,8 +292,17 @@ struct BlockW {
 const char* kStageName[7] = {"down1", "down2", "down3", "body", "up3", "up2", "up1"};
 const int kStageLevel[7] = {0, 1, 2, 3, 2, 1, 0};
 
+// Op classes for profiling (scb_profile_read): the reference's per-op budget
+// classes (docs/TECH_NOTES.md:346-367).
+enum OpTag : int {
+  TAG_HEAD = 0, TAG_TAIL = 1, TAG_CONV1X1 = 2, TAG_CONV3X3 = 3, TAG_QKV = 4, TAG_ATTN = 5, TAG_PROJ = 6,
+  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10
+};
+
 struct Op {
   enum Kind { GEMM, ATTN, HEAD, TAIL } kind;
+  int tag = 0;
+  double flops = 0;  // algorithmic FLOPs of this launch (2 per multiply-add)
   GemmOp gemm;
   AttnGeom attn{};
   const __half* attn_in = nullptr;
@@ -363,6 +372,12 @@ struct scb_ctx {
   float* wtail = nullptr;
   Arena arena;
   int last_launches = 0;
+  // SCUNET_PROFILE equivalent (src/cuda.rs:106-135): events around every launch
+  bool profiling = false;
+  std::vector<cudaEvent_t> events;
+  std::vector<int> prof_tags;
+  std::vector<double> prof_flops;
+  std::vector<float> prof_ms;
 };
 
 namespace {
@@ -452,6 +467,14 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
 int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w, cudaStream_t st) {
   Arena& A = ctx->arena;
   int launches = 0;
+  if (ctx->profiling) {
+    while (ctx->events.size() < A.ops.size() + 1) {
+      cudaEvent_t ev;
+      CKC(ctx, cudaEventCreate(&ev), "cudaEventCreate");
+      ctx->events.push_back(ev);
+    }
+    CKC(ctx, cudaEventRecord(ctx->events[0], st), "cudaEventRecord");
+  }
   for (const Op& op : A.ops) {
     cudaError_t e = cudaSuccess;
     switch (op.kind) {
@@ -478,8 +501,18 @@ int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int
     }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
     ++launches;
+    if (ctx->profiling) CKC(ctx, cudaEventRecord(ctx->events[launches], st), "cudaEventRecord");
   }
   ctx->last_launches = launches;
+  if (ctx->profiling) {
+    ctx->prof_tags.clear();
+    ctx->prof_flops.clear();
+    for (const Op& op : A.ops) {
+      ctx->prof_tags.push_back(op.tag);
+      ctx->prof_flops.push_back(op.flops);
+    }
+    ctx->prof_ms.assign(A.ops.size(), -1.f);  // filled by scb_profile_read after a sync
+  }
   return SCB_OK;
 }
 
@@ -507,6 +540,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.ln_lo = cc;
     g.e.ln_n = t;
     op.gemm = g;
+    op.tag = TAG_CONV1X1;
+    op.flops = 2.0 * P * c * c;
     ops.push_back(op);
   }
   // 2. h = relu(conv3x3(y_c))
@@ -517,6 +552,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16 = A.hc;
     g.e.out16_ld = cc;
     op.gemm = g;
+    op.tag = TAG_CONV3X3;
+    op.flops = 2.0 * P * 9 * cc * cc;
     ops.push_back(op);
   }
   // 3. z[:, :cc] = conv3x3(h) + y_c
@@ -528,6 +565,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16 = A.z;
     g.e.out16_ld = c;
     op.gemm = g;
+    op.tag = TAG_CONV3X3;
+    op.flops = 2.0 * P * 9 * cc * cc;
     ops.push_back(op);
   }
   // 4. qkv = LN1(y_t) W^T + b
@@ -538,6 +577,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16 = A.qh;
     g.e.out16_ld = 3 * t;
     op.gemm = g;
+    op.tag = TAG_QKV;
+    op.flops = 2.0 * P * t * 3 * t;
     ops.push_back(op);
   }
   // 5. window attention
@@ -548,6 +589,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     at.attn_in = A.qh;
     at.attn_out = A.o;
     at.attn_rp = bw.rp;
+    at.tag = TAG_ATTN;
+    at.flops = 2.0 * 2.0 * P * 64 * t;
     ops.push_back(at);
   }
   // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
@@ -566,6 +609,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.ln_lo = 0;
     g.e.ln_n = t;
     op.gemm = g;
+    op.tag = TAG_PROJ;
+    op.flops = 2.0 * P * t * t;
     ops.push_back(op);
   }
   // 7. hid = gelu(LN2 W0^T + b0)
@@ -577,6 +622,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16 = A.qh;
     g.e.out16_ld = 4 * t;
     op.gemm = g;
+    op.tag = TAG_MLP0;
+    op.flops = 2.0 * P * t * 4 * t;
     ops.push_back(op);
   }
   // 8. z[:, cc:] = hid W2^T + b2 + x1t
@@ -589,6 +636,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16 = A.z + cc;
     g.e.out16_ld = c;
     op.gemm = g;
+    op.tag = TAG_MLP2;
+    op.flops = 2.0 * P * t * 4 * t;
     ops.push_back(op);
   }
   // 9. x = x + conv1_2(z) + b  (fp32) and its shadow (or the shadow of x + skip)
@@ -605,6 +654,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.skip32 = skip;
     g.e.skip_ld = c;
     op.gemm = g;
+    op.tag = TAG_CONV1X1;
+    op.flops = 2.0 * P * c * c;
     ops.push_back(op);
   }
   (void)ctx;
@@ -619,8 +670,11 @@ int build_plan(scb_ctx* ctx) {
   const int n = A.n;
   auto H = [&](int lvl) { return A.hp >> lvl; };
   auto W = [&](int lvl) { return A.wp >> lvl; };
+  const double P0 = (double)n * A.hp * A.wp;
   Op head{};
   head.kind = Op::HEAD;
+  head.tag = TAG_HEAD;
+  head.flops = 2.0 * P0 * 9 * ctx->in_nc * 64;
   ops.push_back(head);
   for (int s = 0; s < 7; ++s) {
     const int lvl = kStageLevel[s];
@@ -638,6 +692,8 @@ int build_plan(scb_ctx* ctx) {
       g.e.out16 = A.xs[lvl];
       g.e.out16_ld = c;
       op.gemm = g;
+      op.tag = TAG_UP;
+      op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (2 * c) * (4 * c);
       ops.push_back(op);
     }
     const int nb = ctx->config[s];
@@ -665,11 +721,15 @@ int build_plan(scb_ctx* ctx) {
       g.e.out16 = A.xs[lvl + 1];
       g.e.out16_ld = 2 * c;
       op.gemm = g;
+      op.tag = TAG_DOWN;
+      op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (4 * c) * (2 * c);
       ops.push_back(op);
     }
   }
   Op tail{};
   tail.kind = Op::TAIL;
+  tail.tag = TAG_TAIL;
+  tail.flops = 2.0 * P0 * 9 * 64 * ctx->in_nc;
   ops.push_back(tail);
   return SCB_OK;
 }
@@ -959,6 +1019,26 @@ void scb_release_scratch(scb_ctx* ctx) {
   ctx->arena = Arena{};
 }
 
+int scb_set_profiling(scb_ctx* ctx, int on) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  ctx->profiling = on != 0;
+  return SCB_OK;
+}
+
+int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!ctx->profiling || ctx->prof_tags.empty()) return 0;
+  const int n = (int)std::min<size_t>(ctx->prof_tags.size(), (size_t)std::max(max, 0));
+  for (int i = 0; i < n; ++i) {
+    float t = -1.f;
+    if (cudaEventSynchronize(ctx->events[i + 1]) == cudaSuccess) cudaEventElapsedTime(&t, ctx->events[i], ctx->events[i + 1]);
+    if (tags) tags[i] = ctx->prof_tags[i];
+    if (flops) flops[i] = ctx->prof_flops[i];
+    if (ms) ms[i] = t;
+  }
+  return n;
+}
+
 const char* scb_last_error(const scb_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_error.c_str(); }
 
 int scb_last_launch_count(const scb_ctx* ctx) { return ctx ? ctx->last_launches : 0; }
@@ -968,6 +1048,7 @@ void scb_destroy(scb_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   scb_release_scratch(ctx);
+  for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
   if (ctx->wblob) cudaFree(ctx->wblob);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
