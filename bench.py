@@ -1,0 +1,298 @@
+#!/usr/bin/env python3
+"""Throughput of the SCUNet forward pass on B200, in megapixels per second.
+
+Workload: seeded 1920x1080 RGB uint8 frames (smooth field
+plus luma-dependent and 2x2-correlated noise), replicate-padded to 1920x1088 on the
+device, colour SCUNet with seeded weights. A step is one pass over `--frames`
+frames per GPU (batch sharding, no collective: weak scaling); frames go through
+the library in micro-batches of `--micro` frames per `scb_forward_dev` call.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One JSON line on rank 0. `value` is device-timed (CUDA events on the launch
+stream, max over ranks) with inputs resident in HBM; `e2e` is the same metric
+through the host-pointer C-ABI call `scb_forward_host` (pinned host uint8 in,
+float32 out, copies inside the timed region). `roofline` is the dominant op class
+from a live per-launch event profile (`scb_set_profiling`). `cpu_baseline` times
+the CPU oracle (`oracle/scunet_np.py`, the reference's algorithm restated in
+numpy) on a bounded crop.
+
+`--impl reference` times the reference's CPU implementation of the path. The
+reference's own CPU code is Rust and cannot be built here (no cargo, unvendored
+crates), so the arm runs the oracle port on all host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, W, C = 1080, 1920, 3
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--frames", type=int, default=16, help="frames per GPU per step")
+    ap.add_argument("--micro", type=int, default=4, help="frames per library call")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+    Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = [r.split(", ") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        rows = [r for r in rows if len(r) >= 9 and (self.uuid is None or self.uuid in r[0])]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def cpu_oracle_mps(img_u8, size, reps=1):
+    """The CPU oracle on a size x size crop; returns (MP/s, seconds, threads)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import scunet_np
+    scb = importlib.import_module("scunet-rs_b200")
+    wt = scb.Weights.seeded(3, 0).tensors
+    x = img_u8[None, :, :size, :size].astype(np.float32) / 255.0
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        scunet_np.forward(x, wt)
+    dt = (time.perf_counter() - t0) / reps
+    return size * size / 1e6 / dt, dt, os.cpu_count()
+
+
+def reference_arm(a, rank, world):
+    """Rank 0 times the CPU implementation of the path; other ranks exit."""
+    if rank != 0:
+        return
+    scb = importlib.import_module("scunet-rs_b200")
+    img = scb.synth.frames(4000, 1, H, W)[0]
+    size = 128
+    times = []
+    for i in range(a.warmup + a.steps):
+        mps, dt, cores = cpu_oracle_mps(img, size)
+        if i >= a.warmup:
+            times.append(dt)
+    tot = sum(times)
+    value = a.steps * size * size / 1e6 / tot
+    sample = (f"{size}x{size} crop of a config-4 frame per step (CPU oracle port of the reference's forward, "
+              f"numpy float32, all BLAS threads)")
+    print(json.dumps({
+        "impl": "reference", "metric": "megapixels/sec", "value": value, "unit": "MP/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4 1920x1080 RGB frames (bounded CPU sample)", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "MP/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "MP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    a = args_()
+    rank, world, local = dist_env()
+    if a.impl == "reference":
+        reference_arm(a, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+
+    scb = importlib.import_module("scunet-rs_b200")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    F, micro = a.frames, a.micro
+    assert F % micro == 0, "--frames must be a multiple of --micro"
+    wt = scb.Weights.seeded(3, 0)
+    be = scb.B200(wt, device=local)
+    frames = scb.synth.frames(4000 + rank, F, H, W, distinct=min(F, 4))
+    x_dev = torch.from_numpy(frames).cuda()
+    y_dev = torch.empty((F, C, H, W), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        for i in range(0, F, micro):
+            be.forward_dev(x_dev[i].data_ptr(), scb.SCB_U8, micro, C, H, W, y_dev[i].data_ptr(), scb.SCB_F32, sp)
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    launches_per_call = be.last_launch_count()
+    barrier()
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clk = Clocks(uuid)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(a.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = t0.elapsed_time(t1) / a.steps
+    ms = max_over_ranks(ms)
+    barrier()
+    mp_step = F * H * W * world / 1e6
+    value = mp_step / (ms / 1e3)
+
+    # ---- live per-launch profile of one call (untimed above) -> roofline ----
+    be.set_profiling(True)
+    be.forward_dev(x_dev[0].data_ptr(), scb.SCB_U8, micro, C, H, W, y_dev[0].data_ptr(), scb.SCB_F32, sp)
+    torch.cuda.synchronize()
+    prof = be.profile()
+    be.set_profiling(False)
+    cls = {}
+    for name, fl, t in prof:
+        c = cls.setdefault(name, [0.0, 0.0, 0])
+        c[0] += fl
+        c[1] += t
+        c[2] += 1
+    tot_ms = sum(v[1] for v in cls.values())
+    dom = max(cls, key=lambda k: cls[k][1])
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    achieved = cls[dom][0] / (cls[dom][1] / 1e3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom)
+    roofline = {
+        "kernel": f"gemm_tc_kernel [{dom}]" if dom != "attention" else "window_attn_kernel",
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+        "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,
+        "launches": cls[dom][2], "share_of_forward": cls[dom][1] / tot_ms,
+        "classes_ms_share": {k: round(v[1] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][1])},
+        "whole_forward_tflops": sum(v[0] for v in cls.values()) / (tot_ms / 1e3) / 1e12,
+    }
+
+    # ---- end to end through the host-pointer C ABI ----
+    e2e = None
+    if not a.no_e2e:
+        hx = torch.from_numpy(frames).pin_memory()
+        hy = torch.empty((F, C, H, W), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            for i in range(0, F, micro):
+                rc = be.lib.scb_forward_host(be.ctx, hx[i].data_ptr(), scb.SCB_U8, micro, C, H, W, hy[i].data_ptr(),
+                                             scb.SCB_F32)
+                if rc:
+                    raise RuntimeError(be.lib.scb_last_error(be.ctx).decode())
+
+        e2e_step()
+        barrier()
+        t = time.perf_counter()
+        for _ in range(a.steps):
+            e2e_step()
+        dt = (time.perf_counter() - t) / a.steps
+        dt = max_over_ranks(dt)
+        e2e = {"value": mp_step / dt, "unit": "MP/s", "h2d_bytes_per_step": int(hx.numel()),
+               "d2h_bytes_per_step": int(hy.numel() * 4), "api": "scb_forward_host (pinned host buffers)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        mps, dt, cores = cpu_oracle_mps(frames[0], 256)
+        cpu = {"value": mps, "unit": "MP/s", "cores": cores, "kind": "port",
+               "sample": f"one 256x256 crop of frame 0 ({dt:.1f} s), numpy oracle of the reference forward"}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": "megapixels/sec (device-timed, max over ranks)", "value": value, "unit": "MP/s",
+            "n_gpus": world, "steps": a.steps, "warmup": max(a.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded config-4 frames; seeded weights)",
+            "config": {"workload": "config4: 1920x1080 RGB uint8 frames -> 1920x1088 padded, colour SCUNet",
+                       "frames_per_gpu": F, "global_batch": F * world, "micro_batch": micro,
+                       "parallelism": f"dp{world} (batch sharding, no collective)",
+                       "l2": "inputs larger than L2 (each step streams %.1f GB of activations)" % (
+                           scb.need_bytes(micro, 3, 1088, 1920) / 1e9),
+                       "arith": "fp16 tensor-core operands, fp32 accumulate and residual stream"},
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_call * (F // micro) * a.steps,
+            "roofline": roofline, "cpu_baseline": cpu,
+        }), flush=True)
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
