@@ -134,6 +134,13 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
 /* Number of kernel launches the last forward issued (for launch accounting). */
 int scb_last_launch_count(const scb_ctx* ctx);
 
+/* Execution options. SCB_OPT_FUSE_TRANS (default 1): run the transformer half of
+ * the blocks whose trans width is 32 or 64 (full and half resolution) as one fused
+ * kernel; 0 runs it as separate qkv / attention / proj / mlp launches (the
+ * reference's op sequence, src/cuda.rs:1104-1131). Takes effect at the next forward. */
+enum { SCB_OPT_FUSE_TRANS = 1 };
+int scb_set_option(scb_ctx* ctx, int option, int value);
+
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,
  * 263-273): while on, every launch of a forward is bracketed by CUDA events on the
  * launch stream. */

@@ -28,8 +28,9 @@ SYMBOLS = [
     "scb_create", "scb_forward", "scb_forward_dev", "scb_forward_host", "scb_need_bytes", "scb_footprint",
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
-    "scb_set_profiling", "scb_profile_read",
+    "scb_set_profiling", "scb_profile_read", "scb_set_option",
 ]
+SCB_OPT_FUSE_TRANS = 1
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up"]
 
 
@@ -78,6 +79,7 @@ def load_library(path=None):
     lib.scb_probe_attention.argtypes = [vp, vp, i, i, i, i, i, vp, vp]
     lib.scb_probe_block.argtypes = [vp, i, i, vp, i, i, i, vp]
     lib.scb_set_profiling.argtypes = [vp, i]
+    lib.scb_set_option.argtypes = [vp, i, i]
     lib.scb_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(ctypes.c_float), i]
     if path is None:
@@ -167,6 +169,9 @@ class B200:
         """Device pointers (e.g. torch tensors' data_ptr()); asynchronous."""
         self._check(self.lib.scb_forward_dev(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream or None),
                     "scb_forward_dev")
+
+    def set_option(self, option, value):
+        self._check(self.lib.scb_set_option(self.ctx, option, int(value)), "scb_set_option")
 
     def set_profiling(self, on):
         self._check(self.lib.scb_set_profiling(self.ctx, int(bool(on))), "scb_set_profiling")

@@ -69,6 +69,31 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
+// One 16-column chunk of a row's residual inputs, loaded ahead of use.
+struct ResChunk {
+  uint4 r16[2];
+  float4 r32[4];
+  float4 sk[4];
+};
+
+__device__ __forceinline__ void load_res(const GemmEpi& e, long p, int oc, ResChunk& rc) {
+  if (e.res16) {
+    const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + oc);
+    rc.r16[0] = __ldg(src);
+    rc.r16[1] = __ldg(src + 1);
+  }
+  if (e.res32) {
+    const float4* src = reinterpret_cast<const float4*>(e.res32 + p * e.res32_ld + oc);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) rc.r32[h] = __ldg(src + h);
+  }
+  if (e.skip32) {
+    const float4* src = reinterpret_cast<const float4*>(e.skip32 + p * e.skip_ld + oc);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) rc.sk[h] = __ldg(src + h);
+  }
+}
+
 template <int BN, int BK, int STAGES>
 struct GemmSmem {
   static constexpr int A_BYTES = 128 * BK * 2;
@@ -113,7 +138,7 @@ __device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int 
 }
 
 template <int BN, int BK, int STAGES, int GEO>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
                const GemmEpi e) {
   using L = GemmSmem<BN, BK, STAGES>;
@@ -222,6 +247,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else {
     // ---------------- epilogue: warps 2..5, thread = accumulator row ----------------
+    // Residual loads are software-pipelined one 16-column chunk ahead, and the
+    // first chunk's loads are issued before waiting for the accumulator, so their
+    // latency hides behind this tile's main loop.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
     uint32_t t = 0;
@@ -229,15 +257,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
       const int n0 = nt * BN;
       const uint32_t a = t & 1, aph = (t >> 1) & 1;
-      if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
-      tc_fence_after();
       int col0;
       const long p = row_pixel<GEO>(g, mt, r, n0, col0);
+      ResChunk cur, nxt;
+      if (p >= 0) load_res(e, p, col0, cur);
+      if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
       const bool do_ln = e.ln_out != nullptr && e.ln_lo >= n0 && e.ln_lo < n0 + BN;
       float ln_sum = 0.f, ln_sq = 0.f, ln_shift = 0.f;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
+        if (p >= 0 && c + 16 < BN) load_res(e, p, col0 + c + 16, nxt);
         float v[16];
         tmem_ld16(tbase + c, v);
         const int n = n0 + c;       // global GEMM column
@@ -255,11 +286,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         if (p >= 0) {
           if (e.res16) {
-            const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + oc);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              uint4 u = __ldg(src + h);
-              const __half2* hp = reinterpret_cast<const __half2*>(&u);
+              const __half2* hp = reinterpret_cast<const __half2*>(&cur.r16[h]);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 float2 f = __half22float2(hp[j]);
@@ -269,11 +298,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
           }
           if (e.res32) {
-            const float4* src = reinterpret_cast<const float4*>(e.res32 + p * e.res32_ld + oc);
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-              float4 f = __ldg(src + h);
-              v[4 * h] += f.x; v[4 * h + 1] += f.y; v[4 * h + 2] += f.z; v[4 * h + 3] += f.w;
+              v[4 * h] += cur.r32[h].x; v[4 * h + 1] += cur.r32[h].y;
+              v[4 * h + 2] += cur.r32[h].z; v[4 * h + 3] += cur.r32[h].w;
             }
           }
           if (e.out32) {
@@ -286,11 +314,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 16; ++j) s[j] = v[j];
             if (e.skip32) {
-              const float4* sk = reinterpret_cast<const float4*>(e.skip32 + p * e.skip_ld + oc);
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
-                float4 f = __ldg(sk + h);
-                s[4 * h] += f.x; s[4 * h + 1] += f.y; s[4 * h + 2] += f.z; s[4 * h + 3] += f.w;
+                s[4 * h] += cur.sk[h].x; s[4 * h + 1] += cur.sk[h].y;
+                s[4 * h + 2] += cur.sk[h].z; s[4 * h + 3] += cur.sk[h].w;
               }
             }
             uint4* dst = reinterpret_cast<uint4*>(e.out16 + p * e.out16_ld + oc);
@@ -309,6 +336,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             ln_sq += d * d;
           }
         }
+        cur = nxt;
       }
       if (do_ln) {
         // Second pass over the LN columns: recompute v exactly as above and normalise.

@@ -30,6 +30,7 @@
 #include "attn.cuh"
 #include "gemm.cuh"
 #include "io_kernels.cuh"
+#include "trans.cuh"
 
 using namespace scb;
 
@@ -88,8 +89,14 @@ bool encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims
 // --------------------------------------------------------------------------
 // GEMM op: tiles, maps, dispatch over the compiled (BN, BK, GEO) variants
 // --------------------------------------------------------------------------
+// Pipeline depth: GEMMs whose two accumulators fit in half of TMEM (BN <= 128) run
+// two CTAs per SM (more epilogue warps to hide load latency) with ~100 KB of
+// stages each; the BN >= 192 variants own the SM's TMEM and take ~192 KB.
+constexpr int ctas_per_sm_for(int bn) { return bn <= 128 ? 2 : 1; }
 constexpr int stages_for(int bn, int bk) {
-  return (196608 / ((128 + bn) * bk * 2)) > 8 ? 8 : (196608 / ((128 + bn) * bk * 2));
+  return ((ctas_per_sm_for(bn) == 2 ? 100000 : 196608) / ((128 + bn) * bk * 2)) > 8
+             ? 8
+             : ((ctas_per_sm_for(bn) == 2 ? 100000 : 196608) / ((128 + bn) * bk * 2));
 }
 
 struct GemmOp {
@@ -113,7 +120,7 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const int tiles = op.g.m_tiles * op.g.n_tiles;
-  const int grid = std::max(1, std::min(tiles, sms));
+  const int grid = std::max(1, std::min(tiles, sms * ctas_per_sm_for(BN)));
   kfn<<<grid, 192, L::TOTAL, st>>>(op.ta, op.tb, op.g, op.e);
   return cudaGetLastError();
 }
@@ -300,7 +307,9 @@ enum OpTag : int {
 };
 
 struct Op {
-  enum Kind { GEMM, ATTN, HEAD, TAIL } kind;
+  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS } kind;
+  TransGeom trans{};
+  int trans_t = 0;
   int tag = 0;
   double flops = 0;  // algorithmic FLOPs of this launch (2 per multiply-add)
   GemmOp gemm;
@@ -372,6 +381,7 @@ struct scb_ctx {
   float* wtail = nullptr;
   Arena arena;
   int last_launches = 0;
+  bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
   // SCUNET_PROFILE equivalent (src/cuda.rs:106-135): events around every launch
   bool profiling = false;
   std::vector<cudaEvent_t> events;
@@ -463,6 +473,29 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <int T>
+cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
+  using L = TransLayout<T>;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(trans_fused_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long pairs = (op.trans.n_windows + 1) / 2;
+  const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
+  trans_fused_kernel<T><<<grid, 128, L::SMEM, st>>>(op.trans);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
+  if (op.trans_t == 32) return launch_trans_t<32>(op, sms, st);
+  if (op.trans_t == 64) return launch_trans_t<64>(op, sms, st);
+  return cudaErrorInvalidConfiguration;
+}
+
 // Run the ops of the arena's plan on `st`, with the image pointers of this call.
 int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w, cudaStream_t st) {
   Arena& A = ctx->arena;
@@ -498,6 +531,9 @@ int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int
       case Op::ATTN:
         e = launch_attn(op, st);
         break;
+      case Op::TRANS:
+        e = launch_trans(op, ctx->sms, st);
+        break;
     }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
     ++launches;
@@ -523,6 +559,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
                const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err) {
   const int c = bw.c, t = c / 2, cc = c / 2, heads = t / 32;
   const long P = (long)n * H * W;
+  const bool fused = ctx->fuse_trans && (t == 32 || t == 64);
   Maker mk{&err};
   Op op{};
   op.kind = Op::GEMM;
@@ -533,12 +570,14 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.bias = bw.b11;
     g.e.out16 = A.y;
     g.e.out16_ld = c;
-    g.e.ln_g = bw.ln1g;
-    g.e.ln_b = bw.ln1b;
-    g.e.ln_out = A.a;
-    g.e.ln_ld = t;
-    g.e.ln_lo = cc;
-    g.e.ln_n = t;
+    if (!fused) {  // the fused transformer kernel normalises its own input
+      g.e.ln_g = bw.ln1g;
+      g.e.ln_b = bw.ln1b;
+      g.e.ln_out = A.a;
+      g.e.ln_ld = t;
+      g.e.ln_lo = cc;
+      g.e.ln_n = t;
+    }
     op.gemm = g;
     op.tag = TAG_CONV1X1;
     op.flops = 2.0 * P * c * c;
@@ -569,76 +608,96 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     op.flops = 2.0 * P * 9 * cc * cc;
     ops.push_back(op);
   }
-  // 4. qkv = LN1(y_t) W^T + b
-  {
-    GemmOp g{};
-    if (!mk.flat(g, A.a, P, t, t, bw.wqkv, 3 * t)) return false;
-    g.e.bias = bw.bqkv;
-    g.e.out16 = A.qh;
-    g.e.out16_ld = 3 * t;
-    op.gemm = g;
-    op.tag = TAG_QKV;
-    op.flops = 2.0 * P * t * 3 * t;
-    ops.push_back(op);
-  }
-  // 5. window attention
-  {
-    Op at{};
-    at.kind = Op::ATTN;
-    at.attn = AttnGeom{n, H, W, t, heads, shifted ? 4 : 0, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
-    at.attn_in = A.qh;
-    at.attn_out = A.o;
-    at.attn_rp = bw.rp;
-    at.tag = TAG_ATTN;
-    at.flops = 2.0 * 2.0 * P * 64 * t;
-    ops.push_back(at);
-  }
-  // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
-  {
-    GemmOp g{};
-    if (!mk.flat(g, A.o, P, t, t, bw.wproj, t)) return false;
-    g.e.bias = bw.bproj;
-    g.e.res16 = A.y + cc;
-    g.e.res16_ld = c;
-    g.e.out16 = A.z + cc;
-    g.e.out16_ld = c;
-    g.e.ln_g = bw.ln2g;
-    g.e.ln_b = bw.ln2b;
-    g.e.ln_out = A.a;
-    g.e.ln_ld = t;
-    g.e.ln_lo = 0;
-    g.e.ln_n = t;
-    op.gemm = g;
-    op.tag = TAG_PROJ;
-    op.flops = 2.0 * P * t * t;
-    ops.push_back(op);
-  }
-  // 7. hid = gelu(LN2 W0^T + b0)
-  {
-    GemmOp g{};
-    if (!mk.flat(g, A.a, P, t, t, bw.w0, 4 * t)) return false;
-    g.e.bias = bw.b0;
-    g.e.act = ACT_GELU;
-    g.e.out16 = A.qh;
-    g.e.out16_ld = 4 * t;
-    op.gemm = g;
-    op.tag = TAG_MLP0;
-    op.flops = 2.0 * P * t * 4 * t;
-    ops.push_back(op);
-  }
-  // 8. z[:, cc:] = hid W2^T + b2 + x1t
-  {
-    GemmOp g{};
-    if (!mk.flat(g, A.qh, P, 4 * t, 4 * t, bw.w2, t)) return false;
-    g.e.bias = bw.b2;
-    g.e.res16 = A.z + cc;
-    g.e.res16_ld = c;
-    g.e.out16 = A.z + cc;
-    g.e.out16_ld = c;
-    op.gemm = g;
-    op.tag = TAG_MLP2;
-    op.flops = 2.0 * P * t * 4 * t;
-    ops.push_back(op);
+  if (fused) {
+    // 4-8. the whole transformer half in one kernel
+    Op tr{};
+    tr.kind = Op::TRANS;
+    tr.trans_t = t;
+    tr.tag = TAG_ATTN;
+    tr.flops = 2.0 * P * (3.0 * t * t + 2.0 * 64 * t + t * t + 8.0 * t * t);
+    TransGeom& tg = tr.trans;
+    tg.H = H;
+    tg.W = W;
+    tg.shift = shifted ? 4 : 0;
+    tg.n_windows = (long)n * (H / 8) * (W / 8);
+    tg.y = A.y;
+    tg.z = A.z;
+    tg.wqkv = bw.wqkv; tg.wproj = bw.wproj; tg.w0 = bw.w0; tg.w2 = bw.w2;
+    tg.bqkv = bw.bqkv; tg.bproj = bw.bproj; tg.b0 = bw.b0; tg.b2 = bw.b2;
+    tg.ln1g = bw.ln1g; tg.ln1b = bw.ln1b; tg.ln2g = bw.ln2g; tg.ln2b = bw.ln2b; tg.rp = bw.rp;
+    ops.push_back(tr);
+  } else {
+    // 4. qkv = LN1(y_t) W^T + b
+    {
+      GemmOp g{};
+      if (!mk.flat(g, A.a, P, t, t, bw.wqkv, 3 * t)) return false;
+      g.e.bias = bw.bqkv;
+      g.e.out16 = A.qh;
+      g.e.out16_ld = 3 * t;
+      op.gemm = g;
+      op.tag = TAG_QKV;
+      op.flops = 2.0 * P * t * 3 * t;
+      ops.push_back(op);
+    }
+    // 5. window attention
+    {
+      Op at{};
+      at.kind = Op::ATTN;
+      at.attn = AttnGeom{n, H, W, t, heads, shifted ? 4 : 0, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
+      at.attn_in = A.qh;
+      at.attn_out = A.o;
+      at.attn_rp = bw.rp;
+      at.tag = TAG_ATTN;
+      at.flops = 2.0 * 2.0 * P * 64 * t;
+      ops.push_back(at);
+    }
+    // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
+    {
+      GemmOp g{};
+      if (!mk.flat(g, A.o, P, t, t, bw.wproj, t)) return false;
+      g.e.bias = bw.bproj;
+      g.e.res16 = A.y + cc;
+      g.e.res16_ld = c;
+      g.e.out16 = A.z + cc;
+      g.e.out16_ld = c;
+      g.e.ln_g = bw.ln2g;
+      g.e.ln_b = bw.ln2b;
+      g.e.ln_out = A.a;
+      g.e.ln_ld = t;
+      g.e.ln_lo = 0;
+      g.e.ln_n = t;
+      op.gemm = g;
+      op.tag = TAG_PROJ;
+      op.flops = 2.0 * P * t * t;
+      ops.push_back(op);
+    }
+    // 7. hid = gelu(LN2 W0^T + b0)
+    {
+      GemmOp g{};
+      if (!mk.flat(g, A.a, P, t, t, bw.w0, 4 * t)) return false;
+      g.e.bias = bw.b0;
+      g.e.act = ACT_GELU;
+      g.e.out16 = A.qh;
+      g.e.out16_ld = 4 * t;
+      op.gemm = g;
+      op.tag = TAG_MLP0;
+      op.flops = 2.0 * P * t * 4 * t;
+      ops.push_back(op);
+    }
+    // 8. z[:, cc:] = hid W2^T + b2 + x1t
+    {
+      GemmOp g{};
+      if (!mk.flat(g, A.qh, P, 4 * t, 4 * t, bw.w2, t)) return false;
+      g.e.bias = bw.b2;
+      g.e.res16 = A.z + cc;
+      g.e.res16_ld = c;
+      g.e.out16 = A.z + cc;
+      g.e.out16_ld = c;
+      op.gemm = g;
+      op.tag = TAG_MLP2;
+      op.flops = 2.0 * P * t * 4 * t;
+      ops.push_back(op);
+    }
   }
   // 9. x = x + conv1_2(z) + b  (fp32) and its shadow (or the shadow of x + skip)
   {
@@ -1019,6 +1078,17 @@ void scb_release_scratch(scb_ctx* ctx) {
   ctx->arena = Arena{};
 }
 
+int scb_set_option(scb_ctx* ctx, int option, int value) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (option == SCB_OPT_FUSE_TRANS) {
+    ctx->fuse_trans = value != 0;
+    ctx->arena.ops.clear();
+    ctx->arena.n = 0;  // re-plan on the next forward
+    return SCB_OK;
+  }
+  return fail(ctx, SCB_EINVAL, "unknown option " + std::to_string(option));
+}
+
 int scb_set_profiling(scb_ctx* ctx, int on) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   ctx->profiling = on != 0;
@@ -1188,6 +1258,8 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
   for (const Op& op : ops) {
     if (op.kind == Op::GEMM) {
       e = launch_gemm(op.gemm, ctx->sms, ctx->stream);
+    } else if (op.kind == Op::TRANS) {
+      e = launch_trans(op, ctx->sms, ctx->stream);
     } else {
       e = launch_attn(op, ctx->stream);
     }

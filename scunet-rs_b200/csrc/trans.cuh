@@ -1,0 +1,432 @@
+// The whole transformer half of a ConvTransBlock in one kernel, for the two
+// widest stages (trans width T = 32 at full resolution, T = 64 at 1/2):
+//
+//   x  = y_t                                   (fp16 plane, columns [T, 2T) of Y)
+//   x1 = x + proj(WMSA(LN1(x)))                (tools/network_scunet.py:134-135)
+//   z  = x1 + mlp2(GELU(mlp0(LN2(x1))))        (tools/network_scunet.py:128-136)
+//   -> columns [T, 2T) of Z (fp16), the conv1_2 operand.
+//
+// WMSA semantics are those of window_attn_kernel (attn.cuh): cyclic shift read in
+// place, rel-pos bias, SW mask on the last window row/column, softmax, P.V.
+//
+// One CTA (128 threads, thread = token row) walks pairs of 8x8 windows (128
+// tokens) persistently. Every GEMM of the block runs on tcgen05 with its
+// accumulator in TMEM and its operands in shared memory:
+//
+//   qkv   [128 x 3T] = LN1 [128 x T]  . Wqkv^T       (one UMMA chain, N = 3T)
+//   S_h   [128 x 128] = Q_h . K_h^T                  (both windows at once; the
+//         off-window half of each row is never read and P is zero there)
+//   O_h   [128 x 32]  = P_h . V_h
+//   proj  [128 x T]   = O . Wproj^T
+//   hid_j [128 x 128] = LN2 . W0[j]^T                (hidden in 128-wide chunks)
+//   mlp   [128 x T]  += GELU(hid_j) . W2[:, j]^T
+//
+// The weights of the block (24 KB at T = 32, 96 KB at T = 64, fp16) stay in
+// shared memory for the CTA's lifetime; the next pair's tokens are prefetched
+// into registers while the current pair computes. HBM traffic is one read of y_t
+// and one write of z_t per token.
+#pragma once
+#include "ptx.cuh"
+
+namespace scb {
+
+struct TransGeom {
+  int H, W;           // plane per image
+  int shift;          // 0 (W) or 4 (SW)
+  long n_windows;     // n * (H/8) * (W/8)
+  const __half* y;    // Y plane, pixel stride 2T, trans half at column T
+  __half* z;          // Z plane, pixel stride 2T, output at column T
+  const __half* wqkv; // [3T][T]
+  const __half* wproj;// [T][T]
+  const __half* w0;   // [4T][T]
+  const __half* w2;   // [T][4T]
+  const float *bqkv, *bproj, *b0, *b2, *ln1g, *ln1b, *ln2g, *ln2b, *rp;
+};
+
+template <int T>
+struct TransLayout {
+  static constexpr int HEADS = T / 32;
+  static constexpr int RB = T * 2;  // bytes of a T-wide fp16 row (64 or 128 = the swizzle span)
+  static constexpr uint32_t SWZ = (T == 32) ? SW_64B : SW_128B;
+  static constexpr int W_QKV = 0;
+  static constexpr int W_PROJ = W_QKV + 3 * T * RB;
+  static constexpr int W_0 = W_PROJ + T * RB;
+  static constexpr int W_2 = W_0 + 4 * T * RB;          // (4T/64) K-blocks of [T rows x 128 B]
+  static constexpr int A1 = W_2 + 4 * T * 2 * T;         // LN1 out, then LN2 out
+  static constexpr int QS = A1 + 128 * RB;
+  static constexpr int KS = QS + 128 * 64;
+  static constexpr int VT = KS + 128 * 64;               // 2 x [32 x 128 B]
+  static constexpr int PS = VT + 2 * 32 * 128;           // 2 x [128 x 128 B]; also the MLP hidden chunk
+  static constexpr int OS = PS + 2 * 128 * 128;
+  static constexpr int PAR = OS + 128 * RB;              // fp32 parameters
+  static constexpr int P_BQKV = 0, P_BPROJ = 3 * T, P_B0 = 4 * T, P_B2 = 8 * T, P_L1G = 9 * T, P_L1B = 10 * T,
+                       P_L2G = 11 * T, P_L2B = 12 * T, P_RP = 13 * T, P_N = 13 * T + HEADS * 225;
+  static constexpr int BAR = (PAR + P_N * 4 + 15) & ~15;
+  static constexpr int SMEM = BAR + 64 + 1024;
+  // TMEM columns
+  static constexpr int C_QKV = 0, C_O = 3 * T, C_S = 4 * T, C_PROJ = 0, C_MLP2 = T, C_HID = 4 * T;
+  static constexpr int TMEM_COLS = (T == 32) ? 256 : 512;
+  static constexpr int CTAS = (T == 32) ? 2 : 1;
+};
+
+// Copy a row-major fp16 [R][K] matrix into K-major swizzled tiles: K split into
+// blocks of `kblk` elements (kblk*2 = row bytes = swizzle span), block b at
+// dst + b * R * kblk * 2.
+__device__ __forceinline__ void stage_kmajor(uint8_t* dst, const __half* src, int R, int K, int kblk) {
+  const int rb = kblk * 2, cpr = K / 8, cpb = kblk / 8;
+  for (int idx = threadIdx.x; idx < R * cpr; idx += blockDim.x) {
+    const int r = idx / cpr, j = idx - r * cpr;
+    const int b = j / cpb, jj = j - b * cpb;
+    *reinterpret_cast<uint4*>(dst + b * R * rb + swz_off(r, jj, rb)) =
+        __ldg(reinterpret_cast<const uint4*>(src + (long)r * K + j * 8));
+  }
+}
+
+__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+template <int T>
+__global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(const TransGeom g) {
+  using L = TransLayout<T>;
+  constexpr int NCH = T / 8;  // 16-byte chunks per token row
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* par = reinterpret_cast<float*>(sm + L::PAR);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  // ---- once per CTA: weights and parameters into shared memory ----
+  stage_kmajor(sm + L::W_QKV, g.wqkv, 3 * T, T, T);
+  stage_kmajor(sm + L::W_PROJ, g.wproj, T, T, T);
+  stage_kmajor(sm + L::W_0, g.w0, 4 * T, T, T);
+  stage_kmajor(sm + L::W_2, g.w2, T, 4 * T, 64);
+  for (int i = tid; i < L::P_N; i += 128) {
+    float v;
+    if (i < L::P_BPROJ) v = g.bqkv[i];
+    else if (i < L::P_B0) v = g.bproj[i - L::P_BPROJ];
+    else if (i < L::P_B2) v = g.b0[i - L::P_B0];
+    else if (i < L::P_L1G) v = g.b2[i - L::P_B2];
+    else if (i < L::P_L1B) v = g.ln1g[i - L::P_L1G];
+    else if (i < L::P_L2G) v = g.ln1b[i - L::P_L1B];
+    else if (i < L::P_L2B) v = g.ln2g[i - L::P_L2G];
+    else if (i < L::P_RP) v = g.ln2b[i - L::P_L2B];
+    else v = g.rp[i - L::P_RP];
+    par[i] = v;
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t sb = smem_u32(sm);
+  uint32_t phase = 0;
+
+  const int slot = tid >> 6, tok = tid & 63;
+  const int qi = tok >> 3, qj = tok & 7;
+  const int nwh = g.H >> 3, nww = g.W >> 3;
+  const long per_img = (long)nwh * nww;
+  const long n_pairs = (g.n_windows + 1) / 2;
+  constexpr float kScale = 0.17677669529663687f;  // 32^-1/2
+  constexpr float kLog2e = 1.4426950408889634f;
+
+  // token -> pixel of pair `pr` (or -1 when the window does not exist)
+  auto locate = [&](long pr, bool& lr, bool& lc) -> long {
+    const long win = 2 * pr + slot;
+    lr = lc = false;
+    if (pr >= n_pairs || win >= g.n_windows) return -1;
+    const long img = win / per_img;
+    const int wrem = (int)(win - img * per_img);
+    const int wh = wrem / nww, ww = wrem - wh * nww;
+    const int y = (wh * 8 + qi + g.shift) % g.H;
+    const int x = (ww * 8 + qj + g.shift) % g.W;
+    lr = g.shift && wh == nwh - 1;
+    lc = g.shift && ww == nww - 1;
+    return (img * g.H + y) * g.W + x;
+  };
+  auto sync_mma = [&]() {  // all threads: operands written, TMEM reads finished
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
+  auto wait_mma = [&]() {
+    mbar_wait(bar, phase, SCB_ERR_WAIT_ATTN);
+    phase ^= 1;
+    tc_fence_after();
+  };
+
+  long pair = blockIdx.x;
+  bool lr_n, lc_n;
+  long pix_n = locate(pair, lr_n, lc_n);
+  uint4 nx[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+    nx[c] = pix_n >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix_n * (2 * T) + T) + c) : make_uint4(0, 0, 0, 0);
+
+  for (; pair < n_pairs; pair += gridDim.x) {
+    const long pix = pix_n;
+    const bool last_row = lr_n, last_col = lc_n;
+    uint4 cur[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) cur[c] = nx[c];
+    pix_n = locate(pair + gridDim.x, lr_n, lc_n);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      nx[c] = pix_n >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix_n * (2 * T) + T) + c) : make_uint4(0, 0, 0, 0);
+
+    // ---- LN1 -> A1 ----
+    {
+      float x[T];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&cur[c]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h2[j]);
+          x[8 * c + 2 * j] = f.x;
+          x[8 * c + 2 * j + 1] = f.y;
+        }
+      }
+      float mu = 0.f;
+#pragma unroll
+      for (int k = 0; k < T; ++k) mu += x[k];
+      mu *= 1.f / T;
+      float var = 0.f;
+#pragma unroll
+      for (int k = 0; k < T; ++k) var += (x[k] - mu) * (x[k] - mu);
+      const float rstd = rsqrtf(var * (1.f / T) + 1e-5f);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (x[8 * c + j] - mu) * rstd * par[L::P_L1G + 8 * c + j] + par[L::P_L1B + 8 * c + j];
+        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(tid, c, L::RB)) =
+            make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+      }
+      // the other window's key half of P must read as zero in every P.V product
+      uint8_t* pz = sm + L::PS + (slot ^ 1) * 16384;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(pz + swz_off(tid, c, 128)) = make_uint4(0, 0, 0, 0);
+    }
+    sync_mma();
+    if (tid == 0) {
+      constexpr uint32_t id = make_idesc_f16(128, 3 * T);
+#pragma unroll
+      for (int k = 0; k < T / 16; ++k)
+        umma_f16(tmem + L::C_QKV, make_sdesc(sb + L::A1 + k * 32, L::RB, L::SWZ),
+                 make_sdesc(sb + L::W_QKV + k * 32, L::RB, L::SWZ), id, k);
+      umma_commit(bar);
+    }
+    wait_mma();
+
+    // ---- window attention, head by head ----
+    for (int h = 0; h < L::HEADS; ++h) {
+      {
+        float q[32], k[32], v[32];
+        tmem_ld16(trow + L::C_QKV + h * 32, q);
+        tmem_ld16(trow + L::C_QKV + h * 32 + 16, q + 16);
+        tmem_ld16(trow + L::C_QKV + T + h * 32, k);
+        tmem_ld16(trow + L::C_QKV + T + h * 32 + 16, k + 16);
+        tmem_ld16(trow + L::C_QKV + 2 * T + h * 32, v);
+        tmem_ld16(trow + L::C_QKV + 2 * T + h * 32 + 16, v + 16);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float a[8], b[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            a[j] = q[8 * c + j] + par[L::P_BQKV + h * 32 + 8 * c + j];
+            b[j] = k[8 * c + j] + par[L::P_BQKV + T + h * 32 + 8 * c + j];
+          }
+          *reinterpret_cast<uint4*>(sm + L::QS + swz_off(tid, c, 64)) =
+              make_uint4(pack_half2(a[0], a[1]), pack_half2(a[2], a[3]), pack_half2(a[4], a[5]), pack_half2(a[6], a[7]));
+          *reinterpret_cast<uint4*>(sm + L::KS + swz_off(tid, c, 64)) =
+              make_uint4(pack_half2(b[0], b[1]), pack_half2(b[2], b[3]), pack_half2(b[4], b[5]), pack_half2(b[6], b[7]));
+        }
+        uint8_t* vb = sm + L::VT + slot * 4096;
+        const uint32_t kk = tid & 63;
+#pragma unroll
+        for (int d = 0; d < 32; ++d)
+          *reinterpret_cast<__half*>(vb + swz_off(d, kk >> 3, 128) + (kk & 7) * 2) =
+              __float2half_rn(v[d] + par[L::P_BQKV + 2 * T + h * 32 + d]);
+      }
+      sync_mma();
+      if (tid == 0) {
+        constexpr uint32_t id = make_idesc_f16(128, 128);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          umma_f16(tmem + L::C_S, make_sdesc(sb + L::QS + k * 32, 64, SW_64B), make_sdesc(sb + L::KS + k * 32, 64, SW_64B),
+                   id, k);
+        umma_commit(bar);
+      }
+      wait_mma();
+      float s[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld16(trow + L::C_S + slot * 64 + c * 16, s + c * 16);
+      const float* bh = par + L::P_RP + h * 225;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int kt = 0; kt < 64; ++kt) {
+        const int ki = kt >> 3, kj = kt & 7;
+        float v = s[kt] * kScale + bh[(qi - ki + 7) * 15 + (qj - kj + 7)];
+        const bool masked = (last_row && ((qi < 4) != (ki < 4))) || (last_col && ((qj < 4) != (kj < 4)));
+        v = masked ? -INFINITY : v;
+        s[kt] = v;
+        mx = fmaxf(mx, v);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int kt = 0; kt < 64; ++kt) {
+        const float e = exp2f((s[kt] - mx) * kLog2e);
+        s[kt] = e;
+        sum += e;
+      }
+      {
+        uint8_t* pr = sm + L::PS + slot * 16384;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(pr + swz_off(tid, c, 128)) =
+              make_uint4(pack_half2(s[8 * c], s[8 * c + 1]), pack_half2(s[8 * c + 2], s[8 * c + 3]),
+                         pack_half2(s[8 * c + 4], s[8 * c + 5]), pack_half2(s[8 * c + 6], s[8 * c + 7]));
+      }
+      sync_mma();
+      if (tid == 0) {
+        constexpr uint32_t id = make_idesc_f16(128, 32);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + L::C_O + h * 32, make_sdesc(sb + L::PS + kb * 16384 + k * 32, 128, SW_128B),
+                     make_sdesc(sb + L::VT + kb * 4096 + k * 32, 128, SW_128B), id, (kb | k) != 0);
+        umma_commit(bar);
+      }
+      wait_mma();
+      {
+        float o[32];
+        tmem_ld16(trow + L::C_O + h * 32, o);
+        tmem_ld16(trow + L::C_O + h * 32 + 16, o + 16);
+        const float inv = 1.f / sum;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          // head h occupies 16-byte chunks [4h, 4h + 4) of the T-wide O row
+          *reinterpret_cast<uint4*>(sm + L::OS + swz_off(tid, 4 * h + c, L::RB)) =
+              make_uint4(pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv), pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                         pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
+                         pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+        }
+      }
+      sync_mma();  // Q/K/V^T/P free for the next head; O complete after the last
+    }
+
+    // ---- proj + residual -> x1, LN2 -> A1 ----
+    if (tid == 0) {
+      constexpr uint32_t id = make_idesc_f16(128, T);
+#pragma unroll
+      for (int k = 0; k < T / 16; ++k)
+        umma_f16(tmem + L::C_PROJ, make_sdesc(sb + L::OS + k * 32, L::RB, L::SWZ),
+                 make_sdesc(sb + L::W_PROJ + k * 32, L::RB, L::SWZ), id, k);
+      umma_commit(bar);
+    }
+    wait_mma();
+    float x1[T];
+    {
+#pragma unroll
+      for (int c = 0; c < T; c += 16) tmem_ld16(trow + L::C_PROJ + c, x1 + c);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&cur[c]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h2[j]);
+          x1[8 * c + 2 * j] += f.x + par[L::P_BPROJ + 8 * c + 2 * j];
+          x1[8 * c + 2 * j + 1] += f.y + par[L::P_BPROJ + 8 * c + 2 * j + 1];
+        }
+      }
+      float mu = 0.f;
+#pragma unroll
+      for (int k = 0; k < T; ++k) mu += x1[k];
+      mu *= 1.f / T;
+      float var = 0.f;
+#pragma unroll
+      for (int k = 0; k < T; ++k) var += (x1[k] - mu) * (x1[k] - mu);
+      const float rstd = rsqrtf(var * (1.f / T) + 1e-5f);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (x1[8 * c + j] - mu) * rstd * par[L::P_L2G + 8 * c + j] + par[L::P_L2B + 8 * c + j];
+        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(tid, c, L::RB)) =
+            make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+      }
+    }
+    sync_mma();
+
+    // ---- MLP in 128-wide hidden chunks ----
+    for (int j = 0; j < (4 * T) / 128; ++j) {
+      if (tid == 0) {
+        constexpr uint32_t id = make_idesc_f16(128, 128);
+#pragma unroll
+        for (int k = 0; k < T / 16; ++k)
+          umma_f16(tmem + L::C_HID, make_sdesc(sb + L::A1 + k * 32, L::RB, L::SWZ),
+                   make_sdesc(sb + L::W_0 + j * 128 * L::RB + k * 32, L::RB, L::SWZ), id, k);
+        umma_commit(bar);
+      }
+      wait_mma();
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        float hv[16];
+        tmem_ld16(trow + L::C_HID + c, hv);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) hv[q] = gelu_f(hv[q] + par[L::P_B0 + j * 128 + c + q]);
+        uint8_t* hb = sm + L::PS + (c >> 6) * 16384;
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          *reinterpret_cast<uint4*>(hb + swz_off(tid, ((c & 63) >> 3) + q, 128)) =
+              make_uint4(pack_half2(hv[8 * q], hv[8 * q + 1]), pack_half2(hv[8 * q + 2], hv[8 * q + 3]),
+                         pack_half2(hv[8 * q + 4], hv[8 * q + 5]), pack_half2(hv[8 * q + 6], hv[8 * q + 7]));
+      }
+      sync_mma();
+      if (tid == 0) {
+        constexpr uint32_t id = make_idesc_f16(128, T);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + L::C_MLP2, make_sdesc(sb + L::PS + kb * 16384 + k * 32, 128, SW_128B),
+                     make_sdesc(sb + L::W_2 + (2 * j + kb) * T * 128 + k * 32, 128, SW_128B), id,
+                     (j | kb | k) != 0);
+        umma_commit(bar);
+      }
+      wait_mma();  // the hidden chunk buffer is free again
+    }
+
+    // ---- z = x1 + mlp + b2 -> Z[:, T:2T) ----
+    {
+      float m[T];
+#pragma unroll
+      for (int c = 0; c < T; c += 16) tmem_ld16(trow + L::C_MLP2 + c, m + c);
+      if (pix >= 0) {
+        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          float o[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = x1[8 * c + q] + m[8 * c + q] + par[L::P_B2 + 8 * c + q];
+          dst[c] = make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // TMEM and smem are reused by the next pair
+    tc_fence_after();
+  }
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::TMEM_COLS);
+}
+
+}  // namespace scb

@@ -34,6 +34,18 @@ def test_forward_matches_golden(stem, goldens, oracle, scb, be1, be3):
     check_parity(oracle, stem, g["y"][0], got)
 
 
+def test_forward_unfused_transformer_matches_golden(goldens, oracle, scb, be3):
+    """The separate-launch transformer path (SCB_OPT_FUSE_TRANS = 0) end to end."""
+    _gpu()
+    g = goldens["color_80x64"]
+    be3.set_option(scb.backend.SCB_OPT_FUSE_TRANS, 0)
+    try:
+        got = scb.run(be3, g["x"][0], 3, g["h"], g["w"], be3.weights)
+    finally:
+        be3.set_option(scb.backend.SCB_OPT_FUSE_TRANS, 1)
+    check_parity(oracle, "unfused 80x64", g["y"][0], got)
+
+
 def test_forward_host_batched_uint8(scb, oracle, be3, weights3):
     """uint8 in, the pad/crop fused on the device, two different images in one
     call; each must match the oracle."""

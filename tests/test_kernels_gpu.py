@@ -157,14 +157,17 @@ def test_attention(be3, oracle, n, H, W, t, shift):
 STAGES = ["down1", "down2", "down3", "body", "up3", "up2", "up1"]
 
 
+@pytest.mark.parametrize("fused", [1, 0])
 @pytest.mark.parametrize("stage,index,n,H,W", [
     (0, 0, 1, 16, 16), (0, 1, 2, 16, 24), (1, 1, 1, 16, 16), (2, 0, 1, 8, 16), (3, 1, 1, 8, 8), (3, 0, 1, 16, 16),
-    (4, 1, 1, 16, 16), (6, 3, 1, 24, 16),
+    (4, 1, 1, 16, 16), (6, 3, 1, 24, 16), (5, 0, 3, 8, 24), (0, 1, 1, 72, 64),
 ])
-def test_block(be3, weights3, oracle, stage, index, n, H, W):
+def test_block(be3, weights3, oracle, scb, stage, index, n, H, W, fused):
     """One ConvTransBlock against the oracle at several geometries, W and SW
-    (tests/cuda_ops.rs:130-158)."""
+    (tests/cuda_ops.rs:130-158), through the fused transformer kernel (t = 32/64
+    stages) and through the separate-launch path."""
     torch = _torch()
+    be3.set_option(scb.backend.SCB_OPT_FUSE_TRANS, fused)
     c = 64 << [0, 1, 2, 3, 2, 1, 0][stage]
     rng = np.random.default_rng(stage * 10 + index)
     x = (rng.standard_normal((n, H, W, c)) * 0.5).astype(np.float32)
@@ -175,6 +178,7 @@ def test_block(be3, weights3, oracle, stage, index, n, H, W):
     tx = torch.from_numpy(x).cuda()
     ty = torch.empty_like(tx)
     rc = be3.lib.scb_probe_block(be3.ctx, stage, index, tx.data_ptr(), n, H, W, ty.data_ptr())
+    be3.set_option(scb.backend.SCB_OPT_FUSE_TRANS, 1)
     assert rc == 0, be3.lib.scb_last_error(be3.ctx)
     r = close(f"block {prefix} {n}x{H}x{W}", want, ty.cpu().numpy(), 1e-3)
     print(f"block {prefix}: rel err {r:.2e}")
