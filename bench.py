@@ -237,7 +237,8 @@ def main():
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(dom)
     roofline = {
-        "kernel": f"gemm_tc_kernel [{dom}]" if dom != "attention" else "window_attn_kernel",
+        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans_fused_kernel",
+                   "head": "head_conv_kernel", "tail": "tail_conv_kernel"}.get(dom, f"gemm_tc_kernel [{dom}]"),
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,
         "launches": cls[dom][2], "share_of_forward": cls[dom][1] / tot_ms,

@@ -31,7 +31,8 @@ SYMBOLS = [
     "scb_set_profiling", "scb_profile_read", "scb_set_option",
 ]
 SCB_OPT_FUSE_TRANS = 1
-OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up"]
+OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
+              "trans_fused"]
 
 
 class BackendError(RuntimeError):

@@ -303,7 +303,7 @@ const int kStageLevel[7] = {0, 1, 2, 3, 2, 1, 0};
 // classes (docs/TECH_NOTES.md:346-367).
 enum OpTag : int {
   TAG_HEAD = 0, TAG_TAIL = 1, TAG_CONV1X1 = 2, TAG_CONV3X3 = 3, TAG_QKV = 4, TAG_ATTN = 5, TAG_PROJ = 6,
-  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10
+  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10, TAG_TRANS = 11
 };
 
 struct Op {
@@ -613,7 +613,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     Op tr{};
     tr.kind = Op::TRANS;
     tr.trans_t = t;
-    tr.tag = TAG_ATTN;
+    tr.tag = TAG_TRANS;
     tr.flops = 2.0 * P * (3.0 * t * t + 2.0 * 64 * t + t * t + 8.0 * t * t);
     TransGeom& tg = tr.trans;
     tg.H = H;
