@@ -153,17 +153,18 @@ class B200:
         self.lib.scb_release_scratch(self.ctx)
 
     # -- batched paths ----------------------------------------------------------
-    def forward_host(self, x):
-        """[n][c][h][w] uint8 or float32 host array -> float32 [n][c][h][w] (pad and
-        crop fused on the device)."""
+    def forward_host(self, x, out_u8=False):
+        """[n][c][h][w] uint8 or float32 host array -> [n][c][h][w] float32 (or uint8
+        quantised as the CLI writes PNGs, src/image.rs:60-63); pad and crop fused on
+        the device."""
         x = np.ascontiguousarray(x)
         n, c, h, w = x.shape
         xd = SCB_U8 if x.dtype == np.uint8 else SCB_F32
         if xd == SCB_F32:
             x = x.astype(np.float32, copy=False)
-        y = np.empty((n, c, h, w), np.float32)
-        self._check(self.lib.scb_forward_host(self.ctx, x.ctypes.data, xd, n, c, h, w, y.ctypes.data, SCB_F32),
-                    "scb_forward_host")
+        y = np.empty((n, c, h, w), np.uint8 if out_u8 else np.float32)
+        self._check(self.lib.scb_forward_host(self.ctx, x.ctypes.data, xd, n, c, h, w, y.ctypes.data,
+                                              SCB_U8 if out_u8 else SCB_F32), "scb_forward_host")
         return y
 
     def forward_dev(self, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream=0):

@@ -160,7 +160,7 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     float sum = 0.f;
 #pragma unroll
     for (int kt = 0; kt < 64; ++kt) {
-      const float e = exp2f((s[kt] - mx) * kLog2e);
+      const float e = ex2_approx((s[kt] - mx) * kLog2e);
       s[kt] = e;
       sum += e;
     }

@@ -63,11 +63,14 @@ struct GemmEpi {
   __half* ln_out;
   long ln_ld;
   int ln_lo, ln_n;
+  // Crop-to-NCHW output (the tail conv): columns [0, nchw_c) of pixels inside the
+  // h x w crop of each image go to nchw_out[img][c][y][x], as f32 or as uint8
+  // quantised clamp(v,0,1)*255+0.5 truncated (src/image.rs:60-63).
+  void* nchw_out;
+  int nchw_c, nchw_h, nchw_w, nchw_u8;
 };
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
+__device__ __forceinline__ float gelu_erf(float x) { return gelu_as(x); }
 
 // One 16-column chunk of a row's residual inputs, loaded ahead of use.
 struct ResChunk {
@@ -283,6 +286,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         } else if (e.act == ACT_GELU) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
+        }
+        if (p >= 0 && e.nchw_out != nullptr && c == 0) {
+          const long hw = (long)g.H * g.W;
+          const int img = (int)(p / hw);
+          const int rem = (int)(p - img * hw);
+          const int y = rem / g.W, x = rem - y * g.W;
+          if (y < e.nchw_h && x < e.nchw_w) {
+            for (int co = 0; co < e.nchw_c; ++co) {
+              const long o = (((long)img * e.nchw_c + co) * e.nchw_h + y) * e.nchw_w + x;
+              if (e.nchw_u8)
+                reinterpret_cast<uint8_t*>(e.nchw_out)[o] = (uint8_t)(int)(fminf(fmaxf(v[co], 0.f), 1.f) * 255.f + 0.5f);
+              else
+                reinterpret_cast<float*>(e.nchw_out)[o] = v[co];
+            }
+          }
         }
         if (p >= 0) {
           if (e.res16) {

@@ -1,14 +1,12 @@
-// The two ends of the network, where the channel count is 1 or 3 and tensor cores
-// have nothing to chew on:
+// The input end of the network:
 //
 //   head: uint8 or f32 NCHW image [n][c][h][w] -> replicate pad to [hp][wp]
 //         (src/plan.rs:67-82, fused: the pad is a clamped read) -> m_head 3x3 conv
 //         c -> 64, zero pad 1, no bias (tools/network_scunet.py:191) -> the x1 skip
 //         (fp32 NHWC) and its fp16 shadow (the next GEMM's A operand).
-//   tail: fp16 NHWC (y + x1, already summed by the last up1 block's epilogue) ->
-//         m_tail 3x3 conv 64 -> c -> crop to [h][w] (src/plan.rs:85-94) -> f32 NCHW,
-//         or uint8 with the CLI's quantisation clamp(v,0,1)*255+0.5 truncated
-//         (src/image.rs:60-63).
+//
+// The output end (m_tail 3x3 conv 64 -> c, crop, f32 or uint8 NCHW) is the 3x3
+// implicit GEMM of gemm.cuh with N = 16 and its crop-to-NCHW epilogue.
 #pragma once
 #include "ptx.cuh"
 
@@ -19,117 +17,108 @@ struct HeadGeom {
   int in_u8;  // 1: uint8 input scaled by 1/255; 0: f32 in [0,1]
 };
 
-// One thread per (pixel, 16-channel group): 4 threads per pixel.
-__global__ void __launch_bounds__(256)
-head_conv_kernel(const void* __restrict__ x, const float* __restrict__ wt /*[64][c][3][3]*/,
-                 float* __restrict__ out32, __half* __restrict__ out16, const HeadGeom g) {
-  __shared__ float sw[64 * 27];
-  for (int i = threadIdx.x; i < 64 * g.c * 9; i += blockDim.x) sw[i] = wt[i];
-  __syncthreads();
-  const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long npx = (long)g.n * g.hp * g.wp;
-  if (gid >= npx * 4) return;
-  const long p = gid >> 2;
-  const int grp = (int)(gid & 3);
-  const int img = (int)(p / ((long)g.hp * g.wp));
-  const int rem = (int)(p - (long)img * g.hp * g.wp);
-  const int y = rem / g.wp, xx = rem - y * g.wp;
-  float in[27];
-#pragma unroll
-  for (int ci = 0; ci < 3; ++ci) {
-#pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        const int yy = y + ky - 1, xq = xx + kx - 1;
-        float v = 0.f;
-        if (ci < g.c && yy >= 0 && yy < g.hp && xq >= 0 && xq < g.wp) {
-          const int sy = min(yy, g.h - 1), sx = min(xq, g.w - 1);  // replicate pad
-          const long off = (((long)img * g.c + ci) * g.h + sy) * g.w + sx;
-          v = g.in_u8 ? (float)reinterpret_cast<const uint8_t*>(x)[off] * (1.0f / 255.0f)
-                      : reinterpret_cast<const float*>(x)[off];
-        }
-        in[(ci * 3 + ky) * 3 + kx] = v;
-      }
-    }
-  }
-  float acc[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float* wr = sw + (grp * 16 + j) * g.c * 9;
-    float a = 0.f;
-    for (int k = 0; k < g.c * 9; ++k) a = fmaf(wr[k], in[k], a);  // order ci, ky, kx
-    acc[j] = a;
-  }
-  float4* d32 = reinterpret_cast<float4*>(out32 + p * 64 + grp * 16);
-#pragma unroll
-  for (int h4 = 0; h4 < 4; ++h4) d32[h4] = make_float4(acc[4 * h4], acc[4 * h4 + 1], acc[4 * h4 + 2], acc[4 * h4 + 3]);
-  uint4* d16 = reinterpret_cast<uint4*>(out16 + p * 64 + grp * 16);
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2)
-    d16[h2] = make_uint4(pack_half2(acc[8 * h2], acc[8 * h2 + 1]), pack_half2(acc[8 * h2 + 2], acc[8 * h2 + 3]),
-                         pack_half2(acc[8 * h2 + 4], acc[8 * h2 + 5]), pack_half2(acc[8 * h2 + 6], acc[8 * h2 + 7]));
-}
+// m_head on tcgen05: each 128-pixel tile's im2col rows (27 taps, zero-padded to
+// K = 32, order ci, ky, kx) are built by the threads straight into a 64B-swizzled
+// K-major smem tile, then D[128 x 64] = A . Wh^T is one UMMA chain into TMEM and
+// the epilogue writes x1 (f32) and its fp16 shadow. The replicate pad is the
+// clamped read; the conv's own zero pad is the bounds test.
+constexpr int HEAD_SMEM = 8192 + 4096 + 64 + 1024;
 
-struct TailGeom {
-  int n, c, h, w, hp, wp;
-  int out_u8;
-};
-
-// One thread per output pixel (all c outputs); weights [c][64][3][3] in smem.
 __global__ void __launch_bounds__(128)
-tail_conv_kernel(const __half* __restrict__ yin, const float* __restrict__ wt, void* __restrict__ out,
-                 const TailGeom g) {
-  __shared__ float sw[3 * 64 * 9];
-  for (int i = threadIdx.x; i < g.c * 64 * 9; i += blockDim.x) {
-    // repack [co][ci][ky][kx] -> [co][ky][kx][ci]
-    const int co = i / 576, r = i - co * 576, ci = r / 9, t = r - ci * 9;
-    sw[co * 576 + t * 64 + ci] = wt[i];
+head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][32] K-major*/,
+               float* __restrict__ out32, __half* __restrict__ out16, const HeadGeom g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 12288);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int idx = tid; idx < 64 * 4; idx += 128) {
+    const int r = idx >> 2, j = idx & 3;
+    *reinterpret_cast<uint4*>(sm + 8192 + swz_off(r, j, 64)) = __ldg(reinterpret_cast<const uint4*>(wk + r * 32 + j * 8));
   }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 64);
+  fence_proxy_async_smem();
+  tc_fence_before();
   __syncthreads();
-  const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long npx = (long)g.n * g.h * g.w;
-  if (p >= npx) return;
-  const int img = (int)(p / ((long)g.h * g.w));
-  const int rem = (int)(p - (long)img * g.h * g.w);
-  const int y = rem / g.w, xx = rem - y * g.w;
-  float acc[3] = {0.f, 0.f, 0.f};
-  for (int ky = 0; ky < 3; ++ky) {
-    const int yy = y + ky - 1;
-    if (yy < 0 || yy >= g.hp) continue;
-    for (int kx = 0; kx < 3; ++kx) {
-      const int xq = xx + kx - 1;
-      if (xq < 0 || xq >= g.wp) continue;
-      const uint4* src = reinterpret_cast<const uint4*>(yin + (((long)img * g.hp + yy) * g.wp + xq) * 64);
-      const int t = ky * 3 + kx;
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t sb = smem_u32(sm);
+  uint32_t phase = 0;
+  const long npx = (long)g.n * g.hp * g.wp;
+  const long tiles = (npx + 127) / 128;
+  for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const long p = tile * 128 + tid;
+    float in[32];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint4 u = __ldg(src + q);
-        const __half2* hp = reinterpret_cast<const __half2*>(&u);
+    for (int k = 0; k < 32; ++k) in[k] = 0.f;
+    if (p < npx) {
+      const int img = (int)(p / ((long)g.hp * g.wp));
+      const int rem = (int)(p - (long)img * g.hp * g.wp);
+      const int y = rem / g.wp, xx = rem - y * g.wp;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(hp[j]);
-          const int ci = q * 8 + 2 * j;
+      for (int ci = 0; ci < 3; ++ci) {
+        if (ci < g.c) {
 #pragma unroll
-          for (int co = 0; co < 3; ++co) {
-            if (co < g.c) {
-              acc[co] = fmaf(sw[co * 576 + t * 64 + ci], f.x, acc[co]);
-              acc[co] = fmaf(sw[co * 576 + t * 64 + ci + 1], f.y, acc[co]);
+          for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+              const int yy = y + ky - 1, xq = xx + kx - 1;
+              if (yy >= 0 && yy < g.hp && xq >= 0 && xq < g.wp) {
+                const int sy = min(yy, g.h - 1), sx = min(xq, g.w - 1);
+                const long off = (((long)img * g.c + ci) * g.h + sy) * g.w + sx;
+                in[(ci * 3 + ky) * 3 + kx] = g.in_u8 ? (float)reinterpret_cast<const uint8_t*>(x)[off] * (1.0f / 255.0f)
+                                                     : reinterpret_cast<const float*>(x)[off];
+              }
             }
           }
         }
       }
     }
-  }
-  for (int co = 0; co < g.c; ++co) {
-    const long off = (((long)img * g.c + co) * g.h + y) * g.w + xx;
-    if (g.out_u8) {
-      const float v = fminf(fmaxf(acc[co], 0.f), 1.f) * 255.f + 0.5f;
-      reinterpret_cast<uint8_t*>(out)[off] = (uint8_t)(int)v;
-    } else {
-      reinterpret_cast<float*>(out)[off] = acc[co];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(sm + swz_off(tid, c, 64)) =
+          make_uint4(pack_half2(in[8 * c], in[8 * c + 1]), pack_half2(in[8 * c + 2], in[8 * c + 3]),
+                     pack_half2(in[8 * c + 4], in[8 * c + 5]), pack_half2(in[8 * c + 6], in[8 * c + 7]));
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      constexpr uint32_t id = make_idesc_f16(128, 64);
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        umma_f16(tmem, make_sdesc(sb + k * 32, 64, SW_64B), make_sdesc(sb + 8192 + k * 32, 64, SW_64B), id, k);
+      umma_commit(bar);
     }
+    mbar_wait(bar, phase, SCB_ERR_WAIT_ATTN);
+    phase ^= 1;
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+      float v[16];
+      tmem_ld16(trow + c, v);
+      if (p < npx) {
+        float4* d32 = reinterpret_cast<float4*>(out32 + p * 64 + c);
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4) d32[h4] = make_float4(v[4 * h4], v[4 * h4 + 1], v[4 * h4 + 2], v[4 * h4 + 3]);
+        uint4* d16 = reinterpret_cast<uint4*>(out16 + p * 64 + c);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2)
+          d16[h2] = make_uint4(pack_half2(v[8 * h2], v[8 * h2 + 1]), pack_half2(v[8 * h2 + 2], v[8 * h2 + 3]),
+                               pack_half2(v[8 * h2 + 4], v[8 * h2 + 5]), pack_half2(v[8 * h2 + 6], v[8 * h2 + 7]));
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // the A tile and TMEM are reused by the next tile
+    tc_fence_after();
   }
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
 }  // namespace scb

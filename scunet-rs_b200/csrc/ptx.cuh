@@ -216,6 +216,35 @@ __device__ __forceinline__ uint32_t swz_off(uint32_t row, uint32_t chunk, uint32
   return row * row_bytes + (((chunk ^ phase) & mask) << 4);
 }
 
+// 2^x, hardware approximation (relative error ~2^-22, far below the fp16 rounding
+// every consumer of these values applies).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU with the exact-erf definition (nn.GELU(), tools/network_scunet.py:130),
+// erf evaluated by Abramowitz & Stegun 7.1.26 (|erf error| <= 1.5e-7; the same
+// approximation the reference's CPU backend uses, src/cpu.rs:313-332). Max
+// |GELU error| 2.1e-7 over the real line, below the fp16 rounding of its output.
+__device__ __forceinline__ float gelu_as(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+  const float poly =
+      t * fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f);
+  const float e = ex2_approx(-1.4426950408889634f * z * z);
+  const float erf_abs = fmaf(-poly, e, 1.0f);
+  const float erfv = copysignf(erf_abs, x);
+  return 0.5f * x * (1.0f + erfv);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

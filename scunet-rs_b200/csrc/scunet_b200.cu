@@ -140,6 +140,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_CASE(64, 64, GEO_UP2)
   SCB_GEMM_CASE(128, 64, GEO_UP2)
   SCB_GEMM_CASE(256, 64, GEO_UP2)
+  SCB_GEMM_CASE(16, 64, GEO_CONV3)
   SCB_GEMM_CASE(32, 32, GEO_CONV3)
   SCB_GEMM_CASE(64, 64, GEO_CONV3)
   SCB_GEMM_CASE(128, 64, GEO_CONV3)
@@ -152,7 +153,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
 bool gemm_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{32, 32, GEO_FLAT},   {32, 64, GEO_FLAT},   {64, 64, GEO_FLAT},   {96, 32, GEO_FLAT},
                                {128, 32, GEO_FLAT},  {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
-                               {64, 64, GEO_UP2},    {128, 64, GEO_UP2},   {256, 64, GEO_UP2},   {32, 32, GEO_CONV3},
+                               {64, 64, GEO_UP2},    {128, 64, GEO_UP2},   {256, 64, GEO_UP2},   {32, 32, GEO_CONV3},   {16, 64, GEO_CONV3},
                                {64, 64, GEO_CONV3},  {128, 64, GEO_CONV3}, {256, 64, GEO_CONV3}, {128, 64, GEO_DOWN2},
                                {256, 64, GEO_DOWN2}};
   for (auto& r : tab)
@@ -377,8 +378,8 @@ struct scb_ctx {
   std::vector<BlockW> blocks[7];
   __half* wdown[3] = {};
   __half* wup[3] = {};
-  float* whead = nullptr;
-  float* wtail = nullptr;
+  __half* whead16 = nullptr;  // [64][32]: K = (ci, ky, kx) zero-padded to 32
+  __half* wtail16 = nullptr;  // [16][9*64]: rows >= in_nc zero, K = (ky, kx, ci)
   Arena arena;
   int last_launches = 0;
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
@@ -473,6 +474,8 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* out32, __half* out16, cudaStream_t st);
+
 template <int T>
 cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
   using L = TransLayout<T>;
@@ -496,6 +499,21 @@ cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
   return cudaErrorInvalidConfiguration;
 }
 
+cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* out32, __half* out16, cudaStream_t st) {
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(head_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HEAD_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long tiles = ((long)g.n * g.hp * g.wp + 127) / 128;
+  const int grid = (int)std::max(1L, std::min(tiles, (long)ctx->sms * 6));
+  head_tc_kernel<<<grid, 128, HEAD_SMEM, st>>>(x, ctx->whead16, out32, out16, g);
+  return cudaGetLastError();
+}
+
 // Run the ops of the arena's plan on `st`, with the image pointers of this call.
 int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w, cudaStream_t st) {
   Arena& A = ctx->arena;
@@ -513,16 +531,17 @@ int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int
     switch (op.kind) {
       case Op::HEAD: {
         HeadGeom g{A.n, c, h, w, A.hp, A.wp, x_u8};
-        const long threads = (long)A.n * A.hp * A.wp * 4;
-        head_conv_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, ctx->whead, A.skip[0], A.xs[0], g);
-        e = cudaGetLastError();
+        e = launch_head(ctx, x, g, A.skip[0], A.xs[0], st);
         break;
       }
       case Op::TAIL: {
-        TailGeom g{A.n, c, h, w, A.hp, A.wp, y_u8};
-        const long threads = (long)A.n * h * w;
-        tail_conv_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(A.xs[0], ctx->wtail, y, g);
-        e = cudaGetLastError();
+        GemmOp t = op.gemm;  // the 3x3 implicit GEMM over the (y + x1) shadow, N = 16
+        t.e.nchw_out = y;
+        t.e.nchw_c = c;
+        t.e.nchw_h = h;
+        t.e.nchw_w = w;
+        t.e.nchw_u8 = y_u8;
+        e = launch_gemm(t, ctx->sms, st);
         break;
       }
       case Op::GEMM:
@@ -787,6 +806,10 @@ int build_plan(scb_ctx* ctx) {
   }
   Op tail{};
   tail.kind = Op::TAIL;
+  {
+    Maker mk{&err};
+    if (!mk.conv3(tail.gemm, A.xs[0], n, A.hp, A.wp, 64, 64, ctx->wtail16, 16)) return fail(ctx, SCB_EINVAL, err);
+  }
   tail.tag = TAG_TAIL;
   tail.flops = 2.0 * P0 * 9 * 64 * ctx->in_nc;
   ops.push_back(tail);
@@ -880,19 +903,29 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
     int c;
   };
   std::vector<Pending> pend[7];
-  size_t o_down[3], o_up[3], o_head, o_tail;
+  size_t o_down[3], o_up[3], o_head16, o_tail16;
 
   auto need = [&](const std::string& nm, std::initializer_list<int64_t> sh) -> const float* {
     const float* p = tab.get(nm, sh);
     return p;
   };
-  // m_head / m_tail stay fp32 (SIMT kernels)
+  // m_head / m_tail: fp16 K-major tiles for their tensor-core kernels
   const float* p = need("m_head.0.weight", {dim, in_nc, 3, 3});
   if (!p) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
-  o_head = blob.f32(p, (size_t)dim * in_nc * 9);
   p = need("m_tail.0.weight", {in_nc, dim, 3, 3});
   if (!p) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
-  o_tail = blob.f32(p, (size_t)in_nc * dim * 9);
+  {
+    std::vector<float> t16((size_t)16 * 9 * dim, 0.f);
+    for (int co = 0; co < in_nc; ++co)
+      for (int ci = 0; ci < dim; ++ci)
+        for (int k = 0; k < 9; ++k) t16[((size_t)co * 9 + k) * dim + ci] = p[((size_t)co * dim + ci) * 9 + k];
+    o_tail16 = blob.half(t16);
+    const float* hw = tab.get("m_head.0.weight", {dim, in_nc, 3, 3});
+    std::vector<float> h16((size_t)dim * 32, 0.f);
+    for (int co = 0; co < dim; ++co)
+      for (int k = 0; k < in_nc * 9; ++k) h16[(size_t)co * 32 + k] = hw[(size_t)co * in_nc * 9 + k];
+    o_head16 = blob.half(h16);
+  }
 
   for (int s = 0; s < 7; ++s) {
     const int c = dim << kStageLevel[s], t = c / 2, heads = t / 32;
@@ -996,8 +1029,8 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
   char* b = ctx->wblob;
   auto H16 = [&](size_t o) { return reinterpret_cast<__half*>(b + o); };
   auto F = [&](size_t o) { return reinterpret_cast<float*>(b + o); };
-  ctx->whead = F(o_head);
-  ctx->wtail = F(o_tail);
+  ctx->whead16 = H16(o_head16);
+  ctx->wtail16 = H16(o_tail16);
   for (int s = 0; s < 3; ++s) ctx->wdown[s] = H16(o_down[s]);
   for (int s = 0; s < 3; ++s) ctx->wup[s] = H16(o_up[s]);
   for (int s = 0; s < 7; ++s)

@@ -82,7 +82,7 @@ __device__ __forceinline__ void stage_kmajor(uint8_t* dst, const __half* src, in
   }
 }
 
-__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_f(float x) { return gelu_as(x); }
 
 template <int T>
 __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(const TransGeom g) {
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
       float sum = 0.f;
 #pragma unroll
       for (int kt = 0; kt < 64; ++kt) {
-        const float e = exp2f((s[kt] - mx) * kLog2e);
+        const float e = ex2_approx((s[kt] - mx) * kLog2e);
         s[kt] = e;
         sum += e;
       }

@@ -57,6 +57,26 @@ def test_forward_host_batched_uint8(scb, oracle, be3, weights3):
         check_parity(oracle, f"batched {i}", want[i], y[i])
 
 
+def test_uint8_output_matches_quantised_f32(scb, oracle, be3):
+    """The fused uint8 output path quantises exactly like src/image.rs:60-63."""
+    _gpu()
+    x = scb.synth.noisy_image(9, 3, 100, 72, 15 / 255)[None]
+    y32 = be3.forward_host(x)
+    y8 = be3.forward_host(x, out_u8=True)
+    assert y8.dtype == np.uint8
+    assert np.array_equal(y8.astype(np.int32), oracle.quantise(y32))
+
+
+def test_gray_batched(scb, oracle, be1, weights1):
+    """Grayscale (config 3's model) with a batch of 3 uint8 images."""
+    _gpu()
+    x = np.concatenate([scb.synth.noisy_image(20 + s, 1, 64, 128, 50 / 255)[None] for s in range(3)])
+    y = be1.forward_host(x)
+    want = oracle.forward(x.astype(np.float32) / 255.0, weights1.tensors)
+    for i in range(3):
+        check_parity(oracle, f"gray batched {i}", want[i], y[i])
+
+
 def test_repeats_are_bit_identical(scb, be3):
     _gpu()
     x = scb.synth.noisy_image(5, 3, 256, 192, 25 / 255)[None]
