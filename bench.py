@@ -182,8 +182,13 @@ def main():
     frames = scb.synth.frames(4000 + rank, F, H, W, distinct=min(F, 4))
     x_dev = torch.from_numpy(frames).cuda()
     y_dev = torch.empty((F, C, H, W), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    # An explicit stream: the library's kernels and the timing events must share it
+    # (the legacy default stream's handle is 0, which the C ABI reads as "use the
+    # context's own stream").
+    stream = torch.cuda.Stream()
     sp = stream.cuda_stream
+    assert sp != 0
 
     def step():
         for i in range(0, F, micro):
