@@ -21,7 +21,19 @@
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
 // UMMA issuer (one elected lane), warps 2..5 = epilogue (thread = accumulator row).
 // The grid is persistent; tiles are strided over CTAs and the two TMEM
-// accumulator buffers let tile i's epilogue overlap tile i+1's main loop.
+// accumulator buffers let tile i's epilogue overlap tile i+1's main loop. The
+// pipeline depth (stages) is a runtime value so the host can trade stages for
+// epilogue staging space.
+//
+// Two epilogues:
+//   TMAEPI = true : asynchronous. The epilogue works in 32-column slabs. Residual
+//                   slabs (fp16/fp32/skip) are TMA-loaded into swizzled smem one
+//                   slab ahead (the first before the accumulator wait); outputs are
+//                   written to swizzled smem staging and leave through TMA bulk
+//                   tensor stores, double-buffered. Every global byte moves in full
+//                   lines through the TMA unit.
+//   TMAEPI = false: per-thread vector loads/stores; needed for the LayerNorm
+//                   second pass, the pixel-shuffle (UP2) and crop-to-NCHW stores.
 #pragma once
 #include <cuda.h>
 #include "ptx.cuh"
@@ -41,6 +53,7 @@ struct GemmGeom {
   int H, W, TH, TW, tiles_x, tiles_y;
   // UP2: input width and c_out
   int up_w, up_cout;
+  int stages;       // pipeline depth (runtime)
 };
 
 struct GemmEpi {
@@ -68,6 +81,16 @@ struct GemmEpi {
   // quantised clamp(v,0,1)*255+0.5 truncated (src/image.rs:60-63).
   void* nchw_out;
   int nchw_c, nchw_h, nchw_w, nchw_u8;
+  // TMA epilogue: staging offsets (bytes within one buffer) of each stream's
+  // [128 x 32-column] slab; -1 = stream absent.
+  int st_res16, st_res32, st_skip, st_out16, st_out32;
+  int st_res_bytes, st_out_bytes;  // bytes of one buffer of all residual / output slabs
+};
+
+// Tensor maps of the epilogue streams (TMA epilogue only); box = 32 columns x the
+// M tile's pixel block.
+struct EpiMaps {
+  CUtensorMap res16, res32, skip, out16, out32;
 };
 
 __device__ __forceinline__ float gelu_erf(float x) { return gelu_as(x); }
@@ -97,14 +120,15 @@ __device__ __forceinline__ void load_res(const GemmEpi& e, long p, int oc, ResCh
   }
 }
 
-template <int BN, int BK, int STAGES>
+// smem: [stages x (A tile | B tile)] [barriers, tmem slot: 1 KB] [TMA-epilogue staging]
+template <int BN, int BK>
 struct GemmSmem {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + tmem slot + alignment slack
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  __host__ __device__ static constexpr int bar_off(int stages) { return stages * STAGE_BYTES; }
+  __host__ __device__ static constexpr int staging_off(int stages) { return stages * STAGE_BYTES + 1024; }
 };
 
 // Where accumulator row `r` of M tile `mt` lives: returns the output pixel index
@@ -140,24 +164,78 @@ __device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int 
   }
 }
 
-template <int BN, int BK, int STAGES, int GEO>
+// Spatial origin of M tile `mt`: (img, y0, x0) for CONV3, (y0, x0) for DOWN2.
+template <int GEO>
+__device__ __forceinline__ void tile_origin(const GemmGeom& g, int mt, int& img, int& y0, int& x0) {
+  img = 0;
+  y0 = 0;
+  x0 = 0;
+  if (GEO == GEO_CONV3) {
+    const int per_img = g.tiles_y * g.tiles_x;
+    img = mt / per_img;
+    const int rem = mt - img * per_img;
+    const int ty = rem / g.tiles_x;
+    y0 = ty * g.TH;
+    x0 = (rem - ty * g.tiles_x) * g.TW;
+  } else if (GEO == GEO_DOWN2) {
+    const int ty = mt / g.tiles_x;
+    y0 = ty * g.TH;
+    x0 = (mt - ty * g.tiles_x) * g.TW;
+  }
+}
+
+// TMA load / store of one epilogue slab at column `col` of the tile's pixel block.
+template <int GEO>
+__device__ __forceinline__ void epi_slab_load(void* dst, const CUtensorMap* m, uint64_t* bar, int col, int mt,
+                                              const GemmGeom& g) {
+  int img, y0, x0;
+  tile_origin<GEO>(g, mt, img, y0, x0);
+  if (GEO == GEO_CONV3)
+    tma_load_4d(dst, m, bar, col, x0, y0, img);
+  else if (GEO == GEO_DOWN2)
+    tma_load_3d(dst, m, bar, col, x0, y0);
+  else
+    tma_load_2d(dst, m, bar, col, mt * 128);
+}
+
+template <int GEO>
+__device__ __forceinline__ void epi_slab_store(const CUtensorMap* m, const void* src, int col, int mt,
+                                               const GemmGeom& g) {
+  int img, y0, x0;
+  tile_origin<GEO>(g, mt, img, y0, x0);
+  if (GEO == GEO_CONV3)
+    tma_store_4d(m, src, col, x0, y0, img);
+  else if (GEO == GEO_DOWN2)
+    tma_store_3d(m, src, col, x0, y0);
+  else
+    tma_store_2d(m, src, col, mt * 128);
+}
+
+// Named barrier over the four epilogue warps only.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, int BK, int GEO, bool TMAEPI>
 __global__ void __launch_bounds__(192, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
-               const GemmEpi e) {
-  using L = GemmSmem<BN, BK, STAGES>;
+               const GemmEpi e, const __grid_constant__ EpiMaps em) {
+  using L = GemmSmem<BN, BK>;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(BK == 64 || BK == 32, "BK is one 128B or 64B swizzle row of fp16");
+  static_assert(!TMAEPI || BN % 32 == 0, "TMA epilogue works in 32-column slabs");
   constexpr uint32_t ROWB = BK * 2;
   constexpr uint32_t SWZ = (BK == 64) ? SW_128B : SW_64B;
   constexpr uint32_t IDESC = make_idesc_f16(128, BN);
+  const int STAGES = g.stages;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* res_full = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
+  uint8_t* staging = smem + L::staging_off(STAGES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = g.m_tiles * g.n_tiles;
@@ -170,6 +248,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
+      mbar_init(&res_full[a], 1);
     }
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
@@ -189,19 +268,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
         const int n0 = nt * BN;
-        int img = 0, y0 = 0, x0 = 0;
-        if (GEO == GEO_CONV3) {
-          const int per_img = g.tiles_y * g.tiles_x;
-          img = mt / per_img;
-          const int rem = mt - img * per_img;
-          const int ty = rem / g.tiles_x;
-          y0 = ty * g.TH;
-          x0 = (rem - ty * g.tiles_x) * g.TW;
-        } else if (GEO == GEO_DOWN2) {
-          const int ty = mt / g.tiles_x;
-          y0 = ty * g.TH;
-          x0 = (mt - ty * g.tiles_x) * g.TW;
-        }
+        int img, y0, x0;
+        tile_origin<GEO>(g, mt, img, y0, x0);
         for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
@@ -248,12 +316,123 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         umma_commit(&acc_full[a]);
       }
     }
+  } else if (TMAEPI) {
+    // ---------------- asynchronous (TMA) epilogue: warps 2..5 ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const bool elected = (warp == 2 && lane == 0);
+    const bool has_res = e.st_res16 >= 0 || e.st_res32 >= 0 || e.st_skip >= 0;
+    uint32_t t = 0, rs = 0, os = 0;  // tiles, residual slabs consumed, output slabs stored
+    uint8_t* out_stage = staging + 2 * e.st_res_bytes;
+    auto issue_res = [&](int mt, int col, uint32_t idx) {
+      const uint32_t b = idx & 1;
+      uint8_t* base = staging + b * e.st_res_bytes;
+      mbar_arrive_expect_tx(&res_full[b], e.st_res_bytes);
+      if (e.st_res16 >= 0) epi_slab_load<GEO>(base + e.st_res16, &em.res16, &res_full[b], col, mt, g);
+      if (e.st_res32 >= 0) epi_slab_load<GEO>(base + e.st_res32, &em.res32, &res_full[b], col, mt, g);
+      if (e.st_skip >= 0) epi_slab_load<GEO>(base + e.st_skip, &em.skip, &res_full[b], col, mt, g);
+    };
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
+      const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
+      const int n0 = nt * BN;
+      const uint32_t a = t & 1, aph = (t >> 1) & 1;
+      // slab 0's residuals go out before the accumulator wait (buffer rs & 1 was
+      // released by the last slab's second barrier)
+      if (has_res && elected) issue_res(mt, n0, rs);
+      if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32, ++os) {
+        if (has_res && elected && c + 32 < BN) issue_res(mt, n0 + c + 32, rs + 1);
+        float v[32];
+        tmem_ld16(tbase + c, v);
+        tmem_ld16(tbase + c + 16, v + 16);
+        const int n = n0 + c;
+        if (e.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += __ldg(e.bias + n + j);
+        }
+        if (e.act == ACT_RELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+        } else if (e.act == ACT_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        }
+        float sk[32];
+        if (has_res) {
+          const uint32_t b = rs & 1;
+          mbar_wait(&res_full[b], (rs >> 1) & 1, SCB_ERR_WAIT_ACC);
+          const uint8_t* base = staging + b * e.st_res_bytes;
+          if (e.st_res16 >= 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 u = *reinterpret_cast<const uint4*>(base + e.st_res16 + swz_off(r, j, 64));
+              const __half2* hp = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(hp[i]);
+                v[8 * j + 2 * i] += f.x;
+                v[8 * j + 2 * i + 1] += f.y;
+              }
+            }
+          }
+          if (e.st_res32 >= 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 f = *reinterpret_cast<const float4*>(base + e.st_res32 + swz_off(r, j, 128));
+              v[4 * j] += f.x; v[4 * j + 1] += f.y; v[4 * j + 2] += f.z; v[4 * j + 3] += f.w;
+            }
+          }
+          if (e.st_skip >= 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 f = *reinterpret_cast<const float4*>(base + e.st_skip + swz_off(r, j, 128));
+              sk[4 * j] = f.x; sk[4 * j + 1] = f.y; sk[4 * j + 2] = f.z; sk[4 * j + 3] = f.w;
+            }
+          }
+          ++rs;
+        }
+        // Output staging buffer (os & 1): the store that last used it (two slabs
+        // ago) must have finished reading it before the threads refill it.
+        if (elected) bulk_wait_group_read<1>();
+        epi_bar();
+        uint8_t* ob = out_stage + (os & 1) * e.st_out_bytes;
+        if (e.st_out32 >= 0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(ob + e.st_out32 + swz_off(r, j, 128)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        if (e.st_out16 >= 0) {
+          if (e.st_skip >= 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += sk[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(ob + e.st_out16 + swz_off(r, j, 64)) =
+                make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                           pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+        }
+        fence_proxy_async_smem();
+        epi_bar();  // staging complete; also every thread is done with this slab's residuals
+        if (elected) {
+          if (e.st_out32 >= 0) epi_slab_store<GEO>(&em.out32, ob + e.st_out32, n, mt, g);
+          if (e.st_out16 >= 0) epi_slab_store<GEO>(&em.out16, ob + e.st_out16, n, mt, g);
+          bulk_commit_group();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+    if (elected) bulk_wait_group<0>();
   } else {
-    // ---------------- epilogue: warps 2..5, thread = accumulator row ----------------
+    // ---------------- direct epilogue: warps 2..5, thread = accumulator row ----------------
     // Residual loads are software-pipelined one 16-column chunk ahead, and the
-    // first chunk's loads are issued before waiting for the accumulator, so their
-    // latency hides behind this tile's main loop.
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // first chunk's loads are issued before waiting for the accumulator.
+    const int q = warp & 3;
     const int r = q * 32 + lane;
     uint32_t t = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {

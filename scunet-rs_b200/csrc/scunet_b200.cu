@@ -60,22 +60,26 @@ EncodeTiledFn encode_fn(std::string& err) {
   return fn;
 }
 
+// Encode a tiled tensor map. es = element bytes (2: fp16, 4: fp32); swizzle_bytes
+// = 128, 64 or 0 and must equal box[0] * es when non-zero.
 bool encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
-                const uint32_t* box, int bk, std::string& err) {
+                const uint32_t* box, int es, int swizzle_bytes, std::string& err) {
   EncodeTiledFn fn = encode_fn(err);
   if (!fn) return false;
   cuuint64_t d[5], s[4];
-  cuuint32_t b[5], es[5];
+  cuuint32_t b[5], el[5];
   for (int i = 0; i < rank; ++i) {
     d[i] = dims[i];
     b[i] = box[i];
-    es[i] = 1;
+    el[i] = 1;
     if (i < rank - 1) s[i] = strides[i];
   }
-  const CUtensorMapSwizzle swz = bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), d, s, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = fn(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
+                  const_cast<void*>(base), d, s, b, el, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[256];
     snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d), rank %d, dims %llu x %llu", (int)r, rank,
@@ -87,48 +91,77 @@ bool encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims
 }
 
 // --------------------------------------------------------------------------
-// GEMM op: tiles, maps, dispatch over the compiled (BN, BK, GEO) variants
+// GEMM op: tiles, maps, dispatch over the compiled (BN, BK, GEO, epilogue) variants
 // --------------------------------------------------------------------------
-// Pipeline depth: GEMMs whose two accumulators fit in half of TMEM (BN <= 128) run
-// two CTAs per SM (more epilogue warps to hide load latency) with ~100 KB of
-// stages each; the BN >= 192 variants own the SM's TMEM and take ~192 KB.
-constexpr int ctas_per_sm_for(int bn) { return bn <= 128 ? 2 : 1; }
-constexpr int stages_for(int bn, int bk) {
-  return ((ctas_per_sm_for(bn) == 2 ? 100000 : 196608) / ((128 + bn) * bk * 2)) > 8
-             ? 8
-             : ((ctas_per_sm_for(bn) == 2 ? 100000 : 196608) / ((128 + bn) * bk * 2));
-}
+constexpr int kSmemPerSm = 227 * 1024;
 
 struct GemmOp {
   int geo = GEO_FLAT, bn = 64, bk = 64;
+  bool tma_epi = false;
   CUtensorMap ta, tb;
   GemmGeom g{};
   GemmEpi e{};
+  EpiMaps em;
 };
 
-template <int BN, int BK, int GEO>
+// Pipeline depth and CTAs per SM for one op: GEMMs whose two accumulators fit in
+// half of TMEM (BN <= 128) try for two CTAs per SM (more epilogue warps in
+// flight); stages fill what shared memory is left after the epilogue staging.
+void plan_launch(int bn, int bk, int staging_bytes, int& stages, int& ctas, int& smem) {
+  const int stage_bytes = (128 + bn) * bk * 2;
+  ctas = bn <= 128 ? 2 : 1;
+  for (;;) {
+    const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes;
+    stages = std::min(8, budget / stage_bytes);
+    if (stages >= 2 || ctas == 1) break;
+    ctas = 1;
+  }
+  stages = std::max(stages, 2);
+  smem = stages * stage_bytes + 1024 + staging_bytes + 1024;
+}
+
+template <int BN, int BK, int GEO, bool TMAEPI>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
-  constexpr int S = stages_for(BN, BK);
-  using L = GemmSmem<BN, BK, S>;
-  auto kfn = gemm_tc_kernel<BN, BK, S, GEO>;
+  using L = GemmSmem<BN, BK>;
+  auto kfn = gemm_tc_kernel<BN, BK, GEO, TMAEPI>;
   static bool attr_set[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemPerSm);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int tiles = op.g.m_tiles * op.g.n_tiles;
-  const int grid = std::max(1, std::min(tiles, sms * ctas_per_sm_for(BN)));
-  kfn<<<grid, 192, L::TOTAL, st>>>(op.ta, op.tb, op.g, op.e);
+  const int staging = TMAEPI ? 2 * (op.e.st_res_bytes + op.e.st_out_bytes) : 0;
+  int stages, ctas, smem;
+  plan_launch(BN, BK, staging, stages, ctas, smem);
+  (void)L::STAGE_BYTES;
+  GemmGeom g = op.g;
+  g.stages = stages;
+  const int tiles = g.m_tiles * g.n_tiles;
+  const int grid = std::max(1, std::min(tiles, sms * ctas));
+  kfn<<<grid, 192, smem, st>>>(op.ta, op.tb, g, op.e, op.em);
   return cudaGetLastError();
 }
 
-#define SCB_GEMM_CASE(BN, BK, GEO) \
-  if (op.bn == BN && op.bk == BK && op.geo == GEO) return launch_t<BN, BK, GEO>(op, sms, st);
+#define SCB_GEMM_CASE(BN, BK, GEO)                                                     \
+  if (op.bn == BN && op.bk == BK && op.geo == GEO && !op.tma_epi)                      \
+    return launch_t<BN, BK, GEO, false>(op, sms, st);
+#define SCB_GEMM_TCASE(BN, BK, GEO)                                                    \
+  if (op.bn == BN && op.bk == BK && op.geo == GEO && op.tma_epi)                       \
+    return launch_t<BN, BK, GEO, true>(op, sms, st);
 
 cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
+  SCB_GEMM_TCASE(64, 64, GEO_FLAT)
+  SCB_GEMM_TCASE(128, 64, GEO_FLAT)
+  SCB_GEMM_TCASE(192, 64, GEO_FLAT)
+  SCB_GEMM_TCASE(256, 64, GEO_FLAT)
+  SCB_GEMM_TCASE(32, 32, GEO_CONV3)
+  SCB_GEMM_TCASE(64, 64, GEO_CONV3)
+  SCB_GEMM_TCASE(128, 64, GEO_CONV3)
+  SCB_GEMM_TCASE(256, 64, GEO_CONV3)
+  SCB_GEMM_TCASE(128, 64, GEO_DOWN2)
+  SCB_GEMM_TCASE(256, 64, GEO_DOWN2)
   SCB_GEMM_CASE(32, 32, GEO_FLAT)
   SCB_GEMM_CASE(32, 64, GEO_FLAT)
   SCB_GEMM_CASE(64, 64, GEO_FLAT)
@@ -148,6 +181,15 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_CASE(128, 64, GEO_DOWN2)
   SCB_GEMM_CASE(256, 64, GEO_DOWN2)
   return cudaErrorInvalidConfiguration;
+}
+
+bool tma_epi_supported(int geo, int bn, int bk) {
+  static const int tab[][3] = {{64, 64, GEO_FLAT},   {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
+                               {32, 32, GEO_CONV3},  {64, 64, GEO_CONV3},  {128, 64, GEO_CONV3}, {256, 64, GEO_CONV3},
+                               {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}};
+  for (auto& r : tab)
+    if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
+  return false;
 }
 
 bool gemm_supported(int geo, int bn, int bk) {
@@ -190,7 +232,7 @@ struct Maker {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t str[1] = {(uint64_t)K * 2};
     const uint32_t box[2] = {(uint32_t)op.bk, (uint32_t)op.bn};
-    return encode_map(&op.tb, w, 2, dims, str, box, op.bk, *err);
+    return encode_map(&op.tb, w, 2, dims, str, box, 2, op.bk * 2, *err);
   }
 
   // Plain GEMM over M rows of an fp16 [M][lda] matrix (first K columns).
@@ -206,7 +248,7 @@ struct Maker {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t str[1] = {(uint64_t)lda * 2};
     const uint32_t box[2] = {(uint32_t)op.bk, 128};
-    if (!encode_map(&op.ta, a, 2, dims, str, box, op.bk, *err)) return false;
+    if (!encode_map(&op.ta, a, 2, dims, str, box, 2, op.bk * 2, *err)) return false;
     if (!mapB(op, w, N, K)) return false;
     op.g.M = (int)M;
     op.g.n_total = N;
@@ -232,7 +274,7 @@ struct Maker {
     const uint64_t dims[4] = {(uint64_t)cin, (uint64_t)W, (uint64_t)H, (uint64_t)n};
     const uint64_t str[3] = {(uint64_t)pix_ld * 2, (uint64_t)W * pix_ld * 2, (uint64_t)H * W * pix_ld * 2};
     const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)TH, 1};
-    if (!encode_map(&op.ta, x, 4, dims, str, box, op.bk, *err)) return false;
+    if (!encode_map(&op.ta, x, 4, dims, str, box, 2, op.bk * 2, *err)) return false;
     if (!mapB(op, w, cout, 9 * cin)) return false;
     op.g.M = n * H * W;
     op.g.n_total = cout;
@@ -264,7 +306,7 @@ struct Maker {
     const uint64_t dims[5] = {(uint64_t)cin, 2, (uint64_t)Wo, 2, (uint64_t)rows};
     const uint64_t str[4] = {(uint64_t)cin * 2, (uint64_t)cin * 4, (uint64_t)W * cin * 2, (uint64_t)W * cin * 4};
     const uint32_t box[5] = {(uint32_t)op.bk, 1, (uint32_t)TW, 1, (uint32_t)TH};
-    if (!encode_map(&op.ta, x, 5, dims, str, box, op.bk, *err)) return false;
+    if (!encode_map(&op.ta, x, 5, dims, str, box, 2, op.bk * 2, *err)) return false;
     if (!mapB(op, w, cout, 4 * cin)) return false;
     op.g.M = rows * Wo;
     op.g.n_total = cout;
@@ -278,6 +320,73 @@ struct Maker {
     op.g.tiles_y = (rows + TH - 1) / TH;
     op.g.m_tiles = op.g.tiles_y * op.g.tiles_x;
     op.g.n_tiles = cout / op.bn;
+    return true;
+  }
+
+  // One epilogue stream's map: `cols` columns starting at `base` (element stride
+  // `ld` between pixels), boxed as 32 columns x the M tile's pixel block.
+  bool stream_map(const GemmOp& op, CUtensorMap* m, const void* base, long ld, int cols, int es) {
+    const uint32_t sw = 32 * es;
+    const GemmGeom& g = op.g;
+    if (op.geo == GEO_FLAT) {
+      const uint64_t dims[2] = {(uint64_t)cols, (uint64_t)g.M};
+      const uint64_t str[1] = {(uint64_t)ld * es};
+      const uint32_t box[2] = {32, 128};
+      return encode_map(m, base, 2, dims, str, box, es, sw, *err);
+    } else if (op.geo == GEO_CONV3) {
+      const uint64_t n = (uint64_t)g.M / ((uint64_t)g.H * g.W);
+      const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)g.H, n};
+      const uint64_t str[3] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es, (uint64_t)g.H * g.W * ld * es};
+      const uint32_t box[4] = {32, (uint32_t)g.TW, (uint32_t)g.TH, 1};
+      return encode_map(m, base, 4, dims, str, box, es, sw, *err);
+    } else {  // GEO_DOWN2
+      const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)g.H};
+      const uint64_t str[2] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es};
+      const uint32_t box[3] = {32, (uint32_t)g.TW, (uint32_t)g.TH};
+      return encode_map(m, base, 3, dims, str, box, es, sw, *err);
+    }
+  }
+
+  // After the epilogue pointers are set: pick the TMA epilogue when this op can use
+  // it (no LayerNorm pass, no pixel shuffle, no NCHW crop, a compiled variant) and
+  // build its stream maps and staging layout.
+  bool finish_epi(GemmOp& op) {
+    GemmEpi& e = op.e;
+    e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = -1;
+    e.st_res_bytes = e.st_out_bytes = 0;
+    op.tma_epi = false;
+    if (e.ln_out || e.nchw_out || op.geo == GEO_UP2 || !tma_epi_supported(op.geo, op.bn, op.bk)) return true;
+    const int N = op.g.n_total;
+    int off = 0;
+    if (e.res16) {
+      if (!stream_map(op, &op.em.res16, e.res16, e.res16_ld, N, 2)) return false;
+      e.st_res16 = off;
+      off += 128 * 64;
+    }
+    if (e.res32) {
+      if (!stream_map(op, &op.em.res32, e.res32, e.res32_ld, N, 4)) return false;
+      e.st_res32 = off;
+      off += 128 * 128;
+    }
+    if (e.skip32) {
+      if (!stream_map(op, &op.em.skip, e.skip32, e.skip_ld, N, 4)) return false;
+      e.st_skip = off;
+      off += 128 * 128;
+    }
+    e.st_res_bytes = off;
+    off = 0;
+    if (e.out32) {
+      if (!stream_map(op, &op.em.out32, e.out32, e.out32_ld, N, 4)) return false;
+      e.st_out32 = off;
+      off += 128 * 128;
+    }
+    if (e.out16) {
+      if (!stream_map(op, &op.em.out16, e.out16, e.out16_ld, N, 2)) return false;
+      e.st_out16 = off;
+      off += 128 * 64;
+    }
+    e.st_out_bytes = off;
+    op.tma_epi = true;
     return true;
   }
 
@@ -597,6 +706,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       g.e.ln_lo = cc;
       g.e.ln_n = t;
     }
+    if (!mk.finish_epi(g)) return false;
     op.gemm = g;
     op.tag = TAG_CONV1X1;
     op.flops = 2.0 * P * c * c;
@@ -609,6 +719,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.act = ACT_RELU;
     g.e.out16 = A.hc;
     g.e.out16_ld = cc;
+    if (!mk.finish_epi(g)) return false;
     op.gemm = g;
     op.tag = TAG_CONV3X3;
     op.flops = 2.0 * P * 9 * cc * cc;
@@ -622,6 +733,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.res16_ld = c;
     g.e.out16 = A.z;
     g.e.out16_ld = c;
+    if (!mk.finish_epi(g)) return false;
     op.gemm = g;
     op.tag = TAG_CONV3X3;
     op.flops = 2.0 * P * 9 * cc * cc;
@@ -653,6 +765,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       g.e.bias = bw.bqkv;
       g.e.out16 = A.qh;
       g.e.out16_ld = 3 * t;
+      if (!mk.finish_epi(g)) return false;
       op.gemm = g;
       op.tag = TAG_QKV;
       op.flops = 2.0 * P * t * 3 * t;
@@ -685,6 +798,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       g.e.ln_ld = t;
       g.e.ln_lo = 0;
       g.e.ln_n = t;
+      if (!mk.finish_epi(g)) return false;
       op.gemm = g;
       op.tag = TAG_PROJ;
       op.flops = 2.0 * P * t * t;
@@ -698,6 +812,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       g.e.act = ACT_GELU;
       g.e.out16 = A.qh;
       g.e.out16_ld = 4 * t;
+      if (!mk.finish_epi(g)) return false;
       op.gemm = g;
       op.tag = TAG_MLP0;
       op.flops = 2.0 * P * t * 4 * t;
@@ -712,6 +827,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       g.e.res16_ld = c;
       g.e.out16 = A.z + cc;
       g.e.out16_ld = c;
+      if (!mk.finish_epi(g)) return false;
       op.gemm = g;
       op.tag = TAG_MLP2;
       op.flops = 2.0 * P * t * 4 * t;
@@ -731,6 +847,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     g.e.out16_ld = c;
     g.e.skip32 = skip;
     g.e.skip_ld = c;
+    if (!mk.finish_epi(g)) return false;
     op.gemm = g;
     op.tag = TAG_CONV1X1;
     op.flops = 2.0 * P * c * c;
@@ -769,6 +886,7 @@ int build_plan(scb_ctx* ctx) {
       g.e.out32_ld = c;
       g.e.out16 = A.xs[lvl];
       g.e.out16_ld = c;
+      if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
       op.gemm = g;
       op.tag = TAG_UP;
       op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (2 * c) * (4 * c);
@@ -798,6 +916,7 @@ int build_plan(scb_ctx* ctx) {
       g.e.out32_ld = 2 * c;
       g.e.out16 = A.xs[lvl + 1];
       g.e.out16_ld = 2 * c;
+      if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
       op.gemm = g;
       op.tag = TAG_DOWN;
       op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (4 * c) * (2 * c);
@@ -1183,6 +1302,7 @@ int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16,
   g.e.out16_ld = N;
   g.e.out32 = out32;
   g.e.out32_ld = N;
+  if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
   return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
 }
 
@@ -1199,6 +1319,7 @@ int scb_probe_conv3x3(scb_ctx* ctx, const void* x16, int n, int H, int W, int ci
   g.e.res16_ld = cout;
   g.e.out16 = static_cast<__half*>(out16);
   g.e.out16_ld = cout;
+  if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
   return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
 }
 
@@ -1214,6 +1335,7 @@ int scb_probe_down2(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin,
   g.e.out32_ld = cout;
   g.e.out16 = static_cast<__half*>(out16);
   g.e.out16_ld = cout;
+  if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
   return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
 }
 
@@ -1229,6 +1351,7 @@ int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, c
   g.e.out32_ld = cout;
   g.e.out16 = static_cast<__half*>(out16);
   g.e.out16_ld = cout;
+  if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
   return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
 }
 
