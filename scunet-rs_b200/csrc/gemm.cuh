@@ -40,7 +40,13 @@
 
 namespace scb {
 
-enum Geo : int { GEO_FLAT = 0, GEO_CONV3 = 1, GEO_DOWN2 = 2, GEO_UP2 = 3 };
+enum Geo : int { GEO_FLAT = 0, GEO_CONV3 = 1, GEO_DOWN2 = 2, GEO_UP2 = 3, GEO_CONV3X = 4 };
+
+// GEO_CONV3X: the 3x3 conv with 8-row x 16-column output tiles and one TMA box per
+// column shift kx: the box covers the tile's 10 input rows (halo included), and the
+// three row taps ky are 16-row views into it (UMMA descriptors at +16*ky rows). A
+// tile reads 3 x 160 instead of 9 x 128 input pixel-rows.
+__host__ __device__ constexpr bool is_conv3(int geo) { return geo == GEO_CONV3 || geo == GEO_CONV3X; }
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmGeom {
@@ -121,10 +127,12 @@ __device__ __forceinline__ void load_res(const GemmEpi& e, long p, int oc, ResCh
 }
 
 // smem: [stages x (A tile | B tile)] [barriers, tmem slot: 1 KB] [TMA-epilogue staging]
-template <int BN, int BK>
+template <int BN, int BK, int GEO = GEO_FLAT>
 struct GemmSmem {
-  static constexpr int A_BYTES = 128 * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_ROWS = GEO == GEO_CONV3X ? 160 : 128;  // CONV3X: 10 input rows x 16 columns
+  static constexpr int B_TAPS = GEO == GEO_CONV3X ? 3 : 1;      // CONV3X: the three ky taps of one kx
+  static constexpr int A_BYTES = A_ROWS * BK * 2;
+  static constexpr int B_BYTES = B_TAPS * BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   __host__ __device__ static constexpr int bar_off(int stages) { return stages * STAGE_BYTES; }
@@ -140,7 +148,7 @@ __device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int 
   if (GEO == GEO_FLAT) {
     const long p = (long)mt * 128 + r;
     return p < g.M ? p : -1;
-  } else if (GEO == GEO_CONV3) {
+  } else if (is_conv3(GEO)) {
     const int per_img = g.tiles_y * g.tiles_x;
     const int img = mt / per_img;
     const int rem = mt - img * per_img;
@@ -170,7 +178,7 @@ __device__ __forceinline__ void tile_origin(const GemmGeom& g, int mt, int& img,
   img = 0;
   y0 = 0;
   x0 = 0;
-  if (GEO == GEO_CONV3) {
+  if (is_conv3(GEO)) {
     const int per_img = g.tiles_y * g.tiles_x;
     img = mt / per_img;
     const int rem = mt - img * per_img;
@@ -190,7 +198,7 @@ __device__ __forceinline__ void epi_slab_load(void* dst, const CUtensorMap* m, u
                                               const GemmGeom& g) {
   int img, y0, x0;
   tile_origin<GEO>(g, mt, img, y0, x0);
-  if (GEO == GEO_CONV3)
+  if (is_conv3(GEO))
     tma_load_4d(dst, m, bar, col, x0, y0, img);
   else if (GEO == GEO_DOWN2)
     tma_load_3d(dst, m, bar, col, x0, y0);
@@ -203,7 +211,7 @@ __device__ __forceinline__ void epi_slab_store(const CUtensorMap* m, const void*
                                                const GemmGeom& g) {
   int img, y0, x0;
   tile_origin<GEO>(g, mt, img, y0, x0);
-  if (GEO == GEO_CONV3)
+  if (is_conv3(GEO))
     tma_store_4d(m, src, col, x0, y0, img);
   else if (GEO == GEO_DOWN2)
     tma_store_3d(m, src, col, x0, y0);
@@ -218,7 +226,7 @@ template <int BN, int BK, int GEO, bool TMAEPI>
 __global__ void __launch_bounds__(192, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
                const GemmEpi e, const __grid_constant__ EpiMaps em) {
-  using L = GemmSmem<BN, BK>;
+  using L = GemmSmem<BN, BK, GEO>;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(BK == 64 || BK == 32, "BK is one 128B or 64B swizzle row of fp16");
   static_assert(!TMAEPI || BN % 32 == 0, "TMA epilogue works in 32-column slabs");
@@ -282,11 +290,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
             const int ky = tap / 3, kx = tap - ky * 3;
             tma_load_4d(sa, &tmA, &full[s], ch * BK, x0 + kx - 1, y0 + ky - 1, img);
+          } else if (GEO == GEO_CONV3X) {
+            // k block = (channel chunk, kx): one 10 x 16 box, three weight taps
+            const int kx = kb % 3, ch = kb / 3;
+            tma_load_4d(sa, &tmA, &full[s], ch * BK, x0 + kx - 1, y0 - 1, img);
           } else {  // GEO_DOWN2
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
             tma_load_5d(sa, &tmA, &full[s], ch * BK, tap & 1, x0, tap >> 1, y0);
           }
-          tma_load_2d(sb, &tmB, &full[s], kb * BK, n0);
+          if (GEO == GEO_CONV3X) {
+            const int kx = kb % 3, ch = kb / 3;
+            const int cin = g.kb_per_tap * BK;
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+              tma_load_2d(sb + ky * (BN * BK * 2), &tmB, &full[s], (ky * 3 + kx) * cin + ch * BK, n0);
+          } else {
+            tma_load_2d(sb, &tmB, &full[s], kb * BK, n0);
+          }
         }
       }
     }
@@ -306,10 +326,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
+          if (GEO == GEO_CONV3X) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            umma_f16(d_tmem, make_sdesc(sa + k * 32, ROWB, SWZ), make_sdesc(sb + k * 32, ROWB, SWZ), IDESC,
-                     (kb | k) != 0);
+            for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                umma_f16(d_tmem, make_sdesc(sa + ky * 16 * ROWB + k * 32, ROWB, SWZ),
+                         make_sdesc(sb + ky * (BN * BK * 2) + k * 32, ROWB, SWZ), IDESC, (kb | ky | k) != 0);
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              umma_f16(d_tmem, make_sdesc(sa + k * 32, ROWB, SWZ), make_sdesc(sb + k * 32, ROWB, SWZ), IDESC,
+                       (kb | k) != 0);
+            }
           }
           umma_commit(&empty[s]);
         }

@@ -107,8 +107,8 @@ struct GemmOp {
 // Pipeline depth and CTAs per SM for one op: GEMMs whose two accumulators fit in
 // half of TMEM (BN <= 128) try for two CTAs per SM (more epilogue warps in
 // flight); stages fill what shared memory is left after the epilogue staging.
-void plan_launch(int bn, int bk, int staging_bytes, int& stages, int& ctas, int& smem) {
-  const int stage_bytes = (128 + bn) * bk * 2;
+void plan_launch(int bn, int bk, int geo, int staging_bytes, int& stages, int& ctas, int& smem) {
+  const int stage_bytes = geo == GEO_CONV3X ? (160 + 3 * bn) * bk * 2 : (128 + bn) * bk * 2;
   ctas = bn <= 128 ? 2 : 1;
   for (;;) {
     const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes;
@@ -122,7 +122,7 @@ void plan_launch(int bn, int bk, int staging_bytes, int& stages, int& ctas, int&
 
 template <int BN, int BK, int GEO, bool TMAEPI>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
-  using L = GemmSmem<BN, BK>;
+  using L = GemmSmem<BN, BK, GEO>;
   auto kfn = gemm_tc_kernel<BN, BK, GEO, TMAEPI>;
   static bool attr_set[16] = {false};
   int dev = 0;
@@ -134,7 +134,7 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   }
   const int staging = TMAEPI ? 2 * (op.e.st_res_bytes + op.e.st_out_bytes) : 0;
   int stages, ctas, smem;
-  plan_launch(BN, BK, staging, stages, ctas, smem);
+  plan_launch(BN, BK, GEO, staging, stages, ctas, smem);
   (void)L::STAGE_BYTES;
   GemmGeom g = op.g;
   g.stages = stages;
@@ -156,9 +156,9 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_TCASE(128, 64, GEO_FLAT)
   SCB_GEMM_TCASE(192, 64, GEO_FLAT)
   SCB_GEMM_TCASE(256, 64, GEO_FLAT)
-  SCB_GEMM_TCASE(32, 32, GEO_CONV3)
-  SCB_GEMM_TCASE(64, 64, GEO_CONV3)
-  SCB_GEMM_TCASE(128, 64, GEO_CONV3)
+  SCB_GEMM_TCASE(32, 32, GEO_CONV3X)
+  SCB_GEMM_TCASE(64, 64, GEO_CONV3X)
+  SCB_GEMM_TCASE(128, 64, GEO_CONV3X)
   SCB_GEMM_TCASE(256, 64, GEO_CONV3)
   SCB_GEMM_TCASE(128, 64, GEO_DOWN2)
   SCB_GEMM_TCASE(256, 64, GEO_DOWN2)
@@ -185,7 +185,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
 
 bool tma_epi_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{64, 64, GEO_FLAT},   {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
-                               {32, 32, GEO_CONV3},  {64, 64, GEO_CONV3},  {128, 64, GEO_CONV3}, {256, 64, GEO_CONV3},
+                               {32, 32, GEO_CONV3X}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
                                {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}};
   for (auto& r : tab)
     if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
@@ -261,31 +261,40 @@ struct Maker {
 
   // 3x3 implicit GEMM over n images of H x W, input channels [0, cin) of an fp16
   // NHWC buffer whose pixel stride is pix_ld elements.
-  bool conv3(GemmOp& op, const __half* x, int n, int H, int W, int cin, long pix_ld, const __half* w, int cout) {
-    op.geo = GEO_CONV3;
+  // `kx_boxes`: use the GEO_CONV3X schedule (8 x 16 tiles, one box per column
+  // shift); only compiled with the TMA epilogue, for cout <= 128.
+  bool conv3(GemmOp& op, const __half* x, int n, int H, int W, int cin, long pix_ld, const __half* w, int cout,
+             bool kx_boxes = true) {
     op.bk = (cin % 64 == 0) ? 64 : 32;
     op.bn = cout;
-    if (!gemm_supported(op.geo, op.bn, op.bk) || cin % 32) {
+    op.geo = (kx_boxes && tma_epi_supported(GEO_CONV3X, op.bn, op.bk)) ? GEO_CONV3X : GEO_CONV3;
+    if ((op.geo == GEO_CONV3 && !gemm_supported(op.geo, op.bn, op.bk)) || cin % 32) {
       *err = "no conv3x3 variant for cin=" + std::to_string(cin) + " cout=" + std::to_string(cout);
       return false;
     }
     int TW, TH;
-    pick_tile(W, TW, TH);
+    if (op.geo == GEO_CONV3X) {
+      TW = 16;
+      TH = 8;
+    } else {
+      pick_tile(W, TW, TH);
+    }
+    const int box_rows = op.geo == GEO_CONV3X ? TH + 2 : TH;
     const uint64_t dims[4] = {(uint64_t)cin, (uint64_t)W, (uint64_t)H, (uint64_t)n};
     const uint64_t str[3] = {(uint64_t)pix_ld * 2, (uint64_t)W * pix_ld * 2, (uint64_t)H * W * pix_ld * 2};
-    const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)TH, 1};
+    const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)box_rows, 1};
     if (!encode_map(&op.ta, x, 4, dims, str, box, 2, op.bk * 2, *err)) return false;
     if (!mapB(op, w, cout, 9 * cin)) return false;
     op.g.M = n * H * W;
     op.g.n_total = cout;
     op.g.kb_per_tap = cin / op.bk;
-    op.g.num_kb = 9 * op.g.kb_per_tap;
+    op.g.num_kb = op.geo == GEO_CONV3X ? 3 * op.g.kb_per_tap : 9 * op.g.kb_per_tap;
     op.g.H = H;
     op.g.W = W;
     op.g.TH = TH;
     op.g.TW = TW;
     op.g.tiles_x = (W + TW - 1) / TW;
-    op.g.tiles_y = H / TH;
+    op.g.tiles_y = (H + TH - 1) / TH;
     op.g.m_tiles = n * op.g.tiles_y * op.g.tiles_x;
     op.g.n_tiles = 1;
     return true;
@@ -333,7 +342,7 @@ struct Maker {
       const uint64_t str[1] = {(uint64_t)ld * es};
       const uint32_t box[2] = {32, 128};
       return encode_map(m, base, 2, dims, str, box, es, sw, *err);
-    } else if (op.geo == GEO_CONV3) {
+    } else if (op.geo == GEO_CONV3 || op.geo == GEO_CONV3X) {
       const uint64_t n = (uint64_t)g.M / ((uint64_t)g.H * g.W);
       const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)g.H, n};
       const uint64_t str[3] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es, (uint64_t)g.H * g.W * ld * es};
@@ -927,7 +936,8 @@ int build_plan(scb_ctx* ctx) {
   tail.kind = Op::TAIL;
   {
     Maker mk{&err};
-    if (!mk.conv3(tail.gemm, A.xs[0], n, A.hp, A.wp, 64, 64, ctx->wtail16, 16)) return fail(ctx, SCB_EINVAL, err);
+    if (!mk.conv3(tail.gemm, A.xs[0], n, A.hp, A.wp, 64, 64, ctx->wtail16, 16, false))
+      return fail(ctx, SCB_EINVAL, err);
   }
   tail.tag = TAG_TAIL;
   tail.flops = 2.0 * P0 * 9 * 64 * ctx->in_nc;
