@@ -607,7 +607,7 @@ cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
   }
   const long pairs = (op.trans.n_windows + 1) / 2;
   const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
-  trans_fused_kernel<T><<<grid, 128, L::SMEM, st>>>(op.trans);
+  trans_fused_kernel<T><<<grid, 256, L::SMEM, st>>>(op.trans);
   return cudaGetLastError();
 }
 

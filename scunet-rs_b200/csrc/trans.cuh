@@ -9,7 +9,7 @@
 // WMSA semantics are those of window_attn_kernel (attn.cuh): cyclic shift read in
 // place, rel-pos bias, SW mask on the last window row/column, softmax, P.V.
 //
-// One CTA (128 threads, thread = token row) walks pairs of 8x8 windows (128
+// One CTA (256 threads, two per token row) walks pairs of 8x8 windows (128
 // tokens) persistently. Every GEMM of the block runs on tcgen05 with its
 // accumulator in TMEM and its operands in shared memory:
 //
@@ -61,7 +61,8 @@ struct TransLayout {
   static constexpr int PAR = OS + 128 * RB;              // fp32 parameters
   static constexpr int P_BQKV = 0, P_BPROJ = 3 * T, P_B0 = 4 * T, P_B2 = 8 * T, P_L1G = 9 * T, P_L1B = 10 * T,
                        P_L2G = 11 * T, P_L2B = 12 * T, P_RP = 13 * T, P_N = 13 * T + HEADS * 225;
-  static constexpr int BAR = (PAR + P_N * 4 + 15) & ~15;
+  static constexpr int RED = (PAR + P_N * 4 + 15) & ~15;  // 2 x [2 halves x 128 rows] float2
+  static constexpr int BAR = RED + 2 * 256 * 8;
   static constexpr int SMEM = BAR + 64 + 1024;
   // TMEM columns
   static constexpr int C_QKV = 0, C_O = 3 * T, C_S = 4 * T, C_PROJ = 0, C_MLP2 = T, C_HID = 4 * T;
@@ -85,22 +86,28 @@ __device__ __forceinline__ void stage_kmajor(uint8_t* dst, const __half* src, in
 __device__ __forceinline__ float gelu_f(float x) { return gelu_as(x); }
 
 template <int T>
-__global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(const TransGeom g) {
+__global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(const TransGeom g) {
   using L = TransLayout<T>;
-  constexpr int NCH = T / 8;  // 16-byte chunks per token row
+  // Two threads per token row: warps w and w + 4 share TMEM lane quarter w % 4 and
+  // split every row's columns in halves (hf = 0, 1); row statistics (LayerNorm
+  // moments, softmax max and sum) are combined through `red`.
+  constexpr int HALF = T / 2;           // columns of a T-wide row per thread
+  constexpr int NCH = HALF / 8;         // 16-byte chunks per half row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* par = reinterpret_cast<float*>(sm + L::PAR);
+  float2* red = reinterpret_cast<float2*>(sm + L::RED);  // [2 halves][128 rows]
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row = (warp & 3) * 32 + lane, hf = warp >> 2;
 
   // ---- once per CTA: weights and parameters into shared memory ----
   stage_kmajor(sm + L::W_QKV, g.wqkv, 3 * T, T, T);
   stage_kmajor(sm + L::W_PROJ, g.wproj, T, T, T);
   stage_kmajor(sm + L::W_0, g.w0, 4 * T, T, T);
   stage_kmajor(sm + L::W_2, g.w2, T, 4 * T, 64);
-  for (int i = tid; i < L::P_N; i += 128) {
+  for (int i = tid; i < L::P_N; i += blockDim.x) {
     float v;
     if (i < L::P_BPROJ) v = g.bqkv[i];
     else if (i < L::P_B0) v = g.bproj[i - L::P_BPROJ];
@@ -123,11 +130,11 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   const uint32_t sb = smem_u32(sm);
   uint32_t phase = 0;
 
-  const int slot = tid >> 6, tok = tid & 63;
+  const int slot = row >> 6, tok = row & 63;
   const int qi = tok >> 3, qj = tok & 7;
   const int nwh = g.H >> 3, nww = g.W >> 3;
   const long per_img = (long)nwh * nww;
@@ -160,14 +167,25 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
     phase ^= 1;
     tc_fence_after();
   };
+  // combine a per-half pair of partial sums with the partner thread
+  auto pair_sum = [&](float a, float b) -> float2 {
+    red[hf * 128 + row] = make_float2(a, b);
+    __syncthreads();
+    const float2 o = red[(hf ^ 1) * 128 + row];
+    return make_float2(a + o.x, b + o.y);
+  };
+  auto load_half = [&](long pix, uint4* dst) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * (2 * T) + T + hf * HALF) + c)
+                        : make_uint4(0, 0, 0, 0);
+  };
 
   long pair = blockIdx.x;
   bool lr_n, lc_n;
   long pix_n = locate(pair, lr_n, lc_n);
   uint4 nx[NCH];
-#pragma unroll
-  for (int c = 0; c < NCH; ++c)
-    nx[c] = pix_n >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix_n * (2 * T) + T) + c) : make_uint4(0, 0, 0, 0);
+  load_half(pix_n, nx);
 
   for (; pair < n_pairs; pair += gridDim.x) {
     const long pix = pix_n;
@@ -176,43 +194,44 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
 #pragma unroll
     for (int c = 0; c < NCH; ++c) cur[c] = nx[c];
     pix_n = locate(pair + gridDim.x, lr_n, lc_n);
-#pragma unroll
-    for (int c = 0; c < NCH; ++c)
-      nx[c] = pix_n >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix_n * (2 * T) + T) + c) : make_uint4(0, 0, 0, 0);
+    load_half(pix_n, nx);
 
-    // ---- LN1 -> A1 ----
-    {
-      float x[T];
+    float yt[HALF];  // this thread's half of y_t (the first residual)
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        const __half2* h2 = reinterpret_cast<const __half2*>(&cur[c]);
+    for (int c = 0; c < NCH; ++c) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&cur[c]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(h2[j]);
-          x[8 * c + 2 * j] = f.x;
-          x[8 * c + 2 * j + 1] = f.y;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h2[j]);
+        yt[8 * c + 2 * j] = f.x;
+        yt[8 * c + 2 * j + 1] = f.y;
       }
-      float mu = 0.f;
+    }
+
+    // ---- LN1 -> A1 (this thread's half of the row) ----
+    {
+      float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-      for (int k = 0; k < T; ++k) mu += x[k];
-      mu *= 1.f / T;
-      float var = 0.f;
-#pragma unroll
-      for (int k = 0; k < T; ++k) var += (x[k] - mu) * (x[k] - mu);
-      const float rstd = rsqrtf(var * (1.f / T) + 1e-5f);
+      for (int k = 0; k < HALF; ++k) {
+        s1 += yt[k];
+        s2 += yt[k] * yt[k];
+      }
+      const float2 st = pair_sum(s1, s2);
+      const float mu = st.x * (1.f / T);
+      const float rstd = rsqrtf(fmaxf(st.y * (1.f / T) - mu * mu, 0.f) + 1e-5f);
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         float o[8];
+        const int k0 = hf * HALF + 8 * c;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (x[8 * c + j] - mu) * rstd * par[L::P_L1G + 8 * c + j] + par[L::P_L1B + 8 * c + j];
-        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(tid, c, L::RB)) =
+        for (int j = 0; j < 8; ++j) o[j] = (yt[8 * c + j] - mu) * rstd * par[L::P_L1G + k0 + j] + par[L::P_L1B + k0 + j];
+        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(row, hf * NCH + c, L::RB)) =
             make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
       }
       // the other window's key half of P must read as zero in every P.V product
       uint8_t* pz = sm + L::PS + (slot ^ 1) * 16384;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(pz + swz_off(tid, c, 128)) = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(pz + swz_off(row, hf * 4 + c, 128)) = make_uint4(0, 0, 0, 0);
     }
     sync_mma();
     if (tid == 0) {
@@ -228,32 +247,31 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
     // ---- window attention, head by head ----
     for (int h = 0; h < L::HEADS; ++h) {
       {
-        float q[32], k[32], v[32];
-        tmem_ld16(trow + L::C_QKV + h * 32, q);
-        tmem_ld16(trow + L::C_QKV + h * 32 + 16, q + 16);
-        tmem_ld16(trow + L::C_QKV + T + h * 32, k);
-        tmem_ld16(trow + L::C_QKV + T + h * 32 + 16, k + 16);
-        tmem_ld16(trow + L::C_QKV + 2 * T + h * 32, v);
-        tmem_ld16(trow + L::C_QKV + 2 * T + h * 32 + 16, v + 16);
+        // this thread's 16 of the head's 32 channels of q, k, v
+        float q[16], k[16], v[16];
+        const int c0 = h * 32 + hf * 16;
+        tmem_ld16(trow + L::C_QKV + c0, q);
+        tmem_ld16(trow + L::C_QKV + T + c0, k);
+        tmem_ld16(trow + L::C_QKV + 2 * T + c0, v);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float a[8], b[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            a[j] = q[8 * c + j] + par[L::P_BQKV + h * 32 + 8 * c + j];
-            b[j] = k[8 * c + j] + par[L::P_BQKV + T + h * 32 + 8 * c + j];
+            a[j] = q[8 * c + j] + par[L::P_BQKV + c0 + 8 * c + j];
+            b[j] = k[8 * c + j] + par[L::P_BQKV + T + c0 + 8 * c + j];
           }
-          *reinterpret_cast<uint4*>(sm + L::QS + swz_off(tid, c, 64)) =
+          *reinterpret_cast<uint4*>(sm + L::QS + swz_off(row, 2 * hf + c, 64)) =
               make_uint4(pack_half2(a[0], a[1]), pack_half2(a[2], a[3]), pack_half2(a[4], a[5]), pack_half2(a[6], a[7]));
-          *reinterpret_cast<uint4*>(sm + L::KS + swz_off(tid, c, 64)) =
+          *reinterpret_cast<uint4*>(sm + L::KS + swz_off(row, 2 * hf + c, 64)) =
               make_uint4(pack_half2(b[0], b[1]), pack_half2(b[2], b[3]), pack_half2(b[4], b[5]), pack_half2(b[6], b[7]));
         }
         uint8_t* vb = sm + L::VT + slot * 4096;
-        const uint32_t kk = tid & 63;
+        const uint32_t kk = row & 63;
 #pragma unroll
-        for (int d = 0; d < 32; ++d)
-          *reinterpret_cast<__half*>(vb + swz_off(d, kk >> 3, 128) + (kk & 7) * 2) =
-              __float2half_rn(v[d] + par[L::P_BQKV + 2 * T + h * 32 + d]);
+        for (int d = 0; d < 16; ++d)
+          *reinterpret_cast<__half*>(vb + swz_off(hf * 16 + d, kk >> 3, 128) + (kk & 7) * 2) =
+              __float2half_rn(v[d] + par[L::P_BQKV + 2 * T + c0 + d]);
       }
       sync_mma();
       if (tid == 0) {
@@ -265,36 +283,43 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
         umma_commit(bar);
       }
       wait_mma();
-      float s[64];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(trow + L::C_S + slot * 64 + c * 16, s + c * 16);
+      // this thread's 32 of the row's 64 in-window keys
+      float s[32];
+      tmem_ld16(trow + L::C_S + slot * 64 + hf * 32, s);
+      tmem_ld16(trow + L::C_S + slot * 64 + hf * 32 + 16, s + 16);
       const float* bh = par + L::P_RP + h * 225;
       float mx = -INFINITY;
 #pragma unroll
-      for (int kt = 0; kt < 64; ++kt) {
+      for (int j = 0; j < 32; ++j) {
+        const int kt = hf * 32 + j;
         const int ki = kt >> 3, kj = kt & 7;
-        float v = s[kt] * kScale + bh[(qi - ki + 7) * 15 + (qj - kj + 7)];
+        float v = s[j] * kScale + bh[(qi - ki + 7) * 15 + (qj - kj + 7)];
         const bool masked = (last_row && ((qi < 4) != (ki < 4))) || (last_col && ((qj < 4) != (kj < 4)));
         v = masked ? -INFINITY : v;
-        s[kt] = v;
+        s[j] = v;
         mx = fmaxf(mx, v);
       }
+      red[hf * 128 + row].x = mx;
+      __syncthreads();
+      mx = fmaxf(mx, red[(hf ^ 1) * 128 + row].x);
       float sum = 0.f;
 #pragma unroll
-      for (int kt = 0; kt < 64; ++kt) {
-        const float e = ex2_approx((s[kt] - mx) * kLog2e);
-        s[kt] = e;
+      for (int j = 0; j < 32; ++j) {
+        const float e = ex2_approx((s[j] - mx) * kLog2e);
+        s[j] = e;
         sum += e;
       }
       {
         uint8_t* pr = sm + L::PS + slot * 16384;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(pr + swz_off(tid, c, 128)) =
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(pr + swz_off(row, hf * 4 + c, 128)) =
               make_uint4(pack_half2(s[8 * c], s[8 * c + 1]), pack_half2(s[8 * c + 2], s[8 * c + 3]),
                          pack_half2(s[8 * c + 4], s[8 * c + 5]), pack_half2(s[8 * c + 6], s[8 * c + 7]));
       }
+      red[256 + hf * 128 + row].x = sum;  // second exchange slot: no barrier needed before this write
       sync_mma();
+      sum += red[256 + (hf ^ 1) * 128 + row].x;
       if (tid == 0) {
         constexpr uint32_t id = make_idesc_f16(128, 32);
 #pragma unroll
@@ -307,14 +332,13 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
       }
       wait_mma();
       {
-        float o[32];
-        tmem_ld16(trow + L::C_O + h * 32, o);
-        tmem_ld16(trow + L::C_O + h * 32 + 16, o + 16);
+        float o[16];
+        tmem_ld16(trow + L::C_O + h * 32 + hf * 16, o);
         const float inv = 1.f / sum;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           // head h occupies 16-byte chunks [4h, 4h + 4) of the T-wide O row
-          *reinterpret_cast<uint4*>(sm + L::OS + swz_off(tid, 4 * h + c, L::RB)) =
+          *reinterpret_cast<uint4*>(sm + L::OS + swz_off(row, 4 * h + 2 * hf + c, L::RB)) =
               make_uint4(pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv), pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
                          pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
                          pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
@@ -333,40 +357,33 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
       umma_commit(bar);
     }
     wait_mma();
-    float x1[T];
+    float x1[HALF];
     {
 #pragma unroll
-      for (int c = 0; c < T; c += 16) tmem_ld16(trow + L::C_PROJ + c, x1 + c);
+      for (int c = 0; c < HALF; c += 16) tmem_ld16(trow + L::C_PROJ + hf * HALF + c, x1 + c);
+      float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        const __half2* h2 = reinterpret_cast<const __half2*>(&cur[c]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(h2[j]);
-          x1[8 * c + 2 * j] += f.x + par[L::P_BPROJ + 8 * c + 2 * j];
-          x1[8 * c + 2 * j + 1] += f.y + par[L::P_BPROJ + 8 * c + 2 * j + 1];
-        }
+      for (int k = 0; k < HALF; ++k) {
+        x1[k] += yt[k] + par[L::P_BPROJ + hf * HALF + k];
+        s1 += x1[k];
+        s2 += x1[k] * x1[k];
       }
-      float mu = 0.f;
-#pragma unroll
-      for (int k = 0; k < T; ++k) mu += x1[k];
-      mu *= 1.f / T;
-      float var = 0.f;
-#pragma unroll
-      for (int k = 0; k < T; ++k) var += (x1[k] - mu) * (x1[k] - mu);
-      const float rstd = rsqrtf(var * (1.f / T) + 1e-5f);
+      const float2 st = pair_sum(s1, s2);
+      const float mu = st.x * (1.f / T);
+      const float rstd = rsqrtf(fmaxf(st.y * (1.f / T) - mu * mu, 0.f) + 1e-5f);
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         float o[8];
+        const int k0 = hf * HALF + 8 * c;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (x1[8 * c + j] - mu) * rstd * par[L::P_L2G + 8 * c + j] + par[L::P_L2B + 8 * c + j];
-        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(tid, c, L::RB)) =
+        for (int j = 0; j < 8; ++j) o[j] = (x1[8 * c + j] - mu) * rstd * par[L::P_L2G + k0 + j] + par[L::P_L2B + k0 + j];
+        *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(row, hf * NCH + c, L::RB)) =
             make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
       }
     }
     sync_mma();
 
-    // ---- MLP in 128-wide hidden chunks ----
+    // ---- MLP in 128-wide hidden chunks; thread half hf fills K block hf ----
     for (int j = 0; j < (4 * T) / 128; ++j) {
       if (tid == 0) {
         constexpr uint32_t id = make_idesc_f16(128, 128);
@@ -377,16 +394,16 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
         umma_commit(bar);
       }
       wait_mma();
+      uint8_t* hb = sm + L::PS + hf * 16384;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 16) {
+      for (int c = 0; c < 64; c += 16) {
         float hv[16];
-        tmem_ld16(trow + L::C_HID + c, hv);
+        tmem_ld16(trow + L::C_HID + hf * 64 + c, hv);
 #pragma unroll
-        for (int q = 0; q < 16; ++q) hv[q] = gelu_f(hv[q] + par[L::P_B0 + j * 128 + c + q]);
-        uint8_t* hb = sm + L::PS + (c >> 6) * 16384;
+        for (int q = 0; q < 16; ++q) hv[q] = gelu_f(hv[q] + par[L::P_B0 + j * 128 + hf * 64 + c + q]);
 #pragma unroll
         for (int q = 0; q < 2; ++q)
-          *reinterpret_cast<uint4*>(hb + swz_off(tid, ((c & 63) >> 3) + q, 128)) =
+          *reinterpret_cast<uint4*>(hb + swz_off(row, (c >> 3) + q, 128)) =
               make_uint4(pack_half2(hv[8 * q], hv[8 * q + 1]), pack_half2(hv[8 * q + 2], hv[8 * q + 3]),
                          pack_half2(hv[8 * q + 4], hv[8 * q + 5]), pack_half2(hv[8 * q + 6], hv[8 * q + 7]));
       }
@@ -405,18 +422,18 @@ __global__ void __launch_bounds__(128, TransLayout<T>::CTAS) trans_fused_kernel(
       wait_mma();  // the hidden chunk buffer is free again
     }
 
-    // ---- z = x1 + mlp + b2 -> Z[:, T:2T) ----
+    // ---- z = x1 + mlp + b2 -> Z[:, T:2T) (this thread's half) ----
     {
-      float m[T];
+      float m[HALF];
 #pragma unroll
-      for (int c = 0; c < T; c += 16) tmem_ld16(trow + L::C_MLP2 + c, m + c);
+      for (int c = 0; c < HALF; c += 16) tmem_ld16(trow + L::C_MLP2 + hf * HALF + c, m + c);
       if (pix >= 0) {
-        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
+        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * HALF);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           float o[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) o[q] = x1[8 * c + q] + m[8 * c + q] + par[L::P_B2 + 8 * c + q];
+          for (int q = 0; q < 8; ++q) o[q] = x1[8 * c + q] + m[8 * c + q] + par[L::P_B2 + hf * HALF + 8 * c + q];
           dst[c] = make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
         }
       }
