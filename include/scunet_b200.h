@@ -74,6 +74,25 @@ int scb_forward(scb_ctx* ctx, const float* x_nchw, int c, int hp, int wp, float*
 int scb_forward_dev(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype,
                     void* stream);
 
+/* scb_forward_dev for callers that cannot allocate device memory when they call:
+ * a server that reserves all device memory at start-up and must not have a
+ * request fail or stall on cudaMalloc (which can fail under fragmentation and
+ * synchronises the device), or a host whose own allocator owns the GPU's memory.
+ * This entry point has no counterpart in the reference. It allocates nothing:
+ * its scratch is a 14 MiB array inside the library's device image, which every
+ * GPU that loads the library holds until the process exits. Limit: the padded
+ * batch (n * ceil(h/64)*64 * ceil(w/64)*64) may hold at most 8192 pixels, e.g.
+ * one 64x128 or two 64x64 images; larger requests fail with SCB_EINVAL and a
+ * message. The first call on a context's device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call, from every context on a device, shares the one array and
+ * overwrites it (nothing in it needs to start at zero), so calls whose GPU work
+ * overlaps race: run them on one stream or order them with events. Same inputs,
+ * outputs and asynchrony as scb_forward_dev; the context's weights must already
+ * be on the device (scb_create allocates them). */
+int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y,
+                            int y_dtype, void* stream);
+
 /* Same as scb_forward_dev with host pointers: copies in, runs, copies out,
  * synchronises (the end-to-end call a host application makes). */
 int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype);

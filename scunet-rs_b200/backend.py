@@ -28,7 +28,7 @@ SYMBOLS = [
     "scb_create", "scb_forward", "scb_forward_dev", "scb_forward_host", "scb_need_bytes", "scb_footprint",
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
-    "scb_set_profiling", "scb_profile_read", "scb_set_option",
+    "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
 ]
 SCB_OPT_FUSE_TRANS = 1
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
@@ -63,6 +63,7 @@ def load_library(path=None):
     lib.scb_forward.argtypes = [vp, fp, i, i, i, fp]
     lib.scb_forward_dev.argtypes = [vp, vp, i, i, i, i, i, vp, i, vp]
     lib.scb_forward_host.argtypes = [vp, vp, i, i, i, i, i, vp, i]
+    lib.scb_forward_dev_noalloc.argtypes = [vp, vp, i, i, i, i, i, vp, i, vp]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_footprint.restype = None
@@ -171,6 +172,12 @@ class B200:
         """Device pointers (e.g. torch tensors' data_ptr()); asynchronous."""
         self._check(self.lib.scb_forward_dev(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream or None),
                     "scb_forward_dev")
+
+    def forward_dev_noalloc(self, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype, stream=0):
+        """Like forward_dev, with the library's fixed device scratch instead of an
+        allocation (padded batch of at most 8192 pixels)."""
+        self._check(self.lib.scb_forward_dev_noalloc(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype,
+                                                     stream or None), "scb_forward_dev_noalloc")
 
     def set_option(self, option, value):
         self._check(self.lib.scb_set_option(self.ctx, option, int(value)), "scb_set_option")

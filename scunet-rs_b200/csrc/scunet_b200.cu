@@ -34,6 +34,16 @@
 
 using namespace scb;
 
+// Scratch for scb_forward_dev_noalloc, for callers that cannot allocate device
+// memory at call time. It is a fixed array in the library's device image: every
+// GPU that loads the library holds these 14 MiB until the process exits. Its size
+// covers the scratch plan of any batch whose padded pixels (n * hp * wp) total at
+// most kNoAllocMaxPixels (1704 bytes per padded pixel plus 1 KiB alignment per
+// buffer). Host code only ever takes its address with cudaGetSymbolAddress.
+static constexpr long kNoAllocMaxPixels = 8192;
+static constexpr size_t kNoAllocBytes = 14u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
 namespace {
 
 thread_local std::string g_create_error;
@@ -501,6 +511,10 @@ struct scb_ctx {
   Arena arena;
   int last_launches = 0;
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
+  // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
+  // context's device (looked up on the first call) and the plan laid out in it.
+  void* noalloc_base = nullptr;
+  Arena noalloc;
   // SCUNET_PROFILE equivalent (src/cuda.rs:106-135): events around every launch
   bool profiling = false;
   std::vector<cudaEvent_t> events;
@@ -633,10 +647,11 @@ cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* o
 }
 
 // Run the ops of the arena's plan on `st`, with the image pointers of this call.
-int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w, cudaStream_t st) {
-  Arena& A = ctx->arena;
+int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w,
+            cudaStream_t st, bool allow_profile = true) {
   int launches = 0;
-  if (ctx->profiling) {
+  const bool profiling = ctx->profiling && allow_profile;
+  if (profiling) {
     while (ctx->events.size() < A.ops.size() + 1) {
       cudaEvent_t ev;
       CKC(ctx, cudaEventCreate(&ev), "cudaEventCreate");
@@ -674,10 +689,10 @@ int run_ops(scb_ctx* ctx, const void* x, int x_u8, void* y, int y_u8, int c, int
     }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
     ++launches;
-    if (ctx->profiling) CKC(ctx, cudaEventRecord(ctx->events[launches], st), "cudaEventRecord");
+    if (profiling) CKC(ctx, cudaEventRecord(ctx->events[launches], st), "cudaEventRecord");
   }
   ctx->last_launches = launches;
-  if (ctx->profiling) {
+  if (profiling) {
     ctx->prof_tags.clear();
     ctx->prof_flops.clear();
     for (const Op& op : A.ops) {
@@ -866,8 +881,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   return true;
 }
 
-int build_plan(scb_ctx* ctx) {
-  Arena& A = ctx->arena;
+int build_plan(scb_ctx* ctx, Arena& A) {
   std::string err;
   std::vector<Op>& ops = A.ops;
   ops.clear();
@@ -975,7 +989,7 @@ int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
   A.hp = hp;
   A.wp = wp;
   arena_layout(n, ctx->in_nc, hp, wp, &A);
-  return build_plan(ctx);
+  return build_plan(ctx, A);
 }
 
 int check_device_error(scb_ctx* ctx) {
@@ -1188,7 +1202,52 @@ int scb_forward_dev(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int 
   int r = ensure_arena(ctx, n, hp, wp);
   if (r) return r;
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-  r = run_ops(ctx, x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w, st);
+  r = run_ops(ctx, ctx->arena, x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w, st);
+  if (r) return r;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y,
+                            int y_dtype, void* stream) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
+  if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  if ((long)n * hp * wp > kNoAllocMaxPixels) {
+    char buf[256];
+    snprintf(buf, sizeof buf,
+             "%d image(s) of %dx%d pad to %ld pixels; the no-allocation forward takes at most %ld padded pixels "
+             "(one 64x128 or two 64x64 images) - use scb_forward_dev for larger batches",
+             n, h, w, (long)n * hp * wp, kNoAllocMaxPixels);
+    return fail(ctx, SCB_EINVAL, buf);
+  }
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (!ctx->noalloc_base) {
+    void* base = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
+    if (e != cudaSuccess || !base) return cuda_fail(ctx, e, "cudaGetSymbolAddress(no-allocation scratch)");
+    ctx->noalloc_base = base;
+  }
+  Arena& A = ctx->noalloc;
+  if (!(A.n == n && A.hp == hp && A.wp == wp && !A.ops.empty())) {
+    const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr);
+    if (need > kNoAllocBytes) return fail(ctx, SCB_EINVAL, "no-allocation scratch is too small for this geometry");
+    A = Arena{};
+    A.base = static_cast<char*>(ctx->noalloc_base);
+    A.bytes = kNoAllocBytes;
+    A.n = n;
+    A.hp = hp;
+    A.wp = wp;
+    arena_layout(n, ctx->in_nc, hp, wp, &A);
+    int r = build_plan(ctx, A);
+    if (r) {
+      A.ops.clear();
+      return r;
+    }
+  }
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  int r = run_ops(ctx, A, x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w, st, /*allow_profile=*/false);
   if (r) return r;
   ctx->err.clear();
   return SCB_OK;
@@ -1206,7 +1265,7 @@ int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int
   const size_t in_b = (size_t)n * c * h * w * (x_dtype == SCB_U8 ? 1 : 4);
   const size_t out_b = (size_t)n * c * h * w * (y_dtype == SCB_U8 ? 1 : 4);
   CKC(ctx, cudaMemcpyAsync(A.io_in, x, in_b, cudaMemcpyHostToDevice, ctx->stream), "H2D");
-  r = run_ops(ctx, A.io_in, x_dtype == SCB_U8, A.io_out, y_dtype == SCB_U8, c, h, w, ctx->stream);
+  r = run_ops(ctx, A, A.io_in, x_dtype == SCB_U8, A.io_out, y_dtype == SCB_U8, c, h, w, ctx->stream);
   if (r) return r;
   CKC(ctx, cudaMemcpyAsync(y, A.io_out, out_b, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
   CKC(ctx, cudaStreamSynchronize(ctx->stream), "forward");
@@ -1246,6 +1305,8 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     ctx->fuse_trans = value != 0;
     ctx->arena.ops.clear();
     ctx->arena.n = 0;  // re-plan on the next forward
+    ctx->noalloc.ops.clear();
+    ctx->noalloc.n = 0;
     return SCB_OK;
   }
   return fail(ctx, SCB_EINVAL, "unknown option " + std::to_string(option));
