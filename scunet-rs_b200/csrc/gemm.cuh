@@ -361,19 +361,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (e.st_res32 >= 0) epi_slab_load<GEO>(base + e.st_res32, &em.res32, &res_full[b], col, mt, g);
       if (e.st_skip >= 0) epi_slab_load<GEO>(base + e.st_skip, &em.skip, &res_full[b], col, mt, g);
     };
+    // Residual slabs are requested one slab ahead, across tile boundaries: the last
+    // slab of a tile requests slab 0 of the CTA's next tile, so the first slab of a
+    // tile never waits a full DRAM round trip.
+    if (has_res && elected && (int)blockIdx.x < total_tiles) {
+      const int mt0 = blockIdx.x / g.n_tiles;
+      issue_res(mt0, (blockIdx.x - mt0 * g.n_tiles) * BN, 0);
+    }
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
       const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
       const int n0 = nt * BN;
       const uint32_t a = t & 1, aph = (t >> 1) & 1;
-      // slab 0's residuals go out before the accumulator wait (buffer rs & 1 was
-      // released by the last slab's second barrier)
-      if (has_res && elected) issue_res(mt, n0, rs);
       if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32, ++os) {
-        if (has_res && elected && c + 32 < BN) issue_res(mt, n0 + c + 32, rs + 1);
+        if (has_res && elected) {
+          // buffer (rs + 1) & 1 was released by the previous slab's second barrier
+          if (c + 32 < BN) {
+            issue_res(mt, n0 + c + 32, rs + 1);
+          } else if (tile + (int)gridDim.x < total_tiles) {
+            const int nxt = tile + gridDim.x, mtn = nxt / g.n_tiles;
+            issue_res(mtn, (nxt - mtn * g.n_tiles) * BN, rs + 1);
+          }
+        }
         float v[32];
         tmem_ld16(tbase + c, v);
         tmem_ld16(tbase + c + 16, v + 16);
