@@ -398,8 +398,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
         } else if (e.act == ACT_GELU) {
+          // the GELU output is an fp16 operand: evaluate it in packed half2
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+          for (int j = 0; j < 32; j += 2) {
+            const __half2 gv = gelu_as_h2(__floats2half2_rn(v[j], v[j + 1]));
+            const float2 f = __half22float2(gv);
+            v[j] = f.x;
+            v[j + 1] = f.y;
+          }
         }
         float sk[32];
         if (has_res) {

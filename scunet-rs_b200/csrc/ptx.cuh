@@ -283,6 +283,28 @@ __device__ __forceinline__ float gelu_as(float x) {
   return 0.5f * x * (1.0f + erfv);
 }
 
+// The same GELU on two fp16 values at once (packed half2 arithmetic). Used where
+// the result is stored as fp16 anyway (the MLP hidden): its extra error is of the
+// order of that fp16 rounding (measured through the whole network: max |diff| vs
+// fp32 1.03e-3 instead of 0.96e-3 at 256x256).
+__device__ __forceinline__ __half2 gelu_as_h2(__half2 x) {
+  const __half2 z = __hmul2(__habs2(x), __float2half2_rn(0.70710678118654752f));
+  const __half2 t = h2rcp(__hfma2(__float2half2_rn(0.3275911f), z, __float2half2_rn(1.0f)));
+  __half2 p = __hfma2(__float2half2_rn(1.061405429f), t, __float2half2_rn(-1.453152027f));
+  p = __hfma2(p, t, __float2half2_rn(1.421413741f));
+  p = __hfma2(p, t, __float2half2_rn(-0.284496736f));
+  p = __hfma2(p, t, __float2half2_rn(0.254829592f));
+  p = __hmul2(p, t);
+  const __half2 e = h2exp2(__hmul2(__hmul2(z, z), __float2half2_rn(-1.4426950408889634f)));
+  const __half2 erf_abs = __hfma2(__hneg2(p), e, __float2half2_rn(1.0f));
+  uint32_t ea = *reinterpret_cast<const uint32_t*>(&erf_abs);
+  const uint32_t xs = *reinterpret_cast<const uint32_t*>(&x) & 0x80008000u;
+  ea = (ea & 0x7fff7fffu) | xs;
+  const __half2 erfv = *reinterpret_cast<const __half2*>(&ea);
+  const __half2 half = __float2half2_rn(0.5f);
+  return __hmul2(x, __hfma2(half, erfv, half));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -253,13 +253,23 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
         tmem_ld16(trow + L::C_QKV + c0, q);
         tmem_ld16(trow + L::C_QKV + T + c0, k);
         tmem_ld16(trow + L::C_QKV + 2 * T + c0, v);
+        const float4* bq4 = reinterpret_cast<const float4*>(par + L::P_BQKV + c0);
+        const float4* bk4 = reinterpret_cast<const float4*>(par + L::P_BQKV + T + c0);
+        const float4* bv4 = reinterpret_cast<const float4*>(par + L::P_BQKV + 2 * T + c0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 bq = bq4[j], bk = bk4[j], bv = bv4[j];
+          q[4 * j] += bq.x; q[4 * j + 1] += bq.y; q[4 * j + 2] += bq.z; q[4 * j + 3] += bq.w;
+          k[4 * j] += bk.x; k[4 * j + 1] += bk.y; k[4 * j + 2] += bk.z; k[4 * j + 3] += bk.w;
+          v[4 * j] += bv.x; v[4 * j + 1] += bv.y; v[4 * j + 2] += bv.z; v[4 * j + 3] += bv.w;
+        }
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float a[8], b[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            a[j] = q[8 * c + j] + par[L::P_BQKV + c0 + 8 * c + j];
-            b[j] = k[8 * c + j] + par[L::P_BQKV + T + c0 + 8 * c + j];
+            a[j] = q[8 * c + j];
+            b[j] = k[8 * c + j];
           }
           *reinterpret_cast<uint4*>(sm + L::QS + swz_off(row, 2 * hf + c, 64)) =
               make_uint4(pack_half2(a[0], a[1]), pack_half2(a[2], a[3]), pack_half2(a[4], a[5]), pack_half2(a[6], a[7]));
@@ -270,8 +280,7 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
         const uint32_t kk = row & 63;
 #pragma unroll
         for (int d = 0; d < 16; ++d)
-          *reinterpret_cast<__half*>(vb + swz_off(hf * 16 + d, kk >> 3, 128) + (kk & 7) * 2) =
-              __float2half_rn(v[d] + par[L::P_BQKV + 2 * T + c0 + d]);
+          *reinterpret_cast<__half*>(vb + swz_off(hf * 16 + d, kk >> 3, 128) + (kk & 7) * 2) = __float2half_rn(v[d]);
       }
       sync_mma();
       if (tid == 0) {
@@ -399,13 +408,22 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
       for (int c = 0; c < 64; c += 16) {
         float hv[16];
         tmem_ld16(trow + L::C_HID + hf * 64 + c, hv);
+        const float4* b4 = reinterpret_cast<const float4*>(par + L::P_B0 + j * 128 + hf * 64 + c);
+        uint32_t pk[8];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) hv[q] = gelu_f(hv[q] + par[L::P_B0 + j * 128 + hf * 64 + c + q]);
+        for (int q = 0; q < 4; ++q) {
+          const float4 b = b4[q];
+          __half2 a0 = __floats2half2_rn(hv[4 * q] + b.x, hv[4 * q + 1] + b.y);
+          __half2 a1 = __floats2half2_rn(hv[4 * q + 2] + b.z, hv[4 * q + 3] + b.w);
+          a0 = gelu_as_h2(a0);
+          a1 = gelu_as_h2(a1);
+          pk[2 * q] = *reinterpret_cast<uint32_t*>(&a0);
+          pk[2 * q + 1] = *reinterpret_cast<uint32_t*>(&a1);
+        }
 #pragma unroll
         for (int q = 0; q < 2; ++q)
           *reinterpret_cast<uint4*>(hb + swz_off(row, (c >> 3) + q, 128)) =
-              make_uint4(pack_half2(hv[8 * q], hv[8 * q + 1]), pack_half2(hv[8 * q + 2], hv[8 * q + 3]),
-                         pack_half2(hv[8 * q + 4], hv[8 * q + 5]), pack_half2(hv[8 * q + 6], hv[8 * q + 7]));
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
       sync_mma();
       if (tid == 0) {
