@@ -387,8 +387,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
         float v[32];
-        tmem_ld16(tbase + c, v);
-        tmem_ld16(tbase + c + 16, v + 16);
+        tmem_ld16x2(tbase + c, v, tbase + c + 16, v + 16);
         const int n = n0 + c;
         if (e.bias) {
 #pragma unroll

@@ -204,18 +204,63 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // 32 lanes x 32 bit, 16 consecutive columns: thread t of the warp gets row
-// (lane base + t), columns [col, col + 16).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// (lane base + t), columns [col, col + 16). The _issue form only starts the load:
+// several loads can be in flight before one tmem_wait_ld(); tmem_fence16 then ties
+// the registers to the wait so no use is scheduled above it.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_fence16(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+__device__ __forceinline__ void u32_to_f32_16(const uint32_t* r, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One 16-column load, waited for immediately.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  tmem_ld16_issue(taddr, r);
+  tmem_wait_ld();
+  tmem_fence16(r);
+  u32_to_f32_16(r, v);
+}
+
+// Two / three / four 16-column loads in flight, one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t a0, float* v0, uint32_t a1, float* v1) {
+  uint32_t r0[16], r1[16];
+  tmem_ld16_issue(a0, r0);
+  tmem_ld16_issue(a1, r1);
+  tmem_wait_ld();
+  tmem_fence16(r0);
+  tmem_fence16(r1);
+  u32_to_f32_16(r0, v0);
+  u32_to_f32_16(r1, v1);
+}
+
+__device__ __forceinline__ void tmem_ld16x3(uint32_t a0, float* v0, uint32_t a1, float* v1, uint32_t a2, float* v2) {
+  uint32_t r0[16], r1[16], r2[16];
+  tmem_ld16_issue(a0, r0);
+  tmem_ld16_issue(a1, r1);
+  tmem_ld16_issue(a2, r2);
+  tmem_wait_ld();
+  tmem_fence16(r0);
+  tmem_fence16(r1);
+  tmem_fence16(r2);
+  u32_to_f32_16(r0, v0);
+  u32_to_f32_16(r1, v1);
+  u32_to_f32_16(r2, v2);
 }
 
 // ---------------------------------------------------------------------------

@@ -250,9 +250,7 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
         // this thread's 16 of the head's 32 channels of q, k, v
         float q[16], k[16], v[16];
         const int c0 = h * 32 + hf * 16;
-        tmem_ld16(trow + L::C_QKV + c0, q);
-        tmem_ld16(trow + L::C_QKV + T + c0, k);
-        tmem_ld16(trow + L::C_QKV + 2 * T + c0, v);
+        tmem_ld16x3(trow + L::C_QKV + c0, q, trow + L::C_QKV + T + c0, k, trow + L::C_QKV + 2 * T + c0, v);
         const float4* bq4 = reinterpret_cast<const float4*>(par + L::P_BQKV + c0);
         const float4* bk4 = reinterpret_cast<const float4*>(par + L::P_BQKV + T + c0);
         const float4* bv4 = reinterpret_cast<const float4*>(par + L::P_BQKV + 2 * T + c0);
@@ -294,8 +292,7 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
       wait_mma();
       // this thread's 32 of the row's 64 in-window keys
       float s[32];
-      tmem_ld16(trow + L::C_S + slot * 64 + hf * 32, s);
-      tmem_ld16(trow + L::C_S + slot * 64 + hf * 32 + 16, s + 16);
+      tmem_ld16x2(trow + L::C_S + slot * 64 + hf * 32, s, trow + L::C_S + slot * 64 + hf * 32 + 16, s + 16);
       const float* bh = par + L::P_RP + h * 225;
       float mx = -INFINITY;
 #pragma unroll
@@ -368,8 +365,10 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
     wait_mma();
     float x1[HALF];
     {
-#pragma unroll
-      for (int c = 0; c < HALF; c += 16) tmem_ld16(trow + L::C_PROJ + hf * HALF + c, x1 + c);
+      if (HALF == 32)
+        tmem_ld16x2(trow + L::C_PROJ + hf * HALF, x1, trow + L::C_PROJ + hf * HALF + 16, x1 + 16);
+      else
+        tmem_ld16(trow + L::C_PROJ + hf * HALF, x1);
       float s1 = 0.f, s2 = 0.f;
 #pragma unroll
       for (int k = 0; k < HALF; ++k) {
@@ -405,13 +404,13 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
       wait_mma();
       uint8_t* hb = sm + L::PS + hf * 16384;
 #pragma unroll 1
-      for (int c = 0; c < 64; c += 16) {
-        float hv[16];
-        tmem_ld16(trow + L::C_HID + hf * 64 + c, hv);
+      for (int c = 0; c < 64; c += 32) {
+        float hv[32];
+        tmem_ld16x2(trow + L::C_HID + hf * 64 + c, hv, trow + L::C_HID + hf * 64 + c + 16, hv + 16);
         const float4* b4 = reinterpret_cast<const float4*>(par + L::P_B0 + j * 128 + hf * 64 + c);
-        uint32_t pk[8];
+        uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
           const float4 b = b4[q];
           __half2 a0 = __floats2half2_rn(hv[4 * q] + b.x, hv[4 * q + 1] + b.y);
           __half2 a1 = __floats2half2_rn(hv[4 * q + 2] + b.z, hv[4 * q + 3] + b.w);
@@ -421,7 +420,7 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
           pk[2 * q + 1] = *reinterpret_cast<uint32_t*>(&a1);
         }
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < 4; ++q)
           *reinterpret_cast<uint4*>(hb + swz_off(row, (c >> 3) + q, 128)) =
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
@@ -443,8 +442,10 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
     // ---- z = x1 + mlp + b2 -> Z[:, T:2T) (this thread's half) ----
     {
       float m[HALF];
-#pragma unroll
-      for (int c = 0; c < HALF; c += 16) tmem_ld16(trow + L::C_MLP2 + hf * HALF + c, m + c);
+      if (HALF == 32)
+        tmem_ld16x2(trow + L::C_MLP2 + hf * HALF, m, trow + L::C_MLP2 + hf * HALF + 16, m + 16);
+      else
+        tmem_ld16(trow + L::C_MLP2 + hf * HALF, m);
       if (pix >= 0) {
         uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * HALF);
 #pragma unroll
