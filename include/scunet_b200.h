@@ -97,6 +97,33 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
  * synchronises (the end-to-end call a host application makes). */
 int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype);
 
+/* ---- one large image split into row bands ----
+ * The padded image's 64-row blocks are divided into contiguous row bands. Each band
+ * runs the whole network on its rows, stored with 4 halo rows above and below at
+ * every level; after every block's conv1_1 (and before the tail conv) the bands
+ * swap their 4 boundary rows, which covers the 3x3 conv pair and the shifted
+ * windows that straddle band edges. The shifted-window mask uses the window's row
+ * in the whole image, so the image's top and bottom bands need no wrap-around
+ * exchange. 2x2 down/up convs never cross a 64-aligned band edge. Output equals
+ * scb_forward_dev's on the same image (the same ops on the same pixels). */
+
+/* All `nbands` bands of one image on this context's GPU, run in lockstep with
+ * device-to-device halo copies (validates the banded schedule on one GPU).
+ * x, y: device [1][c][h][w]. Asynchronous on `stream`. */
+int scb_forward_bands(scb_ctx* ctx, int nbands, const void* x, int x_dtype, int c, int h, int w, void* y,
+                      int y_dtype, void* stream);
+
+/* Multi-GPU bands, one process and context per GPU: rank 0 creates a 128-byte
+ * NCCL unique id, every rank passes it to scb_band_init (collective), then every
+ * rank calls scb_forward_band with the FULL image x (device, on its own GPU); it
+ * computes its band and writes that band's rows of y (device [1][c][h][w] on its
+ * own GPU). Halo rows travel with NCCL send/recv over NVLink on the compute
+ * stream. scb_band_init with nranks = 1 runs the whole image as one band. */
+int scb_band_unique_id(void* id_out);
+int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks);
+int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int w, void* y, int y_dtype,
+                     void* stream);
+
 /* Device bytes a forward of n images of hp x wp needs beyond the weights
  * (`memguard::device_need`, src/memguard.rs:66-74). Pure arithmetic. */
 int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes);

@@ -12,7 +12,8 @@ Modules:
   synth    - seeded synthetic inputs for the benchmark configurations
   build    - nvcc build of the library
 """
-from . import plan, weights, synth, build  # noqa: F401
-from .backend import B200, BackendError, run, load_library, need_bytes, SYMBOLS, SCB_F32, SCB_U8  # noqa: F401
+from . import plan, weights, synth, build, shard  # noqa: F401
+from .backend import (B200, BackendError, run, load_library, need_bytes, band_unique_id, SYMBOLS, SCB_F32,  # noqa: F401
+                      SCB_U8)
 from .plan import Plan  # noqa: F401
 from .weights import Weights  # noqa: F401

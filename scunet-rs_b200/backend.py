@@ -29,6 +29,7 @@ SYMBOLS = [
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
+    "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band",
 ]
 SCB_OPT_FUSE_TRANS = 1
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
@@ -64,6 +65,10 @@ def load_library(path=None):
     lib.scb_forward_dev.argtypes = [vp, vp, i, i, i, i, i, vp, i, vp]
     lib.scb_forward_host.argtypes = [vp, vp, i, i, i, i, i, vp, i]
     lib.scb_forward_dev_noalloc.argtypes = [vp, vp, i, i, i, i, i, vp, i, vp]
+    lib.scb_forward_bands.argtypes = [vp, i, vp, i, i, i, i, vp, i, vp]
+    lib.scb_band_unique_id.argtypes = [vp]
+    lib.scb_band_init.argtypes = [vp, vp, i, i]
+    lib.scb_forward_band.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_footprint.restype = None
@@ -87,6 +92,15 @@ def load_library(path=None):
     if path is None:
         _lib = lib
     return lib
+
+
+def band_unique_id():
+    """A fresh 128-byte NCCL unique id for scb_band_init (rank 0 makes it)."""
+    lib = load_library()
+    buf = ctypes.create_string_buffer(128)
+    if lib.scb_band_unique_id(buf) != 0:
+        raise BackendError(f"scb_band_unique_id: {lib.scb_last_error(None).decode()}")
+    return buf.raw
 
 
 def need_bytes(n, in_nc, hp, wp):
@@ -178,6 +192,22 @@ class B200:
         allocation (padded batch of at most 8192 pixels)."""
         self._check(self.lib.scb_forward_dev_noalloc(self.ctx, x_ptr, x_dtype, n, c, h, w, y_ptr, y_dtype,
                                                      stream or None), "scb_forward_dev_noalloc")
+
+    # -- one large image in row bands (config 5) ---------------------------------
+    def forward_bands(self, nbands, x_ptr, x_dtype, c, h, w, y_ptr, y_dtype, stream=0):
+        """All bands on this GPU in lockstep (device pointers, one image)."""
+        self._check(self.lib.scb_forward_bands(self.ctx, nbands, x_ptr, x_dtype, c, h, w, y_ptr, y_dtype,
+                                               stream or None), "scb_forward_bands")
+
+    def band_init(self, uid, rank, nranks):
+        """Join a band group (collective over the ranks); `uid` from band_unique_id()."""
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        self._check(self.lib.scb_band_init(self.ctx, buf, rank, nranks), "scb_band_init")
+
+    def forward_band(self, x_ptr, x_dtype, c, h, w, y_ptr, y_dtype, stream=0):
+        """This rank's band of the full image x; writes its rows of y."""
+        self._check(self.lib.scb_forward_band(self.ctx, x_ptr, x_dtype, c, h, w, y_ptr, y_dtype, stream or None),
+                    "scb_forward_band")
 
     def set_option(self, option, value):
         self._check(self.lib.scb_set_option(self.ctx, option, int(value)), "scb_set_option")

@@ -27,11 +27,9 @@
 namespace scb {
 
 struct AttnGeom {
-  int nimg, H, W;  // plane per image
+  WinGeom win;
   int t;           // channels of the trans half (heads * 32)
   int heads;
-  int shift;       // 0 (W) or 4 (SW)
-  long n_windows;  // nimg * (H/8) * (W/8)
   long qkv_ld;     // elements per pixel row of qkv (3t)
   long out_ld;     // elements per pixel row of out
 };
@@ -56,22 +54,11 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
   const int tid = threadIdx.x, warp = tid >> 5;
   const int slot = tid >> 6, tok = tid & 63;
   const long win = 2L * blockIdx.x + slot;
-  const bool valid = win < g.n_windows;
-  const int nwh = g.H >> 3, nww = g.W >> 3;
+  const bool valid = win < g.win.n_windows;
   const int qi = tok >> 3, qj = tok & 7;
   long pix = 0;
-  bool last_row = false, last_col = false;
-  if (valid) {
-    const long per_img = (long)nwh * nww;
-    const long img = win / per_img;
-    const int wrem = (int)(win - img * per_img);
-    const int wh = wrem / nww, ww = wrem - wh * nww;
-    const int y = (wh * 8 + qi + g.shift) % g.H;
-    const int x = (ww * 8 + qj + g.shift) % g.W;
-    pix = (img * g.H + y) * g.W + x;
-    last_row = g.shift && wh == nwh - 1;
-    last_col = g.shift && ww == nww - 1;
-  }
+  bool last_row = false, last_col = false, store = false;
+  if (valid) pix = win_token_pixel(g.win, win, qi, qj, last_row, last_col, store);
 
   for (int i = tid; i < g.heads * 225; i += 128) bias[i] = rp[i];
   if (tid == 0) {
@@ -193,7 +180,7 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     tmem_ld16(trow, o);
     tmem_ld16(trow + 16, o + 16);
     const float inv = 1.f / sum;
-    if (valid) {
+    if (valid && store) {
       uint4* dst = reinterpret_cast<uint4*>(out + pix * g.out_ld + h * 32);
 #pragma unroll
       for (int c = 0; c < 4; ++c)

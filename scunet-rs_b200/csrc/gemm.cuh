@@ -55,8 +55,11 @@ struct GemmGeom {
   int num_kb;       // K / BK
   int kb_per_tap;   // CONV3/DOWN2: channel chunks per tap
   int m_tiles, n_tiles;
-  // CONV3: per-image plane H x W; DOWN2: stacked output rows H (= n*Ho) x W (= Wo)
+  // CONV3: per-image stored plane H x W, output rows [row0, row0 + rows_out) of it
+  // (the whole plane, or a row band between halo rows); DOWN2: stacked output rows
+  // H (= n*Ho) x W (= Wo)
   int H, W, TH, TW, tiles_x, tiles_y;
+  int row0, rows_out;
   // UP2: input width and c_out
   int up_w, up_cout;
   int stages;       // pipeline depth (runtime)
@@ -87,6 +90,7 @@ struct GemmEpi {
   // quantised clamp(v,0,1)*255+0.5 truncated (src/image.rs:60-63).
   void* nchw_out;
   int nchw_c, nchw_h, nchw_w, nchw_u8;
+  int nchw_row_off;  // image row of stored row y is y + nchw_row_off
   // TMA epilogue: staging offsets (bytes within one buffer) of each stream's
   // [128 x 32-column] slab; -1 = stream absent.
   int st_res16, st_res32, st_skip, st_out16, st_out32;
@@ -153,8 +157,8 @@ __device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int 
     const int img = mt / per_img;
     const int rem = mt - img * per_img;
     const int ty = rem / g.tiles_x, tx = rem - ty * g.tiles_x;
-    const int y = ty * g.TH + r / g.TW, x = tx * g.TW + r % g.TW;
-    if (x >= g.W || y >= g.H) return -1;
+    const int y = g.row0 + ty * g.TH + r / g.TW, x = tx * g.TW + r % g.TW;
+    if (x >= g.W || y >= g.row0 + g.rows_out) return -1;
     return ((long)img * g.H + y) * g.W + x;
   } else if (GEO == GEO_DOWN2) {
     const int ty = mt / g.tiles_x, tx = mt - ty * g.tiles_x;
@@ -183,7 +187,7 @@ __device__ __forceinline__ void tile_origin(const GemmGeom& g, int mt, int& img,
     img = mt / per_img;
     const int rem = mt - img * per_img;
     const int ty = rem / g.tiles_x;
-    y0 = ty * g.TH;
+    y0 = g.row0 + ty * g.TH;
     x0 = (rem - ty * g.tiles_x) * g.TW;
   } else if (GEO == GEO_DOWN2) {
     const int ty = mt / g.tiles_x;
@@ -516,8 +520,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const long hw = (long)g.H * g.W;
           const int img = (int)(p / hw);
           const int rem = (int)(p - img * hw);
-          const int y = rem / g.W, x = rem - y * g.W;
-          if (y < e.nchw_h && x < e.nchw_w) {
+          const int x = rem % g.W;
+          const int y = rem / g.W + e.nchw_row_off;
+          if (y >= 0 && y < e.nchw_h && x < e.nchw_w) {
             for (int co = 0; co < e.nchw_c; ++co) {
               const long o = (((long)img * e.nchw_c + co) * e.nchw_h + y) * e.nchw_w + x;
               if (e.nchw_u8)

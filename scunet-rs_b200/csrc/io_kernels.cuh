@@ -15,6 +15,8 @@ namespace scb {
 struct HeadGeom {
   int n, c, h, w, hp, wp;
   int in_u8;  // 1: uint8 input scaled by 1/255; 0: f32 in [0,1]
+  int row0;   // image row of output row 0 (a row band starts below 0)
+  int rows;   // output rows per image (hp for the whole image)
 };
 
 // m_head on tcgen05: each 128-pixel tile's im2col rows (27 taps, zero-padded to
@@ -49,7 +51,7 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
   const uint32_t sb = smem_u32(sm);
   uint32_t phase = 0;
-  const long npx = (long)g.n * g.hp * g.wp;
+  const long npx = (long)g.n * g.rows * g.wp;
   const long tiles = (npx + 127) / 128;
   for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const long p = tile * 128 + tid;
@@ -57,9 +59,9 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
 #pragma unroll
     for (int k = 0; k < 32; ++k) in[k] = 0.f;
     if (p < npx) {
-      const int img = (int)(p / ((long)g.hp * g.wp));
-      const int rem = (int)(p - (long)img * g.hp * g.wp);
-      const int y = rem / g.wp, xx = rem - y * g.wp;
+      const int img = (int)(p / ((long)g.rows * g.wp));
+      const int rem = (int)(p - (long)img * g.rows * g.wp);
+      const int y = g.row0 + rem / g.wp, xx = rem % g.wp;
 #pragma unroll
       for (int ci = 0; ci < 3; ++ci) {
         if (ci < g.c) {

@@ -350,6 +350,39 @@ __device__ __forceinline__ __half2 gelu_as_h2(__half2 x) {
   return __hmul2(x, __hfma2(half, erfv, half));
 }
 
+// Where the tokens of 8x8 (shifted) windows live in a stored plane. Token (i, j)
+// of window (wr, wc) is pixel (row, (8 wc + j + shift) mod W) with
+//   wrap = 1 (the whole image): row = (8 wr + i + shift) mod H - the cyclic roll
+//            of tools/network_scunet.py:77, read in place;
+//   wrap = 0 (a row band stored with halo rows): row = row_base + 8 wr + i; the
+//            band's first and last shifted window rows reach into the halo rows.
+// The SW mask needs the window's row in the WHOLE image (gwr0 + wr) mod nwr_global:
+// only the image's last window row/column is masked (cuda/scunet.cu:137-147).
+struct WinGeom {
+  int H, W;                 // stored rows and columns per image
+  int shift;                // 0 (W) or 4 (SW)
+  int nwr, nwc;             // window rows handled per image, window columns
+  long n_windows;           // images * nwr * nwc
+  int wrap, row_base;
+  int gwr0, nwr_global;
+  int store_lo, store_hi;   // stored rows whose outputs are written
+};
+
+__device__ __forceinline__ long win_token_pixel(const WinGeom& g, long win, int qi, int qj, bool& last_row,
+                                                bool& last_col, bool& store) {
+  const long per_img = (long)g.nwr * g.nwc;
+  const long img = win / per_img;
+  const int wrem = (int)(win - img * per_img);
+  const int wr = wrem / g.nwc, wc = wrem - wr * g.nwc;
+  const int y = g.wrap ? (wr * 8 + qi + g.shift) % g.H : g.row_base + wr * 8 + qi;
+  const int x = (wc * 8 + qj + g.shift) % g.W;
+  const int gwr = (g.gwr0 + wr) % g.nwr_global;
+  last_row = g.shift && gwr == g.nwr_global - 1;
+  last_col = g.shift && wc == g.nwc - 1;
+  store = y >= g.store_lo && y < g.store_hi;
+  return (img * g.H + y) * g.W + x;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -17,6 +17,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: the functions are resolved with dlopen at run time
 
 #include <algorithm>
 #include <cmath>
@@ -273,8 +275,11 @@ struct Maker {
   // NHWC buffer whose pixel stride is pix_ld elements.
   // `kx_boxes`: use the GEO_CONV3X schedule (8 x 16 tiles, one box per column
   // shift); only compiled with the TMA epilogue, for cout <= 128.
+  // Output rows [row0, row0 + rows_out) of each image's H stored rows (default:
+  // all of them); rows outside are read as input (halo) but never written.
   bool conv3(GemmOp& op, const __half* x, int n, int H, int W, int cin, long pix_ld, const __half* w, int cout,
-             bool kx_boxes = true) {
+             bool kx_boxes = true, int row0 = 0, int rows_out = -1) {
+    if (rows_out < 0) rows_out = H - row0;
     op.bk = (cin % 64 == 0) ? 64 : 32;
     op.bn = cout;
     op.geo = (kx_boxes && tma_epi_supported(GEO_CONV3X, op.bn, op.bk)) ? GEO_CONV3X : GEO_CONV3;
@@ -299,12 +304,14 @@ struct Maker {
     op.g.n_total = cout;
     op.g.kb_per_tap = cin / op.bk;
     op.g.num_kb = op.geo == GEO_CONV3X ? 3 * op.g.kb_per_tap : 9 * op.g.kb_per_tap;
+    op.g.row0 = row0;
+    op.g.rows_out = rows_out;
     op.g.H = H;
     op.g.W = W;
     op.g.TH = TH;
     op.g.TW = TW;
     op.g.tiles_x = (W + TW - 1) / TW;
-    op.g.tiles_y = (H + TH - 1) / TH;
+    op.g.tiles_y = (rows_out + TH - 1) / TH;
     op.g.m_tiles = n * op.g.tiles_y * op.g.tiles_x;
     op.g.n_tiles = 1;
     return true;
@@ -353,8 +360,9 @@ struct Maker {
       const uint32_t box[2] = {32, 128};
       return encode_map(m, base, 2, dims, str, box, es, sw, *err);
     } else if (op.geo == GEO_CONV3 || op.geo == GEO_CONV3X) {
+      // rows past the op's output range are clipped on store and read as zero
       const uint64_t n = (uint64_t)g.M / ((uint64_t)g.H * g.W);
-      const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)g.H, n};
+      const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)(g.row0 + g.rows_out), n};
       const uint64_t str[3] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es, (uint64_t)g.H * g.W * ld * es};
       const uint32_t box[4] = {32, (uint32_t)g.TW, (uint32_t)g.TH, 1};
       return encode_map(m, base, 4, dims, str, box, es, sw, *err);
@@ -436,7 +444,16 @@ enum OpTag : int {
 };
 
 struct Op {
-  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS } kind;
+  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS, XCHG, ZERO } kind;
+  // XCHG (row bands): swap kHalo boundary rows of a stored plane with the
+  // neighbouring bands; xchg_base is the plane, xchg_row the bytes of one row
+  char* xchg_base = nullptr;
+  size_t xchg_row = 0;
+  int xchg_row0 = 0, xchg_rows = 0;  // the band's working rows in the plane
+  // ZERO: clear zero_bytes at zero_ptr (an edge band's halo rows, which the conv's
+  // zero padding reads)
+  char* zero_ptr = nullptr;
+  size_t zero_bytes = 0;
   TransGeom trans{};
   int trans_t = 0;
   int tag = 0;
@@ -448,8 +465,20 @@ struct Op {
   const float* attn_rp = nullptr;
 };
 
+// A row band of one image (config 5): full-resolution rows [R0, R0 + rows) of the
+// padded image, stored with kHalo extra rows above and below at every level.
+constexpr int kHalo = 4;
+
+struct Band {
+  int rank = 0, nranks = 1;
+  int R0 = 0, rows = 0;      // full-resolution band rows
+  bool top = true, bottom = true;  // the band touches the image top / bottom
+};
+
 struct Arena {
   int n = 0, hp = 0, wp = 0;
+  bool banded = false;
+  Band band;
   char* base = nullptr;
   size_t bytes = 0;
   float* skip[4] = {};
@@ -461,20 +490,30 @@ struct Arena {
   std::vector<Op> ops;     // head .. tail
 };
 
-size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A) {
-  const size_t P = (size_t)n * hp * wp;
+// Stored pixels of the level-l plane: the whole image, or a band with its halo rows.
+size_t plane_px(int n, int hp, int wp, const Band* band, int l) {
+  if (band) return (size_t)((band->rows >> l) + 2 * kHalo) * (size_t)(wp >> l);
+  return (size_t)n * (hp >> l) * (wp >> l);
+}
+
+size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band = nullptr) {
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
     off += (bytes + 1023) & ~size_t(1023);
     return o;
   };
+  size_t px[4], wmax = 0;  // wmax: the largest (stored pixels x 64-channel units) over levels
+  for (int l = 0; l < 4; ++l) {
+    px[l] = plane_px(n, hp, wp, band, l);
+    wmax = std::max(wmax, px[l] << l);
+  }
   size_t o_skip[4], o_xs[4];
-  for (int s = 0; s < 4; ++s) o_skip[s] = take(P * 256 >> s);
-  for (int s = 0; s < 4; ++s) o_xs[s] = take(P * 128 >> s);
-  size_t o_xw = take(P * 256), o_y = take(P * 128), o_hc = take(P * 64), o_z = take(P * 128), o_a = take(P * 64),
-         o_o = take(P * 64), o_qh = take(P * 256);
-  size_t o_in = take(P * in_nc * 4), o_out = take(P * in_nc * 4);
+  for (int l = 0; l < 4; ++l) o_skip[l] = take((px[l] << l) * 256);
+  for (int l = 0; l < 4; ++l) o_xs[l] = take((px[l] << l) * 128);
+  size_t o_xw = take(wmax * 256), o_y = take(wmax * 128), o_hc = take(wmax * 64), o_z = take(wmax * 128),
+         o_a = take(wmax * 64), o_o = take(wmax * 64), o_qh = take(wmax * 256);
+  size_t o_in = take(px[0] * in_nc * 4), o_out = take(px[0] * in_nc * 4);
   if (A) {
     char* b = A->base;
     for (int s = 0; s < 4; ++s) {
@@ -492,6 +531,43 @@ size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A) {
     A->io_out = reinterpret_cast<float*>(b + o_out);
   }
   return off;
+}
+
+// The stored plane of one level and the rows the ops work on.
+struct Region {
+  int n = 1;         // images
+  int H = 0, W = 0;  // stored rows per image, columns
+  int row0 = 0;      // first working row (kHalo for a band)
+  int rows = 0;      // working rows per image
+  bool banded = false;
+  int grow0 = 0;     // image row of working row 0 (band)
+  int H_image = 0;   // rows of the whole padded image at this level
+  bool top = true, bottom = true;
+  long px() const { return (long)n * rows * W; }  // working pixels
+  long off(int ch) const { return (long)row0 * W * ch; }  // element offset of working row 0 (n == 1 when banded)
+};
+
+// The level-l region of arena A (the whole batch, or A's band).
+Region region_of(const Arena& A, int l) {
+  Region R;
+  R.W = A.wp >> l;
+  R.H_image = A.hp >> l;
+  if (!A.banded) {
+    R.n = A.n;
+    R.H = A.hp >> l;
+    R.row0 = 0;
+    R.rows = R.H;
+  } else {
+    R.n = 1;
+    R.banded = true;
+    R.rows = A.band.rows >> l;
+    R.row0 = kHalo;
+    R.H = R.rows + 2 * kHalo;
+    R.grow0 = A.band.R0 >> l;
+    R.top = A.band.top;
+    R.bottom = A.band.bottom;
+  }
+  return R;
 }
 
 }  // namespace
@@ -515,6 +591,12 @@ struct scb_ctx {
   // context's device (looked up on the first call) and the plan laid out in it.
   void* noalloc_base = nullptr;
   Arena noalloc;
+  // row bands (config 5): one band per rank over NCCL, or all bands of one image
+  // on this GPU (virtual bands, in lockstep)
+  ncclComm_t nccl = nullptr;
+  int band_rank = 0, band_nranks = 1;
+  Arena band_arena;
+  std::vector<Arena> vbands;
   // SCUNET_PROFILE equivalent (src/cuda.rs:106-135): events around every launch
   bool profiling = false;
   std::vector<cudaEvent_t> events;
@@ -601,7 +683,7 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const unsigned grid = (unsigned)((op.attn.n_windows + 1) / 2);
+  const unsigned grid = (unsigned)((op.attn.win.n_windows + 1) / 2);
   window_attn_kernel<<<grid, 128, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
   return cudaGetLastError();
 }
@@ -619,7 +701,7 @@ cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const long pairs = (op.trans.n_windows + 1) / 2;
+  const long pairs = (op.trans.win.n_windows + 1) / 2;
   const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
   trans_fused_kernel<T><<<grid, 256, L::SMEM, st>>>(op.trans);
   return cudaGetLastError();
@@ -647,10 +729,116 @@ cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* o
 }
 
 // Run the ops of the arena's plan on `st`, with the image pointers of this call.
+// The image of one forward call.
+struct Io {
+  const void* x;
+  int x_u8;
+  void* y;
+  int y_u8;
+  int c, h, w;
+};
+
+// Halo exchange of one XCHG op between bands. `nb` bands of this process (one, for
+// a rank of a NCCL group; all of them for virtual bands on one GPU).
+int exchange_nccl(scb_ctx* ctx, Arena& A, const Op& op, cudaStream_t st);
+
+int exchange_local(scb_ctx* ctx, std::vector<Arena>& bands, size_t k, cudaStream_t st) {
+  // every band copies its kHalo first/last working rows into its neighbours' halo
+  for (size_t b = 0; b < bands.size(); ++b) {
+    const Op& op = bands[b].ops[k];
+    const size_t bytes = (size_t)kHalo * op.xchg_row;
+    if (b > 0) {
+      const Op& up = bands[b - 1].ops[k];
+      CKC(ctx, cudaMemcpyAsync(up.xchg_base + (size_t)(up.xchg_row0 + up.xchg_rows) * up.xchg_row,
+                               op.xchg_base + (size_t)op.xchg_row0 * op.xchg_row, bytes, cudaMemcpyDeviceToDevice, st),
+          "halo copy");
+    }
+    if (b + 1 < bands.size()) {
+      const Op& dn = bands[b + 1].ops[k];
+      CKC(ctx, cudaMemcpyAsync(dn.xchg_base + (size_t)(dn.xchg_row0 - kHalo) * dn.xchg_row,
+                               op.xchg_base + (size_t)(op.xchg_row0 + op.xchg_rows - kHalo) * op.xchg_row, bytes,
+                               cudaMemcpyDeviceToDevice, st),
+          "halo copy");
+    }
+  }
+  return SCB_OK;
+}
+
+// NCCL, loaded at run time so the library needs it only for multi-GPU bands.
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+const NcclApi* nccl_api(std::string& err) {
+  static NcclApi api;
+  static bool loaded = false, tried = false;
+  if (!tried) {
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+      api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+      api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+      api.Send = reinterpret_cast<decltype(api.Send)>(dlsym(h, "ncclSend"));
+      api.Recv = reinterpret_cast<decltype(api.Recv)>(dlsym(h, "ncclRecv"));
+      api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
+      api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
+      api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+      loaded = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.Send && api.Recv && api.GroupStart &&
+               api.GroupEnd && api.GetErrorString;
+    }
+  }
+  if (!loaded) {
+    err = "libnccl.so.2 could not be loaded (needed for multi-GPU row bands)";
+    return nullptr;
+  }
+  return &api;
+}
+
+// Launch one op of arena A's plan.
+cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStream_t st) {
+  switch (op.kind) {
+    case Op::HEAD: {
+      const Region R = region_of(A, 0);
+      HeadGeom g{R.n, io.c, io.h, io.w, A.hp, A.wp, io.x_u8, R.grow0, R.rows};
+      return launch_head(ctx, io.x, g, A.skip[0] + R.off(64), A.xs[0] + R.off(64), st);
+    }
+    case Op::TAIL: {
+      GemmOp t = op.gemm;  // the 3x3 implicit GEMM over the (y + x1) shadow, N = 16
+      t.e.nchw_out = io.y;
+      t.e.nchw_c = io.c;
+      t.e.nchw_h = io.h;
+      t.e.nchw_w = io.w;
+      t.e.nchw_u8 = io.y_u8;
+      return launch_gemm(t, ctx->sms, st);
+    }
+    case Op::GEMM:
+      return launch_gemm(op.gemm, ctx->sms, st);
+    case Op::ATTN:
+      return launch_attn(op, st);
+    case Op::TRANS:
+      return launch_trans(op, ctx->sms, st);
+    case Op::XCHG:
+      return cudaSuccess;  // handled by the caller (it needs the other bands)
+    case Op::ZERO:
+      return op.zero_bytes ? cudaMemsetAsync(op.zero_ptr, 0, op.zero_bytes, st) : cudaSuccess;
+  }
+  return cudaErrorInvalidValue;
+}
+
 int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w,
             cudaStream_t st, bool allow_profile = true) {
+  // (a banded arena here is one rank of a NCCL band group)
   int launches = 0;
   const bool profiling = ctx->profiling && allow_profile;
+  const Io io{x, x_u8, y, y_u8, c, h, w};
   if (profiling) {
     while (ctx->events.size() < A.ops.size() + 1) {
       cudaEvent_t ev;
@@ -660,34 +848,13 @@ int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, 
     CKC(ctx, cudaEventRecord(ctx->events[0], st), "cudaEventRecord");
   }
   for (const Op& op : A.ops) {
-    cudaError_t e = cudaSuccess;
-    switch (op.kind) {
-      case Op::HEAD: {
-        HeadGeom g{A.n, c, h, w, A.hp, A.wp, x_u8};
-        e = launch_head(ctx, x, g, A.skip[0], A.xs[0], st);
-        break;
-      }
-      case Op::TAIL: {
-        GemmOp t = op.gemm;  // the 3x3 implicit GEMM over the (y + x1) shadow, N = 16
-        t.e.nchw_out = y;
-        t.e.nchw_c = c;
-        t.e.nchw_h = h;
-        t.e.nchw_w = w;
-        t.e.nchw_u8 = y_u8;
-        e = launch_gemm(t, ctx->sms, st);
-        break;
-      }
-      case Op::GEMM:
-        e = launch_gemm(op.gemm, ctx->sms, st);
-        break;
-      case Op::ATTN:
-        e = launch_attn(op, st);
-        break;
-      case Op::TRANS:
-        e = launch_trans(op, ctx->sms, st);
-        break;
+    if (op.kind == Op::XCHG) {
+      const int r = exchange_nccl(ctx, A, op, st);
+      if (r) return r;
+    } else {
+      const cudaError_t e = exec_op(ctx, A, op, io, st);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
     }
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
     ++launches;
     if (profiling) CKC(ctx, cudaEventRecord(ctx->events[launches], st), "cudaEventRecord");
   }
@@ -704,13 +871,54 @@ int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, 
   return SCB_OK;
 }
 
-// The ops of one ConvTransBlock at stage plane (n, H, W) with c channels.
-//   xin (fp32, shadow already in xs) -> xout (fp32, may alias xin; may be null
-//   when `skip` is given: then only the fp16 shadow of (x + skip) is written).
-bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena& A, int n, int H, int W,
+Op xchg_op(void* plane, const Region& R, int ch, int elem_bytes) {
+  Op x{};
+  x.kind = Op::XCHG;
+  x.xchg_base = static_cast<char*>(plane);
+  x.xchg_row = (size_t)R.W * ch * elem_bytes;
+  x.xchg_row0 = R.row0;
+  x.xchg_rows = R.rows;
+  return x;
+}
+
+// Window placement of a block's attention over region R.
+WinGeom win_geom(const Region& R, bool shifted) {
+  WinGeom g{};
+  g.H = R.H;
+  g.W = R.W;
+  g.shift = shifted ? 4 : 0;
+  g.nwc = R.W / 8;
+  g.nwr_global = R.H_image / 8;
+  if (!R.banded) {
+    g.wrap = 1;
+    g.row_base = 0;
+    g.nwr = R.H / 8;
+    g.gwr0 = 0;
+    g.store_lo = 0;
+    g.store_hi = R.H;
+  } else {
+    // W: the band's own windows. SW: one more window row; the first starts 4 rows
+    // above the band, the last ends 4 rows below it (both in the halo).
+    g.wrap = 0;
+    g.row_base = shifted ? R.row0 - 4 : R.row0;
+    g.nwr = R.rows / 8 + (shifted ? 1 : 0);
+    g.gwr0 = ((R.grow0 / 8 - (shifted ? 1 : 0)) % g.nwr_global + g.nwr_global) % g.nwr_global;
+    g.store_lo = R.row0;
+    g.store_hi = R.row0 + R.rows;
+  }
+  g.n_windows = (long)R.n * g.nwr * g.nwc;
+  return g;
+}
+
+// The ops of one ConvTransBlock over region R of a level with c channels.
+//   xin (fp32, its fp16 shadow already in xs) -> xout (fp32, may alias xin; may be
+//   null when `skip` is given: then only the fp16 shadow of (x + skip) is written).
+// Plane pointers are the stored planes; FLAT ops address the working rows.
+bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena& A, const Region& R,
                const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err) {
   const int c = bw.c, t = c / 2, cc = c / 2, heads = t / 32;
-  const long P = (long)n * H * W;
+  const int n = R.n, H = R.H, W = R.W;
+  const long P = R.px();
   const bool fused = ctx->fuse_trans && (t == 32 || t == 64);
   Maker mk{&err};
   Op op{};
@@ -718,14 +926,14 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
   {
     GemmOp g{};
-    if (!mk.flat(g, xs, P, c, c, bw.w11, c)) return false;
+    if (!mk.flat(g, xs + R.off(c), P, c, c, bw.w11, c)) return false;
     g.e.bias = bw.b11;
-    g.e.out16 = A.y;
+    g.e.out16 = A.y + R.off(c);
     g.e.out16_ld = c;
     if (!fused) {  // the fused transformer kernel normalises its own input
       g.e.ln_g = bw.ln1g;
       g.e.ln_b = bw.ln1b;
-      g.e.ln_out = A.a;
+      g.e.ln_out = A.a + R.off(t);
       g.e.ln_ld = t;
       g.e.ln_lo = cc;
       g.e.ln_n = t;
@@ -736,23 +944,32 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     op.flops = 2.0 * P * c * c;
     ops.push_back(op);
   }
-  // 2. h = relu(conv3x3(y_c))
+  if (R.banded) {
+    // the one exchange of the block: Y's boundary rows (3x3 pair and SW windows),
+    // and for the separate-launch transformer path also LN1's
+    ops.push_back(xchg_op(A.y, R, c, 2));
+    if (!fused) ops.push_back(xchg_op(A.a, R, t, 2));
+  }
+  // 2. h = relu(conv3x3(y_c)), on the working rows plus one halo row on each side
+  //    that has a neighbour (conv 3 reads it); the image's own edges stay zero
   {
+    const int lo = R.banded && !R.top ? R.row0 - 1 : R.row0;
+    const int hi = R.banded && !R.bottom ? R.row0 + R.rows + 1 : R.row0 + R.rows;
     GemmOp g{};
-    if (!mk.conv3(g, A.y, n, H, W, cc, c, bw.wc0, cc)) return false;
+    if (!mk.conv3(g, A.y, n, H, W, cc, c, bw.wc0, cc, true, lo, hi - lo)) return false;
     g.e.act = ACT_RELU;
     g.e.out16 = A.hc;
     g.e.out16_ld = cc;
     if (!mk.finish_epi(g)) return false;
     op.gemm = g;
     op.tag = TAG_CONV3X3;
-    op.flops = 2.0 * P * 9 * cc * cc;
+    op.flops = 2.0 * n * (hi - lo) * W * 9 * cc * cc;
     ops.push_back(op);
   }
   // 3. z[:, :cc] = conv3x3(h) + y_c
   {
     GemmOp g{};
-    if (!mk.conv3(g, A.hc, n, H, W, cc, cc, bw.wc2, cc)) return false;
+    if (!mk.conv3(g, A.hc, n, H, W, cc, cc, bw.wc2, cc, true, R.row0, R.rows)) return false;
     g.e.res16 = A.y;
     g.e.res16_ld = c;
     g.e.out16 = A.z;
@@ -763,6 +980,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     op.flops = 2.0 * P * 9 * cc * cc;
     ops.push_back(op);
   }
+  const WinGeom wg = win_geom(R, shifted);
   if (fused) {
     // 4-8. the whole transformer half in one kernel
     Op tr{};
@@ -771,10 +989,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     tr.tag = TAG_TRANS;
     tr.flops = 2.0 * P * (3.0 * t * t + 2.0 * 64 * t + t * t + 8.0 * t * t);
     TransGeom& tg = tr.trans;
-    tg.H = H;
-    tg.W = W;
-    tg.shift = shifted ? 4 : 0;
-    tg.n_windows = (long)n * (H / 8) * (W / 8);
+    tg.win = wg;
     tg.y = A.y;
     tg.z = A.z;
     tg.wqkv = bw.wqkv; tg.wproj = bw.wproj; tg.w0 = bw.w0; tg.w2 = bw.w2;
@@ -782,24 +997,26 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     tg.ln1g = bw.ln1g; tg.ln1b = bw.ln1b; tg.ln2g = bw.ln2g; tg.ln2b = bw.ln2b; tg.rp = bw.rp;
     ops.push_back(tr);
   } else {
-    // 4. qkv = LN1(y_t) W^T + b
+    // 4. qkv = LN1(y_t) W^T + b; a band needs it on its halo rows too (SW windows)
     {
+      const long Pq = R.banded ? (long)n * H * W : P;
+      const long oq = R.banded ? 0 : R.off(t);
       GemmOp g{};
-      if (!mk.flat(g, A.a, P, t, t, bw.wqkv, 3 * t)) return false;
+      if (!mk.flat(g, A.a + oq, Pq, t, t, bw.wqkv, 3 * t)) return false;
       g.e.bias = bw.bqkv;
-      g.e.out16 = A.qh;
+      g.e.out16 = A.qh + (R.banded ? 0 : R.off(3 * t));
       g.e.out16_ld = 3 * t;
       if (!mk.finish_epi(g)) return false;
       op.gemm = g;
       op.tag = TAG_QKV;
-      op.flops = 2.0 * P * t * 3 * t;
+      op.flops = 2.0 * Pq * t * 3 * t;
       ops.push_back(op);
     }
     // 5. window attention
     {
       Op at{};
       at.kind = Op::ATTN;
-      at.attn = AttnGeom{n, H, W, t, heads, shifted ? 4 : 0, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
+      at.attn = AttnGeom{wg, t, heads, 3L * t, (long)t};
       at.attn_in = A.qh;
       at.attn_out = A.o;
       at.attn_rp = bw.rp;
@@ -810,15 +1027,15 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
     {
       GemmOp g{};
-      if (!mk.flat(g, A.o, P, t, t, bw.wproj, t)) return false;
+      if (!mk.flat(g, A.o + R.off(t), P, t, t, bw.wproj, t)) return false;
       g.e.bias = bw.bproj;
-      g.e.res16 = A.y + cc;
+      g.e.res16 = A.y + R.off(c) + cc;
       g.e.res16_ld = c;
-      g.e.out16 = A.z + cc;
+      g.e.out16 = A.z + R.off(c) + cc;
       g.e.out16_ld = c;
       g.e.ln_g = bw.ln2g;
       g.e.ln_b = bw.ln2b;
-      g.e.ln_out = A.a;
+      g.e.ln_out = A.a + R.off(t);
       g.e.ln_ld = t;
       g.e.ln_lo = 0;
       g.e.ln_n = t;
@@ -831,10 +1048,10 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     // 7. hid = gelu(LN2 W0^T + b0)
     {
       GemmOp g{};
-      if (!mk.flat(g, A.a, P, t, t, bw.w0, 4 * t)) return false;
+      if (!mk.flat(g, A.a + R.off(t), P, t, t, bw.w0, 4 * t)) return false;
       g.e.bias = bw.b0;
       g.e.act = ACT_GELU;
-      g.e.out16 = A.qh;
+      g.e.out16 = A.qh + R.off(4 * t);
       g.e.out16_ld = 4 * t;
       if (!mk.finish_epi(g)) return false;
       op.gemm = g;
@@ -845,11 +1062,11 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     // 8. z[:, cc:] = hid W2^T + b2 + x1t
     {
       GemmOp g{};
-      if (!mk.flat(g, A.qh, P, 4 * t, 4 * t, bw.w2, t)) return false;
+      if (!mk.flat(g, A.qh + R.off(4 * t), P, 4 * t, 4 * t, bw.w2, t)) return false;
       g.e.bias = bw.b2;
-      g.e.res16 = A.z + cc;
+      g.e.res16 = A.z + R.off(c) + cc;
       g.e.res16_ld = c;
-      g.e.out16 = A.z + cc;
+      g.e.out16 = A.z + R.off(c) + cc;
       g.e.out16_ld = c;
       if (!mk.finish_epi(g)) return false;
       op.gemm = g;
@@ -861,15 +1078,15 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   // 9. x = x + conv1_2(z) + b  (fp32) and its shadow (or the shadow of x + skip)
   {
     GemmOp g{};
-    if (!mk.flat(g, A.z, P, c, c, bw.w12, c)) return false;
+    if (!mk.flat(g, A.z + R.off(c), P, c, c, bw.w12, c)) return false;
     g.e.bias = bw.b12;
-    g.e.res32 = xin;
+    g.e.res32 = xin + R.off(c);
     g.e.res32_ld = c;
-    g.e.out32 = xout;
+    g.e.out32 = xout ? xout + R.off(c) : nullptr;
     g.e.out32_ld = c;
-    g.e.out16 = xs;
+    g.e.out16 = xs + R.off(c);
     g.e.out16_ld = c;
-    g.e.skip32 = skip;
+    g.e.skip32 = skip ? skip + R.off(c) : nullptr;
     g.e.skip_ld = c;
     if (!mk.finish_epi(g)) return false;
     op.gemm = g;
@@ -885,10 +1102,8 @@ int build_plan(scb_ctx* ctx, Arena& A) {
   std::string err;
   std::vector<Op>& ops = A.ops;
   ops.clear();
-  const int n = A.n;
-  auto H = [&](int lvl) { return A.hp >> lvl; };
-  auto W = [&](int lvl) { return A.wp >> lvl; };
-  const double P0 = (double)n * A.hp * A.wp;
+  const Region R0 = region_of(A, 0);
+  const double P0 = (double)R0.px();
   Op head{};
   head.kind = Op::HEAD;
   head.tag = TAG_HEAD;
@@ -898,21 +1113,44 @@ int build_plan(scb_ctx* ctx, Arena& A) {
     const int lvl = kStageLevel[s];
     const int c = 64 << lvl;
     const bool up = s >= 4;
+    const Region R = region_of(A, lvl);
+    if (R.banded) {
+      // Y and Hc are shared by all levels; at an image edge their halo rows must read
+      // as zero (conv zero padding) although other levels wrote that memory
+      // (every band gets the same ops - lockstep execution pairs them by index - and
+      // the interior sides clear nothing)
+      const size_t rb_y = (size_t)R.W * c * 2, rb_h = (size_t)R.W * (c / 2) * 2;
+      for (int side = 0; side < 2; ++side) {
+        const bool edge = side == 0 ? R.top : R.bottom;
+        const int r = side == 0 ? 0 : R.row0 + R.rows;
+        Op zy{};
+        zy.kind = Op::ZERO;
+        zy.zero_ptr = reinterpret_cast<char*>(A.y) + r * rb_y;
+        zy.zero_bytes = edge ? kHalo * rb_y : 0;
+        ops.push_back(zy);
+        Op zh = zy;
+        zh.zero_ptr = reinterpret_cast<char*>(A.hc) + r * rb_h;
+        zh.zero_bytes = edge ? kHalo * rb_h : 0;
+        ops.push_back(zh);
+      }
+    }
     if (up) {
       // m_up{k}.0 : transposed conv from level lvl+1 (shadow already holds x + skip)
+      const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
       Maker mk{&err};
       GemmOp g{};
-      if (!mk.up2(g, A.xs[lvl + 1], n, H(lvl + 1), W(lvl + 1), 2 * c, ctx->wup[s - 4], c)) return fail(ctx, SCB_EINVAL, err);
-      g.e.out32 = A.xw;
+      if (!mk.up2(g, A.xs[lvl + 1] + Rn.off(2 * c), Rn.n, Rn.rows, Rn.W, 2 * c, ctx->wup[s - 4], c))
+        return fail(ctx, SCB_EINVAL, err);
+      g.e.out32 = A.xw + R.off(c);
       g.e.out32_ld = c;
-      g.e.out16 = A.xs[lvl];
+      g.e.out16 = A.xs[lvl] + R.off(c);
       g.e.out16_ld = c;
       if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
       op.gemm = g;
       op.tag = TAG_UP;
-      op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (2 * c) * (4 * c);
+      op.flops = 2.0 * Rn.px() * (2 * c) * (4 * c);
       ops.push_back(op);
     }
     const int nb = ctx->config[s];
@@ -925,33 +1163,37 @@ int build_plan(scb_ctx* ctx, Arena& A) {
         skip = A.skip[lvl];
         xout = nullptr;
       }
-      if (!block_ops(ctx, ops, ctx->blocks[s][i], A, n, H(lvl), W(lvl), xin, xout, A.xs[lvl], skip, (i % 2) == 1, err))
+      if (!block_ops(ctx, ops, ctx->blocks[s][i], A, R, xin, xout, A.xs[lvl], skip, (i % 2) == 1, err))
         return fail(ctx, SCB_EINVAL, err);
     }
     if (s < 3) {
       // m_down{k}.4 : 2x2 stride-2 conv -> the next level's skip (fp32) + shadow
+      const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
       Maker mk{&err};
       GemmOp g{};
-      if (!mk.down2(g, A.xs[lvl], n, H(lvl), W(lvl), c, ctx->wdown[s], 2 * c)) return fail(ctx, SCB_EINVAL, err);
-      g.e.out32 = A.skip[lvl + 1];
+      if (!mk.down2(g, A.xs[lvl] + R.off(c), R.n, R.rows, R.W, c, ctx->wdown[s], 2 * c))
+        return fail(ctx, SCB_EINVAL, err);
+      g.e.out32 = A.skip[lvl + 1] + Rn.off(2 * c);
       g.e.out32_ld = 2 * c;
-      g.e.out16 = A.xs[lvl + 1];
+      g.e.out16 = A.xs[lvl + 1] + Rn.off(2 * c);
       g.e.out16_ld = 2 * c;
       if (!mk.finish_epi(g)) return fail(ctx, SCB_EINVAL, err);
       op.gemm = g;
       op.tag = TAG_DOWN;
-      op.flops = 2.0 * (P0 / (4 << (2 * lvl))) * (4 * c) * (2 * c);
+      op.flops = 2.0 * Rn.px() * (4 * c) * (2 * c);
       ops.push_back(op);
     }
   }
+  if (R0.banded) ops.push_back(xchg_op(A.xs[0], R0, 64, 2));  // the tail conv's halo row
   Op tail{};
   tail.kind = Op::TAIL;
   {
     Maker mk{&err};
-    if (!mk.conv3(tail.gemm, A.xs[0], n, A.hp, A.wp, 64, 64, ctx->wtail16, 16, false))
+    if (!mk.conv3(tail.gemm, A.xs[0], R0.n, R0.H, R0.W, 64, 64, ctx->wtail16, 16, false, R0.row0, R0.rows))
       return fail(ctx, SCB_EINVAL, err);
+    tail.gemm.e.nchw_row_off = R0.grow0 - R0.row0;
   }
   tail.tag = TAG_TAIL;
   tail.flops = 2.0 * P0 * 9 * 64 * ctx->in_nc;
@@ -990,6 +1232,89 @@ int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
   A.wp = wp;
   arena_layout(n, ctx->in_nc, hp, wp, &A);
   return build_plan(ctx, A);
+}
+
+int exchange_nccl(scb_ctx* ctx, Arena& A, const Op& op, cudaStream_t st) {
+  if (!A.banded || A.band.nranks == 1) return SCB_OK;
+  std::string err;
+  const NcclApi* nc = nccl_api(err);
+  if (!nc || !ctx->nccl) return fail(ctx, SCB_EINVAL, err.empty() ? "band group not initialised" : err);
+  const size_t bytes = (size_t)kHalo * op.xchg_row;
+  char* first = op.xchg_base + (size_t)op.xchg_row0 * op.xchg_row;                      // first working rows
+  char* last = op.xchg_base + (size_t)(op.xchg_row0 + op.xchg_rows - kHalo) * op.xchg_row;  // last working rows
+  char* halo_top = op.xchg_base + (size_t)(op.xchg_row0 - kHalo) * op.xchg_row;
+  char* halo_bot = op.xchg_base + (size_t)(op.xchg_row0 + op.xchg_rows) * op.xchg_row;
+  const int r = A.band.rank;
+  ncclResult_t e = nc->GroupStart();
+  if (e == ncclSuccess && !A.band.top) {
+    e = nc->Send(first, bytes, ncclUint8, r - 1, ctx->nccl, st);
+    if (e == ncclSuccess) e = nc->Recv(halo_top, bytes, ncclUint8, r - 1, ctx->nccl, st);
+  }
+  if (e == ncclSuccess && !A.band.bottom) {
+    e = nc->Send(last, bytes, ncclUint8, r + 1, ctx->nccl, st);
+    if (e == ncclSuccess) e = nc->Recv(halo_bot, bytes, ncclUint8, r + 1, ctx->nccl, st);
+  }
+  const ncclResult_t e2 = nc->GroupEnd();
+  if (e == ncclSuccess) e = e2;
+  if (e != ncclSuccess) return fail(ctx, SCB_ECUDA, std::string("halo exchange: ") + nc->GetErrorString(e));
+  return SCB_OK;
+}
+
+// Rank `rank` of `nranks` gets a contiguous run of the padded image's 64-row blocks.
+bool band_of(int hp, int rank, int nranks, Band& b, std::string& err) {
+  const int nblk = hp / 64;
+  if (nranks < 1 || rank < 0 || rank >= nranks) {
+    err = "band rank out of range";
+    return false;
+  }
+  if (nblk < nranks) {
+    err = "the padded image has " + std::to_string(nblk) + " 64-row blocks, fewer than the " +
+          std::to_string(nranks) + " bands asked for";
+    return false;
+  }
+  const int b0 = (int)((long)rank * nblk / nranks), b1 = (int)((long)(rank + 1) * nblk / nranks);
+  b.rank = rank;
+  b.nranks = nranks;
+  b.R0 = 64 * b0;
+  b.rows = 64 * (b1 - b0);
+  b.top = rank == 0;
+  b.bottom = rank == nranks - 1;
+  return true;
+}
+
+// Allocate (zeroed: edge halo rows must read as zero) and plan one band's arena.
+int ensure_band_arena(scb_ctx* ctx, Arena& A, const Band& band, int hp, int wp) {
+  if (A.base && A.banded && A.hp == hp && A.wp == wp && A.band.R0 == band.R0 && A.band.rows == band.rows &&
+      A.band.nranks == band.nranks && !A.ops.empty())
+    return SCB_OK;
+  const size_t need = arena_layout(1, ctx->in_nc, hp, wp, nullptr, &band);
+  if (A.base && A.bytes < need) {
+    cudaFree(A.base);
+    A.base = nullptr;
+    A.bytes = 0;
+  }
+  if (!A.base) {
+    cudaError_t e = cudaMalloc(&A.base, need);
+    if (e != cudaSuccess) {
+      A.base = nullptr;
+      return fail(ctx, SCB_ENOMEM, std::string("band arena allocation refused: ") + cudaGetErrorString(e));
+    }
+    A.bytes = need;
+  }
+  CKC(ctx, cudaMemset(A.base, 0, A.bytes), "band arena clear");
+  CKC(ctx, cudaDeviceSynchronize(), "band arena clear");
+  A.n = 1;
+  A.hp = hp;
+  A.wp = wp;
+  A.banded = true;
+  A.band = band;
+  arena_layout(1, ctx->in_nc, hp, wp, &A, &band);
+  return build_plan(ctx, A);
+}
+
+void free_arena(Arena& A) {
+  if (A.base) cudaFree(A.base);
+  A = Arena{};
 }
 
 int check_device_error(scb_ctx* ctx) {
@@ -1281,6 +1606,104 @@ int scb_forward(scb_ctx* ctx, const float* x_nchw, int c, int hp, int wp, float*
   return scb_forward_host(ctx, x_nchw, SCB_F32, 1, c, hp, wp, y_nchw, SCB_F32);
 }
 
+int scb_forward_bands(scb_ctx* ctx, int nbands, const void* x, int x_dtype, int c, int h, int w, void* y,
+                      int y_dtype, void* stream) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
+  if (!geom_ok(ctx, 1, c, h, w)) return SCB_EINVAL;
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if ((int)ctx->vbands.size() != nbands) {
+    for (Arena& A : ctx->vbands) free_arena(A);
+    ctx->vbands.assign(std::max(nbands, 0), Arena{});
+  }
+  std::string err;
+  for (int b = 0; b < nbands; ++b) {
+    Band band;
+    if (!band_of(hp, b, nbands, band, err)) return fail(ctx, SCB_EINVAL, err);
+    const int r = ensure_band_arena(ctx, ctx->vbands[b], band, hp, wp);
+    if (r) return r;
+  }
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  const Io io{x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w};
+  const size_t nops = ctx->vbands[0].ops.size();
+  for (const Arena& A : ctx->vbands)
+    if (A.ops.size() != nops) return fail(ctx, SCB_EINVAL, "band plans differ in length");
+  int launches = 0;
+  for (size_t k = 0; k < nops; ++k) {  // lockstep: op k of every band before op k + 1
+    if (ctx->vbands[0].ops[k].kind == Op::XCHG) {
+      const int r = exchange_local(ctx, ctx->vbands, k, st);
+      if (r) return r;
+      continue;
+    }
+    for (Arena& A : ctx->vbands) {
+      const cudaError_t e = exec_op(ctx, A, A.ops[k], io, st);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
+      ++launches;
+    }
+  }
+  ctx->last_launches = launches;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_band_unique_id(void* id_out) {
+  if (!id_out) return fail(nullptr, SCB_EINVAL, "id_out is NULL");
+  std::string err;
+  const NcclApi* nc = nccl_api(err);
+  if (!nc) return fail(nullptr, SCB_EINVAL, err);
+  ncclUniqueId id;
+  const ncclResult_t e = nc->GetUniqueId(&id);
+  if (e != ncclSuccess) return fail(nullptr, SCB_ECUDA, std::string("ncclGetUniqueId: ") + nc->GetErrorString(e));
+  memcpy(id_out, &id, sizeof id);
+  return SCB_OK;
+}
+
+int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!id || rank < 0 || nranks < 1 || rank >= nranks) return fail(ctx, SCB_EINVAL, "band rank / id");
+  std::string err;
+  const NcclApi* nc = nccl_api(err);
+  if (!nc) return fail(ctx, SCB_EINVAL, err);
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (ctx->nccl) {
+    nc->CommDestroy(ctx->nccl);
+    ctx->nccl = nullptr;
+  }
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof uid);
+  const ncclResult_t e = nc->CommInitRank(&ctx->nccl, nranks, uid, rank);
+  if (e != ncclSuccess) {
+    ctx->nccl = nullptr;
+    return fail(ctx, SCB_ECUDA, std::string("ncclCommInitRank: ") + nc->GetErrorString(e));
+  }
+  ctx->band_rank = rank;
+  ctx->band_nranks = nranks;
+  free_arena(ctx->band_arena);
+  ctx->err.clear();
+  return SCB_OK;
+}
+
+int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int w, void* y, int y_dtype,
+                     void* stream) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
+  if (!geom_ok(ctx, 1, c, h, w)) return SCB_EINVAL;
+  if (ctx->band_nranks > 1 && !ctx->nccl) return fail(ctx, SCB_EINVAL, "scb_band_init has not run");
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  std::string err;
+  Band band;
+  if (!band_of(hp, ctx->band_rank, ctx->band_nranks, band, err)) return fail(ctx, SCB_EINVAL, err);
+  int r = ensure_band_arena(ctx, ctx->band_arena, band, hp, wp);
+  if (r) return r;
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  r = run_ops(ctx, ctx->band_arena, x, x_dtype == SCB_U8, y, y_dtype == SCB_U8, c, h, w, st);
+  if (r) return r;
+  ctx->err.clear();
+  return SCB_OK;
+}
+
 int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes) {
   if (!bytes || n <= 0 || hp <= 0 || wp <= 0 || hp % 64 || wp % 64 || (in_nc != 1 && in_nc != 3)) return SCB_EINVAL;
   *bytes = arena_layout(n, in_nc, hp, wp, nullptr);
@@ -1307,6 +1730,8 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     ctx->arena.n = 0;  // re-plan on the next forward
     ctx->noalloc.ops.clear();
     ctx->noalloc.n = 0;
+    ctx->band_arena.ops.clear();
+    for (Arena& A : ctx->vbands) A.ops.clear();
     return SCB_OK;
   }
   return fail(ctx, SCB_EINVAL, "unknown option " + std::to_string(option));
@@ -1341,6 +1766,12 @@ void scb_destroy(scb_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   scb_release_scratch(ctx);
+  free_arena(ctx->band_arena);
+  for (Arena& A : ctx->vbands) free_arena(A);
+  if (ctx->nccl) {
+    std::string err;
+    if (const NcclApi* nc = nccl_api(err)) nc->CommDestroy(ctx->nccl);
+  }
   for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
   if (ctx->wblob) cudaFree(ctx->wblob);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -1432,7 +1863,11 @@ int scb_probe_attention(scb_ctx* ctx, const void* qkv16, int n, int H, int W, in
   if (t % 32 || t / 32 > 8 || H % 8 || W % 8 || (shift != 0 && shift != 4)) return fail(ctx, SCB_EINVAL, "attention geometry");
   Op op{};
   op.kind = Op::ATTN;
-  op.attn = AttnGeom{n, H, W, t, t / 32, shift, (long)n * (H / 8) * (W / 8), 3L * t, (long)t};
+  Region R;
+  R.n = n;
+  R.H = R.rows = R.H_image = H;
+  R.W = W;
+  op.attn = AttnGeom{win_geom(R, shift != 0), t, t / 32, 3L * t, (long)t};
   op.attn_in = static_cast<const __half*>(qkv16);
   op.attn_out = static_cast<__half*>(out16);
   op.attn_rp = rp;
@@ -1477,7 +1912,11 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
   }
   std::vector<Op> ops;
   std::string err;
-  if (!block_ops(ctx, ops, bw, tmp, n, H, W, x32, y32, xs, nullptr, (index % 2) == 1, err)) {
+  Region R;
+  R.n = n;
+  R.H = R.rows = R.H_image = H;
+  R.W = W;
+  if (!block_ops(ctx, ops, bw, tmp, R, x32, y32, xs, nullptr, (index % 2) == 1, err)) {
     cudaFree(base);
     return fail(ctx, SCB_EINVAL, err);
   }

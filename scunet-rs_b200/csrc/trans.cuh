@@ -31,9 +31,7 @@
 namespace scb {
 
 struct TransGeom {
-  int H, W;           // plane per image
-  int shift;          // 0 (W) or 4 (SW)
-  long n_windows;     // n * (H/8) * (W/8)
+  WinGeom win;
   const __half* y;    // Y plane, pixel stride 2T, trans half at column T
   __half* z;          // Z plane, pixel stride 2T, output at column T
   const __half* wqkv; // [3T][T]
@@ -136,25 +134,17 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
 
   const int slot = row >> 6, tok = row & 63;
   const int qi = tok >> 3, qj = tok & 7;
-  const int nwh = g.H >> 3, nww = g.W >> 3;
-  const long per_img = (long)nwh * nww;
-  const long n_pairs = (g.n_windows + 1) / 2;
+  const long n_pairs = (g.win.n_windows + 1) / 2;
   constexpr float kScale = 0.17677669529663687f;  // 32^-1/2
   constexpr float kLog2e = 1.4426950408889634f;
 
-  // token -> pixel of pair `pr` (or -1 when the window does not exist)
-  auto locate = [&](long pr, bool& lr, bool& lc) -> long {
+  // token -> pixel of pair `pr` (or -1 when the window does not exist); `st`:
+  // whether this token's output is stored (band halo rows are not)
+  auto locate = [&](long pr, bool& lr, bool& lc, bool& st) -> long {
     const long win = 2 * pr + slot;
-    lr = lc = false;
-    if (pr >= n_pairs || win >= g.n_windows) return -1;
-    const long img = win / per_img;
-    const int wrem = (int)(win - img * per_img);
-    const int wh = wrem / nww, ww = wrem - wh * nww;
-    const int y = (wh * 8 + qi + g.shift) % g.H;
-    const int x = (ww * 8 + qj + g.shift) % g.W;
-    lr = g.shift && wh == nwh - 1;
-    lc = g.shift && ww == nww - 1;
-    return (img * g.H + y) * g.W + x;
+    lr = lc = st = false;
+    if (pr >= n_pairs || win >= g.win.n_windows) return -1;
+    return win_token_pixel(g.win, win, qi, qj, lr, lc, st);
   };
   auto sync_mma = [&]() {  // all threads: operands written, TMEM reads finished
     fence_proxy_async_smem();
@@ -182,18 +172,18 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
   };
 
   long pair = blockIdx.x;
-  bool lr_n, lc_n;
-  long pix_n = locate(pair, lr_n, lc_n);
+  bool lr_n, lc_n, st_n;
+  long pix_n = locate(pair, lr_n, lc_n, st_n);
   uint4 nx[NCH];
   load_half(pix_n, nx);
 
   for (; pair < n_pairs; pair += gridDim.x) {
     const long pix = pix_n;
-    const bool last_row = lr_n, last_col = lc_n;
+    const bool last_row = lr_n, last_col = lc_n, store = st_n;
     uint4 cur[NCH];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) cur[c] = nx[c];
-    pix_n = locate(pair + gridDim.x, lr_n, lc_n);
+    pix_n = locate(pair + gridDim.x, lr_n, lc_n, st_n);
     load_half(pix_n, nx);
 
     float yt[HALF];  // this thread's half of y_t (the first residual)
@@ -446,7 +436,7 @@ __global__ void __launch_bounds__(256, TransLayout<T>::CTAS) trans_fused_kernel(
         tmem_ld16x2(trow + L::C_MLP2 + hf * HALF, m, trow + L::C_MLP2 + hf * HALF + 16, m + 16);
       else
         tmem_ld16(trow + L::C_MLP2 + hf * HALF, m);
-      if (pix >= 0) {
+      if (pix >= 0 && store) {
         uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * HALF);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
