@@ -14,9 +14,10 @@ import numpy as np
 
 
 def smooth_field(rng, c, h, w):
-    """[c][h][w] float64 in [0, 1]."""
-    yy = (np.arange(h, dtype=np.float64) / h)[:, None]
-    xx = (np.arange(w, dtype=np.float64) / w)[None, :]
+    """[c][h][w] float64 in [0, 1]. Each sinusoid sin(2 pi (fy y/h + fx x/w) + ph) is
+    evaluated separably, sin(a + b) = sin a cos b + cos a sin b, as two outer products."""
+    ya = 2 * np.pi * np.arange(h, dtype=np.float64) / h
+    xa = 2 * np.pi * np.arange(w, dtype=np.float64) / w
     out = np.empty((c, h, w))
     for ch in range(c):
         f = np.zeros((h, w))
@@ -24,7 +25,10 @@ def smooth_field(rng, c, h, w):
             fy, fx = rng.uniform(0.0, 4.0, 2)
             ph = rng.uniform(0.0, 2 * np.pi)
             amp = rng.uniform(0.2, 1.0)
-            f += amp * np.sin(2 * np.pi * (fy * yy + fx * xx) + ph)
+            a = fy * ya + ph
+            b = fx * xa
+            f += np.multiply.outer(amp * np.sin(a), np.cos(b))
+            f += np.multiply.outer(amp * np.cos(a), np.sin(b))
         for _ in range(16):
             y0, x0 = int(rng.integers(0, h)), int(rng.integers(0, w))
             rh, rw = int(rng.integers(2, max(3, h // 4))), int(rng.integers(2, max(3, w // 4)))
@@ -32,6 +36,36 @@ def smooth_field(rng, c, h, w):
         lo, hi = f.min(), f.max()
         out[ch] = (f - lo) / (hi - lo + 1e-12)
     return out
+
+
+def noisy_image_device(seed, c, h, w, sigma, device="cuda"):
+    """Config 5 on the GPU: the same construction as `noisy_image` (smooth field +
+    N(0, sigma), clipped, quantised) computed with torch on `device`, for sizes
+    where the host generator would dominate a benchmark run. Deterministic for a
+    seed on a given device type (its random stream is torch's, not numpy's)."""
+    import torch
+    rng = np.random.default_rng(seed)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    ya = 2 * np.pi * torch.arange(h, device=device, dtype=torch.float32) / h
+    xa = 2 * np.pi * torch.arange(w, device=device, dtype=torch.float32) / w
+    out = torch.empty((c, h, w), device=device, dtype=torch.float32)
+    for ch in range(c):
+        f = torch.zeros((h, w), device=device, dtype=torch.float32)
+        for _ in range(8):
+            fy, fx = rng.uniform(0.0, 4.0, 2)
+            ph = rng.uniform(0.0, 2 * np.pi)
+            amp = rng.uniform(0.2, 1.0)
+            a = fy * ya + ph
+            b = fx * xa
+            f += amp * (torch.outer(torch.sin(a), torch.cos(b)) + torch.outer(torch.cos(a), torch.sin(b)))
+        for _ in range(16):
+            y0, x0 = int(rng.integers(0, h)), int(rng.integers(0, w))
+            rh, rw = int(rng.integers(2, max(3, h // 4))), int(rng.integers(2, max(3, w // 4)))
+            f[y0:y0 + rh, x0:x0 + rw] = float(rng.uniform(float(f.min()), float(f.max())))
+        out[ch] = (f - f.min()) / (f.max() - f.min() + 1e-12)
+    out += torch.randn(out.shape, generator=gen, device=device) * sigma
+    return torch.floor(out.clamp(0.0, 1.0) * 255.0 + 0.5).to(torch.uint8)[None]
 
 
 def quantise(x):
