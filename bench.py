@@ -17,6 +17,12 @@ from a live per-launch event profile (`scb_set_profiling`). `cpu_baseline` times
 the CPU oracle (`oracle/scunet_np.py`, the reference's algorithm restated in
 numpy) on a bounded crop.
 
+`--workload band` measures BASELINE.json config 5 instead: one seeded 8192x8192
+RGB uint8 image split into 64-row-aligned row bands, one band per rank
+(`scb_band_init` + `scb_forward_band`; halo rows cross NVLink with NCCL send/recv
+inside the forward). A step is one forward of the whole image; the total work is
+fixed as N grows (strong scaling).
+
 `--impl reference` times the reference's CPU implementation of the path. The
 reference's own CPU code is Rust and cannot be built here (no cargo, unvendored
 crates), so the arm runs the oracle port on all host cores, rank 0 only.
@@ -50,6 +56,9 @@ def args_():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["frames", "band"], default="frames",
+                    help="frames: config 4 batch sharding (default); band: config 5 row bands")
+    ap.add_argument("--size", type=int, default=8192, help="band workload: image side")
     ap.add_argument("--frames", type=int, default=16, help="frames per GPU per step")
     ap.add_argument("--micro", type=int, default=4, help="frames per library call")
     ap.add_argument("--no-e2e", action="store_true")
@@ -149,32 +158,90 @@ def reference_arm(a, rank, world):
     }), flush=True)
 
 
-def main():
-    a = args_()
-    rank, world, local = dist_env()
-    if a.impl == "reference":
-        reference_arm(a, rank, world)
-        return
-    import torch
-    import torch.distributed as dist
+def roofline_from_profile(prof):
+    """The dominant op class of one profiled forward against the tensor peak."""
+    cls = {}
+    for name, fl, t in prof:
+        c = cls.setdefault(name, [0.0, 0.0, 0])
+        c[0] += fl
+        c[1] += t
+        c[2] += 1
+    tot_ms = sum(v[1] for v in cls.values())
+    dom = max((k for k in cls if k != "halo"), key=lambda k: cls[k][1])
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    achieved = cls[dom][0] / (cls[dom][1] / 1e3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom)
+    return {
+        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans_fused_kernel",
+                   "head": "head_tc_kernel", "tail": "tail_conv_kernel"}.get(dom, f"gemm_tc_kernel [{dom}]"),
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+        "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,
+        "launches": cls[dom][2], "share_of_forward": cls[dom][1] / tot_ms,
+        "classes_ms_share": {k: round(v[1] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][1])},
+        "whole_forward_tflops": sum(v[0] for v in cls.values()) / (tot_ms / 1e3) / 1e12,
+    }
 
-    scb = importlib.import_module("scunet-rs_b200")
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+class Job:
+    """Process-group plumbing shared by both workloads."""
 
-    def max_over_ranks(v):
-        if world == 1:
+    def __init__(self, a):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.rank, self.world, self.local = dist_env()
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+        except Exception:
+            pass
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
             return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def timed(self, step, steps, stream):
+        """ms per step: CUDA events on `stream`, barrier + synchronize on both sides,
+        max over ranks; clocks sampled during the region."""
+        torch = self.torch
+        self.barrier()
+        clk = Clocks(self.uuid)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        ms = self.max_over_ranks(t0.elapsed_time(t1) / steps)
+        self.barrier()
+        return ms, clocks
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def frames_workload(a, job, scb):
+    torch = job.torch
+    rank, world, local = job.rank, job.world, job.local
     F, micro = a.frames, a.micro
     assert F % micro == 0, "--frames must be a multiple of --micro"
     wt = scb.Weights.seeded(3, 0)
@@ -198,25 +265,7 @@ def main():
         step()
     torch.cuda.synchronize()
     launches_per_call = be.last_launch_count()
-    barrier()
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(local).uuid)
-    except Exception:
-        pass
-    clk = Clocks(uuid)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    t0.record(stream)
-    for _ in range(a.steps):
-        step()
-    t1.record(stream)
-    torch.cuda.synchronize()
-    clocks = clk.stop()
-    ms = t0.elapsed_time(t1) / a.steps
-    ms = max_over_ranks(ms)
-    barrier()
+    ms, clocks = job.timed(step, a.steps, stream)
     mp_step = F * H * W * world / 1e6
     value = mp_step / (ms / 1e3)
 
@@ -224,32 +273,8 @@ def main():
     be.set_profiling(True)
     be.forward_dev(x_dev[0].data_ptr(), scb.SCB_U8, micro, C, H, W, y_dev[0].data_ptr(), scb.SCB_F32, sp)
     torch.cuda.synchronize()
-    prof = be.profile()
+    roofline = roofline_from_profile(be.profile())
     be.set_profiling(False)
-    cls = {}
-    for name, fl, t in prof:
-        c = cls.setdefault(name, [0.0, 0.0, 0])
-        c[0] += fl
-        c[1] += t
-        c[2] += 1
-    tot_ms = sum(v[1] for v in cls.values())
-    dom = max(cls, key=lambda k: cls[k][1])
-    pk, pk_kind = peaks()
-    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
-    achieved = cls[dom][0] / (cls[dom][1] / 1e3) / 1e12
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get(dom)
-    roofline = {
-        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans_fused_kernel",
-                   "head": "head_conv_kernel", "tail": "tail_conv_kernel"}.get(dom, f"gemm_tc_kernel [{dom}]"),
-        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-        "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,
-        "launches": cls[dom][2], "share_of_forward": cls[dom][1] / tot_ms,
-        "classes_ms_share": {k: round(v[1] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][1])},
-        "whole_forward_tflops": sum(v[0] for v in cls.values()) / (tot_ms / 1e3) / 1e12,
-    }
 
     # ---- end to end through the host-pointer C ABI ----
     e2e = None
@@ -265,14 +290,14 @@ def main():
                     raise RuntimeError(be.lib.scb_last_error(be.ctx).decode())
 
         e2e_step()
-        barrier()
+        job.barrier()
         t = time.perf_counter()
         for _ in range(a.steps):
             e2e_step()
         dt = (time.perf_counter() - t) / a.steps
-        dt = max_over_ranks(dt)
-        e2e = {"value": mp_step / dt, "unit": "MP/s", "h2d_bytes_per_step": int(hx.numel()),
-               "d2h_bytes_per_step": int(hy.numel() * 4), "api": "scb_forward_host (pinned host buffers)"}
+        dt = job.max_over_ranks(dt)
+        e2e = {"value": mp_step / dt, "unit": "MP/s", "h2d_bytes_per_step": int(hx.numel()) * world,
+               "d2h_bytes_per_step": int(hy.numel() * 4) * world, "api": "scb_forward_host (pinned host buffers)"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -296,8 +321,107 @@ def main():
             "roofline": roofline, "cpu_baseline": cpu,
         }), flush=True)
     be.close()
+
+
+def band_workload(a, job, scb):
+    """Config 5: one image, one row band per rank, halo exchange inside the forward."""
+    torch, dist = job.torch, job.dist
+    rank, world, local = job.rank, job.world, job.local
+    S = a.size
+    wt = scb.Weights.seeded(3, 0)
+    be = scb.B200(wt, device=local)
+    # Rank 0 makes the image on its GPU and broadcasts it over NCCL; every rank
+    # passes the whole image to scb_forward_band and computes its own band.
+    x_dev = torch.empty((1, C, S, S), dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        x_dev.copy_(scb.synth.noisy_image_device(1005, C, S, S, 25.0 / 255.0, device="cuda"))
+    uid = [scb.band_unique_id() if rank == 0 else None]
     if world > 1:
-        dist.destroy_process_group()
+        dist.broadcast(x_dev, 0)
+        dist.broadcast_object_list(uid, 0)
+    be.band_init(uid[0], rank, world)
+    y_dev = torch.empty((1, C, S, S), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    assert sp != 0
+    hp = (S + 63) // 64 * 64
+    r0, rows = scb.shard.band_rows(hp, rank, world)
+    rows = max(0, min(rows, S - r0))
+
+    def step():
+        be.forward_band(x_dev.data_ptr(), scb.SCB_U8, C, S, S, y_dev.data_ptr(), scb.SCB_F32, sp)
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    launches_per_call = be.last_launch_count()
+    ms, clocks = job.timed(step, a.steps, stream)
+    mp_step = S * S / 1e6
+    value = mp_step / (ms / 1e3)
+
+    # Profile one banded forward (every rank runs it: the halo exchange pairs them).
+    be.set_profiling(True)
+    step()
+    torch.cuda.synchronize()
+    roofline = roofline_from_profile(be.profile())
+    be.set_profiling(False)
+    job.barrier()
+
+    e2e = None
+    if not a.no_e2e:
+        # Host image in, this rank's output rows out, copies on the compute stream.
+        hx = torch.empty((1, C, S, S), dtype=torch.uint8).pin_memory()
+        hx.copy_(x_dev.cpu())
+        hy = torch.empty((1, C, rows, S), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                x_dev.copy_(hx, non_blocking=True)
+                step()
+                hy.copy_(y_dev[:, :, r0:r0 + rows], non_blocking=True)
+            stream.synchronize()
+
+        e2e_step()
+        job.barrier()
+        t = time.perf_counter()
+        for _ in range(a.steps):
+            e2e_step()
+        dt = job.max_over_ranks((time.perf_counter() - t) / a.steps)
+        e2e = {"value": mp_step / dt, "unit": "MP/s", "h2d_bytes_per_step": int(hx.numel()) * world,
+               "d2h_bytes_per_step": S * S * C * 4,
+               "api": "scb_forward_band (image copied from pinned host memory to every rank, band rows back)"}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": "megapixels/sec (device-timed, max over ranks)", "value": value, "unit": "MP/s",
+            "n_gpus": world, "steps": a.steps, "warmup": max(a.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded config-5 image generated on the GPU; seeded weights)",
+            "config": {"workload": f"config5: one {S}x{S} RGB uint8 image in 64-row-aligned row bands",
+                       "bands": world, "rows_per_band_rank0": rows,
+                       "parallelism": f"row bands over {world} GPU(s), halo rows by NCCL send/recv",
+                       "l2": "inputs larger than L2 (one forward streams %.0f GB of activations)" % (
+                           scb.need_bytes(1, 3, hp, hp) / 1e9),
+                       "arith": "fp16 tensor-core operands, fp32 accumulate and residual stream"},
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_call * a.steps,
+            "roofline": roofline, "cpu_baseline": None,
+        }), flush=True)
+    be.close()
+
+
+def main():
+    a = args_()
+    rank, world, local = dist_env()
+    if a.impl == "reference":
+        reference_arm(a, rank, world)
+        return
+    scb = importlib.import_module("scunet-rs_b200")
+    job = Job(a)
+    try:
+        (band_workload if a.workload == "band" else frames_workload)(a, job, scb)
+    finally:
+        job.close()
 
 
 if __name__ == "__main__":

@@ -194,7 +194,7 @@ int scb_set_profiling(scb_ctx* ctx, int on);
 
 /* For the last profiled forward: per launch, its op class (0 head, 1 tail,
  * 2 conv1x1, 3 conv3x3, 4 qkv, 5 attention, 6 proj, 7 mlp0, 8 mlp2, 9 down,
- * 10 up, 11 fused transformer half), its algorithmic FLOPs and its device time in ms (waits for the
+ * 10 up, 11 fused transformer half, 12 band halo exchange or edge-halo clear), its algorithmic FLOPs and its device time in ms (waits for the
  * events). Returns the number of entries written (<= max). */
 int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max);
 

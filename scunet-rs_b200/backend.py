@@ -33,7 +33,7 @@ SYMBOLS = [
 ]
 SCB_OPT_FUSE_TRANS = 1
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
-              "trans_fused"]
+              "trans_fused", "halo"]
 
 
 class BackendError(RuntimeError):

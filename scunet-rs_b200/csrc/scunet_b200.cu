@@ -440,7 +440,7 @@ const int kStageLevel[7] = {0, 1, 2, 3, 2, 1, 0};
 // classes (docs/TECH_NOTES.md:346-367).
 enum OpTag : int {
   TAG_HEAD = 0, TAG_TAIL = 1, TAG_CONV1X1 = 2, TAG_CONV3X3 = 3, TAG_QKV = 4, TAG_ATTN = 5, TAG_PROJ = 6,
-  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10, TAG_TRANS = 11
+  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10, TAG_TRANS = 11, TAG_HALO = 12
 };
 
 struct Op {
@@ -874,6 +874,7 @@ int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, 
 Op xchg_op(void* plane, const Region& R, int ch, int elem_bytes) {
   Op x{};
   x.kind = Op::XCHG;
+  x.tag = TAG_HALO;
   x.xchg_base = static_cast<char*>(plane);
   x.xchg_row = (size_t)R.W * ch * elem_bytes;
   x.xchg_row0 = R.row0;
@@ -1125,6 +1126,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
         const int r = side == 0 ? 0 : R.row0 + R.rows;
         Op zy{};
         zy.kind = Op::ZERO;
+        zy.tag = TAG_HALO;
         zy.zero_ptr = reinterpret_cast<char*>(A.y) + r * rb_y;
         zy.zero_bytes = edge ? kHalo * rb_y : 0;
         ops.push_back(zy);
