@@ -301,6 +301,32 @@ __device__ __forceinline__ uint32_t swz_off(uint32_t row, uint32_t chunk, uint32
 
 // 2^x, hardware approximation (relative error ~2^-22, far below the fp16 rounding
 // every consumer of these values applies).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+__device__ __forceinline__ __half2 tanh_approx_h2(__half2 x) {
+  uint32_t y;
+  asm("tanh.approx.f16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
+  return *reinterpret_cast<const __half2*>(&y);
+}
+
+// GELU on two fp16 values in the tanh form of Hendrycks & Gimpel,
+//   GELU(x) ~= x/2 (1 + tanh(x (a + b x^2))),
+// with a, b refitted (minimax over the real line) to the exact-erf GELU of
+// nn.GELU() (tools/network_scunet.py:130): a = 0.80015708, b = 0.03470089, max
+// |error| 2.7e-4 (the textbook a = sqrt(2/pi), b = 0.044715 a gives 4.7e-4). Used
+// where the result is stored as fp16 (the MLP hidden layer); six packed operations
+// and one tanh.approx.f16x2 per two values. Large |x| saturates: x^2 -> inf gives
+// tanh -> +-1 and GELU -> x or 0.
+__device__ __forceinline__ __half2 gelu_tanh_h2(__half2 x) {
+  const __half2 x2 = __hmul2(x, x);
+  const __half2 p = __hfma2(__float2half2_rn(0.03470089f), x2, __float2half2_rn(0.80015708f));
+  const __half2 t = tanh_approx_h2(__hmul2(x, p));
+  const __half2 hx = __hmul2(__float2half2_rn(0.5f), x);
+  return __hfma2(hx, t, hx);
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -370,17 +396,29 @@ struct WinGeom {
 
 __device__ __forceinline__ long win_token_pixel(const WinGeom& g, long win, int qi, int qj, bool& last_row,
                                                 bool& last_col, bool& store) {
-  const long per_img = (long)g.nwr * g.nwc;
-  const long img = win / per_img;
-  const int wrem = (int)(win - img * per_img);
-  const int wr = wrem / g.nwc, wc = wrem - wr * g.nwc;
-  const int y = g.wrap ? (wr * 8 + qi + g.shift) % g.H : g.row_base + wr * 8 + qi;
-  const int x = (wc * 8 + qj + g.shift) % g.W;
-  const int gwr = (g.gwr0 + wr) % g.nwr_global;
+  // 32-bit index arithmetic: a plane that fits in device memory holds far fewer than
+  // 2^31 windows; every wrapped coordinate is below twice its period, so one
+  // conditional subtraction replaces the modulo
+  const unsigned per_img = (unsigned)(g.nwr * g.nwc);
+  const unsigned w = (unsigned)win;
+  const unsigned img = w / per_img;
+  const unsigned wrem = w - img * per_img;
+  const int wr = (int)(wrem / (unsigned)g.nwc), wc = (int)wrem - wr * g.nwc;
+  int y;
+  if (g.wrap) {
+    y = wr * 8 + qi + g.shift;
+    if (y >= g.H) y -= g.H;
+  } else {
+    y = g.row_base + wr * 8 + qi;
+  }
+  int x = wc * 8 + qj + g.shift;
+  if (x >= g.W) x -= g.W;
+  int gwr = g.gwr0 + wr;
+  if (gwr >= g.nwr_global) gwr -= g.nwr_global;
   last_row = g.shift && gwr == g.nwr_global - 1;
   last_col = g.shift && wc == g.nwc - 1;
   store = y >= g.store_lo && y < g.store_hi;
-  return (img * g.H + y) * g.W + x;
+  return ((long)img * g.H + y) * g.W + x;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

@@ -33,6 +33,7 @@
 #include "gemm.cuh"
 #include "io_kernels.cuh"
 #include "trans.cuh"
+#include "trans32.cuh"
 
 using namespace scb;
 
@@ -707,8 +708,24 @@ cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
+  using L = Trans32Layout;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(trans32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long pairs = (op.trans.win.n_windows + 1) / 2;
+  const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
+  trans32_kernel<<<grid, 256, L::SMEM, st>>>(op.trans);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
-  if (op.trans_t == 32) return launch_trans_t<32>(op, sms, st);
+  if (op.trans_t == 32) return launch_trans32(op, sms, st);
   if (op.trans_t == 64) return launch_trans_t<64>(op, sms, st);
   return cudaErrorInvalidConfiguration;
 }
