@@ -176,7 +176,7 @@ def roofline_from_profile(prof):
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(dom)
     return {
-        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans_fused_kernel",
+        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans32_kernel + trans64_kernel",
                    "head": "head_tc_kernel", "tail": "tail_conv_kernel"}.get(dom, f"gemm_tc_kernel [{dom}]"),
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,

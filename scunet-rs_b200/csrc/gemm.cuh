@@ -103,7 +103,6 @@ struct EpiMaps {
   CUtensorMap res16, res32, skip, out16, out32;
 };
 
-__device__ __forceinline__ float gelu_erf(float x) { return gelu_as(x); }
 
 // One 16-column chunk of a row's residual inputs, loaded ahead of use.
 struct ResChunk {
@@ -404,7 +403,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           // the GELU output is an fp16 operand: evaluate it in packed half2
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const __half2 gv = gelu_as_h2(__floats2half2_rn(v[j], v[j + 1]));
+            const __half2 gv = gelu_tanh_h2(__floats2half2_rn(v[j], v[j + 1]));
             const float2 f = __half22float2(gv);
             v[j] = f.x;
             v[j + 1] = f.y;
@@ -513,8 +512,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
         } else if (e.act == ACT_GELU) {
+          // the GELU output is an fp16 operand: evaluate it in packed half2
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
+          for (int j = 0; j < 16; j += 2) {
+            const float2 f = __half22float2(gelu_tanh_h2(__floats2half2_rn(v[j], v[j + 1])));
+            v[j] = f.x;
+            v[j + 1] = f.y;
+          }
         }
         if (p >= 0 && e.nchw_out != nullptr && c == 0) {
           const long hw = (long)g.H * g.W;

@@ -339,43 +339,6 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// GELU with the exact-erf definition (nn.GELU(), tools/network_scunet.py:130),
-// erf evaluated by Abramowitz & Stegun 7.1.26 (|erf error| <= 1.5e-7; the same
-// approximation the reference's CPU backend uses, src/cpu.rs:313-332). Max
-// |GELU error| 2.1e-7 over the real line, below the fp16 rounding of its output.
-__device__ __forceinline__ float gelu_as(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
-  const float poly =
-      t * fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f);
-  const float e = ex2_approx(-1.4426950408889634f * z * z);
-  const float erf_abs = fmaf(-poly, e, 1.0f);
-  const float erfv = copysignf(erf_abs, x);
-  return 0.5f * x * (1.0f + erfv);
-}
-
-// The same GELU on two fp16 values at once (packed half2 arithmetic). Used where
-// the result is stored as fp16 anyway (the MLP hidden): its extra error is of the
-// order of that fp16 rounding (measured through the whole network: max |diff| vs
-// fp32 1.03e-3 instead of 0.96e-3 at 256x256).
-__device__ __forceinline__ __half2 gelu_as_h2(__half2 x) {
-  const __half2 z = __hmul2(__habs2(x), __float2half2_rn(0.70710678118654752f));
-  const __half2 t = h2rcp(__hfma2(__float2half2_rn(0.3275911f), z, __float2half2_rn(1.0f)));
-  __half2 p = __hfma2(__float2half2_rn(1.061405429f), t, __float2half2_rn(-1.453152027f));
-  p = __hfma2(p, t, __float2half2_rn(1.421413741f));
-  p = __hfma2(p, t, __float2half2_rn(-0.284496736f));
-  p = __hfma2(p, t, __float2half2_rn(0.254829592f));
-  p = __hmul2(p, t);
-  const __half2 e = h2exp2(__hmul2(__hmul2(z, z), __float2half2_rn(-1.4426950408889634f)));
-  const __half2 erf_abs = __hfma2(__hneg2(p), e, __float2half2_rn(1.0f));
-  uint32_t ea = *reinterpret_cast<const uint32_t*>(&erf_abs);
-  const uint32_t xs = *reinterpret_cast<const uint32_t*>(&x) & 0x80008000u;
-  ea = (ea & 0x7fff7fffu) | xs;
-  const __half2 erfv = *reinterpret_cast<const __half2*>(&ea);
-  const __half2 half = __float2half2_rn(0.5f);
-  return __hmul2(x, __hfma2(half, erfv, half));
-}
-
 // Where the tokens of 8x8 (shifted) windows live in a stored plane. Token (i, j)
 // of window (wr, wc) is pixel (row, (8 wc + j + shift) mod W) with
 //   wrap = 1 (the whole image): row = (8 wr + i + shift) mod H - the cyclic roll

@@ -34,6 +34,7 @@
 #include "io_kernels.cuh"
 #include "trans.cuh"
 #include "trans32.cuh"
+#include "trans64.cuh"
 
 using namespace scb;
 
@@ -691,23 +692,6 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
 
 cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* out32, __half* out16, cudaStream_t st);
 
-template <int T>
-cudaError_t launch_trans_t(const Op& op, int sms, cudaStream_t st) {
-  using L = TransLayout<T>;
-  static bool attr_set[16] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 16 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(trans_fused_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
-  const long pairs = (op.trans.win.n_windows + 1) / 2;
-  const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
-  trans_fused_kernel<T><<<grid, 256, L::SMEM, st>>>(op.trans);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
   using L = Trans32Layout;
   static bool attr_set[16] = {false};
@@ -724,9 +708,25 @@ cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+cudaError_t launch_trans64(const Op& op, int sms, cudaStream_t st) {
+  using L = Trans64Layout;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(trans64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long pairs = (op.trans.win.n_windows + 1) / 2;
+  const int grid = (int)std::max(1L, std::min((pairs + 1) / 2, (long)sms));  // two pair pipelines per CTA
+  trans64_kernel<<<grid, 512, L::SMEM, st>>>(op.trans);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
   if (op.trans_t == 32) return launch_trans32(op, sms, st);
-  if (op.trans_t == 64) return launch_trans_t<64>(op, sms, st);
+  if (op.trans_t == 64) return launch_trans64(op, sms, st);
   return cudaErrorInvalidConfiguration;
 }
 

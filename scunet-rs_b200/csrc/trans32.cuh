@@ -1,11 +1,11 @@
 // The transformer half of a full-resolution ConvTransBlock (trans width T = 32, one
-// head) in one kernel: the computation of trans_fused_kernel<32> (trans.cuh), laid
-// out so that three CTAs fit on an SM, with fewer instructions per token.
+// head) in one kernel per launch; the common structure and semantics are described
+// in trans.cuh. This kernel is laid out so that three CTAs fit on an SM:
 //
 //   x  = y_t;  x1 = x + proj(WMSA(LN1(x)));  z = x1 + mlp2(GELU(mlp0(LN2(x1))))
 //   (tools/network_scunet.py:128-136)
 //
-// What changes against the generic kernel:
+// Layout and schedule:
 //  * TMEM: 128 columns. Each accumulator is read out before the next MMA that
 //    overwrites it is issued, so qkv [0, 96), S [0, 128), O' [0, 64) and proj [0, 32)
 //    share columns; the MLP output accumulates on top of proj (cols 0-31) and the
@@ -24,7 +24,7 @@
 //    window row or column (a warp's 32 tokens share one window).
 //
 // z = acc + y_t + b_proj + b_2 with acc = O.Wproj^T + GELU(hid).W2^T accumulated in
-// fp32 in TMEM: the same sums as x1 + mlp in the generic kernel.
+// fp32 in TMEM, i.e. x1 + mlp with x1 = y_t + proj + b_proj.
 #pragma once
 #include "trans.cuh"
 

@@ -55,7 +55,9 @@ def test_gemm(be3, M, K, N, act, res):
     rc = be3.lib.scb_probe_gemm(be3.ctx, ta.data_ptr(), M, K, tb.data_ptr(), N, tbias.data_ptr(), act,
                                 tr.data_ptr() if res else None, o16.data_ptr(), o32.data_ptr())
     assert rc == 0, be3.lib.scb_last_error(be3.ctx)
-    close(f"gemm {M}x{K}x{N} f32", ref, o32.cpu().numpy(), 1e-5)
+    # a GELU epilogue evaluates GELU in packed fp16 (its output is an fp16 operand),
+    # so with act = 2 the f32 output carries fp16 accuracy too
+    close(f"gemm {M}x{K}x{N} f32", ref, o32.cpu().numpy(), 2e-3 if act == 2 else 1e-5)
     close(f"gemm {M}x{K}x{N} f16", ref, o16.float().cpu().numpy(), 2e-3)
 
 
