@@ -92,15 +92,16 @@ struct GemmEpi {
   int nchw_c, nchw_h, nchw_w, nchw_u8;
   int nchw_row_off;  // image row of stored row y is y + nchw_row_off
   // TMA epilogue: staging offsets (bytes within one buffer) of each stream's
-  // [128 x 32-column] slab; -1 = stream absent.
-  int st_res16, st_res32, st_skip, st_out16, st_out32;
+  // [128 x 32-column] slab; -1 = stream absent. st_ln: the LayerNorm output slab
+  // (GEO_FLAT, no activation, fp16 residual at most).
+  int st_res16, st_res32, st_skip, st_out16, st_out32, st_ln;
   int st_res_bytes, st_out_bytes;  // bytes of one buffer of all residual / output slabs
 };
 
 // Tensor maps of the epilogue streams (TMA epilogue only); box = 32 columns x the
 // M tile's pixel block.
 struct EpiMaps {
-  CUtensorMap res16, res32, skip, out16, out32;
+  CUtensorMap res16, res32, skip, out16, out32, lnout;
 };
 
 
@@ -378,6 +379,49 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+      // LayerNorm statistics of this row over the tile's LN columns, from the
+      // accumulator (+ bias + fp16 residual, re-read from global memory here), with
+      // a shifted sum of squares
+      const bool do_ln = e.st_ln >= 0 && e.ln_lo >= n0 && e.ln_lo < n0 + BN;
+      float ln_mean = 0.f, ln_rstd = 0.f;
+      if (GEO == GEO_FLAT && do_ln) {
+        const long p = (long)mt * 128 + r;
+        float shift = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll 1
+        for (int c = e.ln_lo - n0; c < e.ln_lo - n0 + e.ln_n; c += 32) {
+          float v[32];
+          tmem_ld16x2(tbase + c, v, tbase + c + 16, v + 16);
+          if (e.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __ldg(e.bias + n0 + c + j);
+          }
+          if (e.res16 && p < g.M) {
+            const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + n0 + c);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const uint4 u = __ldg(src + h);
+              const __half2* hp = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(hp[i]);
+                v[8 * h + 2 * i] += f.x;
+                v[8 * h + 2 * i + 1] += f.y;
+              }
+            }
+          }
+          if (c == e.ln_lo - n0) shift = v[0];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float d = v[j] - shift;
+            s1 += d;
+            s2 += d * d;
+          }
+        }
+        const float inv_n = 1.f / (float)e.ln_n;
+        const float md = s1 * inv_n;
+        ln_mean = shift + md;
+        ln_rstd = rsqrtf(fmaxf(s2 * inv_n - md * md, 0.f) + 1e-5f);
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32, ++os) {
         if (has_res && elected) {
@@ -454,6 +498,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             *reinterpret_cast<float4*>(ob + e.st_out32 + swz_off(r, j, 128)) =
                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
+        const bool ln_slab = do_ln && n >= e.ln_lo && n < e.ln_lo + e.ln_n;
+        if (ln_slab) {
+          const float* lg = e.ln_g + (n - e.ln_lo);
+          const float* lb = e.ln_b + (n - e.ln_lo);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (v[8 * j + i] - ln_mean) * ln_rstd * __ldg(lg + 8 * j + i) + __ldg(lb + 8 * j + i);
+            *reinterpret_cast<uint4*>(ob + e.st_ln + swz_off(r, j, 64)) =
+                make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+          }
+        }
         if (e.st_out16 >= 0) {
           if (e.st_skip >= 0) {
 #pragma unroll
@@ -470,6 +527,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (elected) {
           if (e.st_out32 >= 0) epi_slab_store<GEO>(&em.out32, ob + e.st_out32, n, mt, g);
           if (e.st_out16 >= 0) epi_slab_store<GEO>(&em.out16, ob + e.st_out16, n, mt, g);
+          if (ln_slab) epi_slab_store<GEO>(&em.lnout, ob + e.st_ln, n - e.ln_lo, mt, g);
           bulk_commit_group();
         }
       }

@@ -170,6 +170,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_TCASE(128, 64, GEO_FLAT)
   SCB_GEMM_TCASE(192, 64, GEO_FLAT)
   SCB_GEMM_TCASE(256, 64, GEO_FLAT)
+  SCB_GEMM_TCASE(128, 32, GEO_FLAT)
   SCB_GEMM_TCASE(32, 32, GEO_CONV3X)
   SCB_GEMM_TCASE(64, 64, GEO_CONV3X)
   SCB_GEMM_TCASE(128, 64, GEO_CONV3X)
@@ -199,7 +200,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
 
 bool tma_epi_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{64, 64, GEO_FLAT},   {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
-                               {32, 32, GEO_CONV3X}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
+                               {128, 32, GEO_FLAT},  {32, 32, GEO_CONV3X}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
                                {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}};
   for (auto& r : tab)
     if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
@@ -215,6 +216,17 @@ bool gemm_supported(int geo, int bn, int bk) {
   for (auto& r : tab)
     if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
   return false;
+}
+
+// Tile width of a 1x1 (flat) GEMM: at most 128 columns, so that the tile's two TMEM
+// accumulators (2 BN columns) leave room for a second CTA on the SM: these GEMMs are
+// memory-bound with short K, and one CTA per SM leaves only four epilogue warps to
+// drain the accumulators. `min_bn` widens it where a LayerNorm epilogue needs its
+// whole row range inside one tile.
+int pick_bn_flat(int N, int min_bn) {
+  int bn = (N == 32 || N == 64 || N == 96 || N == 128) ? N : (N % 128 == 0) ? 128 : (N % 64 == 0) ? 64 : 32;
+  while (bn < min_bn && N % (2 * bn) == 0 && 2 * bn <= 256) bn *= 2;
+  return bn;
 }
 
 int pick_bn(int N) {
@@ -250,11 +262,13 @@ struct Maker {
   }
 
   // Plain GEMM over M rows of an fp16 [M][lda] matrix (first K columns).
-  bool flat(GemmOp& op, const __half* a, long M, int K, long lda, const __half* w, int N, int geo = GEO_FLAT) {
+  // `bk32`: 32-wide K blocks where the tile is 128 columns wide (half the
+  // pipeline-stage bytes, for epilogues whose staging leaves little shared memory).
+  bool flat(GemmOp& op, const __half* a, long M, int K, long lda, const __half* w, int N, int geo = GEO_FLAT,
+            int min_bn = 0, bool bk32 = false) {
     op.geo = geo;
-    op.bk = (K % 64 == 0) ? 64 : 32;
-    op.bn = pick_bn(N);
-    if (geo == GEO_UP2) op.bn = std::min(op.bn, op.g.up_cout);
+    op.bn = geo == GEO_UP2 ? std::min(pick_bn(N), op.g.up_cout) : pick_bn_flat(N, min_bn);
+    op.bk = (K % 64 == 0 && !(bk32 && op.bn == 128)) ? 64 : 32;
     if (!gemm_supported(op.geo, op.bn, op.bk) || K % 32 || N % op.bn) {
       *err = "no GEMM variant for N=" + std::to_string(N) + " K=" + std::to_string(K);
       return false;
@@ -381,10 +395,17 @@ struct Maker {
   // build its stream maps and staging layout.
   bool finish_epi(GemmOp& op) {
     GemmEpi& e = op.e;
-    e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = -1;
+    e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = e.st_ln = -1;
     e.st_res_bytes = e.st_out_bytes = 0;
     op.tma_epi = false;
-    if (e.ln_out || e.nchw_out || op.geo == GEO_UP2 || !tma_epi_supported(op.geo, op.bn, op.bk)) return true;
+    if (e.ln_out && (e.ln_lo % op.bn) + e.ln_n > op.bn) {
+      *err = "LayerNorm columns [" + std::to_string(e.ln_lo) + ", +" + std::to_string(e.ln_n) + ") span two " +
+             std::to_string(op.bn) + "-column tiles";
+      return false;
+    }
+    // the TMA epilogue's LayerNorm: flat GEMMs without activation, fp16 residual at most
+    const bool ln_tma = !e.ln_out || (op.geo == GEO_FLAT && e.act == ACT_NONE && !e.res32 && !e.skip32);
+    if (!ln_tma || e.nchw_out || op.geo == GEO_UP2 || !tma_epi_supported(op.geo, op.bn, op.bk)) return true;
     const int N = op.g.n_total;
     int off = 0;
     if (e.res16) {
@@ -412,6 +433,11 @@ struct Maker {
     if (e.out16) {
       if (!stream_map(op, &op.em.out16, e.out16, e.out16_ld, N, 2)) return false;
       e.st_out16 = off;
+      off += 128 * 64;
+    }
+    if (e.ln_out) {
+      if (!stream_map(op, &op.em.lnout, e.ln_out, e.ln_ld, e.ln_n, 2)) return false;
+      e.st_ln = off;
       off += 128 * 64;
     }
     e.st_out_bytes = off;
@@ -944,7 +970,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
   {
     GemmOp g{};
-    if (!mk.flat(g, xs + R.off(c), P, c, c, bw.w11, c)) return false;
+    if (!mk.flat(g, xs + R.off(c), P, c, c, bw.w11, c, GEO_FLAT, fused ? 0 : t)) return false;
     g.e.bias = bw.b11;
     g.e.out16 = A.y + R.off(c);
     g.e.out16_ld = c;
@@ -1045,7 +1071,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     // 6. x1t = o Wp^T + b + y_t -> z[:, cc:]; LN2(x1t) -> A
     {
       GemmOp g{};
-      if (!mk.flat(g, A.o + R.off(t), P, t, t, bw.wproj, t)) return false;
+      if (!mk.flat(g, A.o + R.off(t), P, t, t, bw.wproj, t, GEO_FLAT, t, true)) return false;
       g.e.bias = bw.bproj;
       g.e.res16 = A.y + R.off(c) + cc;
       g.e.res16_ld = c;
