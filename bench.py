@@ -13,7 +13,9 @@ One JSON line on rank 0. `value` is device-timed (CUDA events on the launch
 stream, max over ranks) with inputs resident in HBM; `e2e` is the same metric
 through the host-pointer C-ABI call `scb_forward_host` (pinned host uint8 in,
 float32 out, copies inside the timed region). `roofline` is the dominant op class
-from a live per-launch event profile (`scb_set_profiling`). `cpu_baseline` times
+from a live per-launch event profile (`scb_set_profiling` / `scb_profile_bytes`),
+against HBM or the tensor pipe by its arithmetic intensity, with the DRAM traffic
+ncu measured for it (`profiles/traffic.json`, written by `--ncu-traffic`). `cpu_baseline` times
 the CPU oracle (`oracle/scunet_np.py`, the reference's algorithm restated in
 numpy) on a bounded crop.
 
@@ -63,6 +65,9 @@ def args_():
     ap.add_argument("--micro", type=int, default=4, help="frames per library call")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-traffic", metavar="CSV",
+                    help="write profiles/traffic.json from an ncu capture of one 1-frame forward and exit")
+    ap.add_argument("--ncu-launches", metavar="CSV", help="print a per-kernel launch table of an ncu capture and exit")
     return ap.parse_args()
 
 
@@ -158,32 +163,133 @@ def reference_arm(a, rank, world):
     }), flush=True)
 
 
-def roofline_from_profile(prof):
-    """The dominant op class of one profiled forward against the tensor peak."""
+KERNEL_OF_CLASS = {"attention": "window_attn_kernel", "trans_fused": "trans32_kernel + trans64_kernel",
+                   "head": "head_tc_kernel"}
+
+
+def class_totals(prof):
+    """{class: [flops, bytes, ms, launches]} over one profiled forward."""
     cls = {}
-    for name, fl, t in prof:
-        c = cls.setdefault(name, [0.0, 0.0, 0])
+    for name, fl, nb, t in prof:
+        c = cls.setdefault(name, [0.0, 0.0, 0.0, 0])
         c[0] += fl
-        c[1] += t
-        c[2] += 1
-    tot_ms = sum(v[1] for v in cls.values())
-    dom = max((k for k in cls if k != "halo"), key=lambda k: cls[k][1])
+        c[1] += nb
+        c[2] += t
+        c[3] += 1
+    return cls
+
+
+def roofline_from_profile(prof, frames_per_call):
+    """The dominant op class of one profiled forward against its roofline: HBM when
+    its arithmetic intensity is below the ridge point of the measured peaks, the
+    tensor pipe otherwise. `achieved` = the class's algorithmic bytes (or FLOPs) per
+    launch / its average launch time; `traffic` = measured DRAM bytes per launch
+    (profiles/traffic.json, an ncu capture of a one-frame forward scaled to
+    `frames_per_call` frames)."""
+    cls = class_totals(prof)
+    tot_ms = sum(v[2] for v in cls.values())
+    dom = max((k for k in cls if k != "halo"), key=lambda k: cls[k][2])
+    fl, nb, ms, n = cls[dom]
     pk, pk_kind = peaks()
-    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
-    achieved = cls[dom][0] / (cls[dom][1] / 1e3) / 1e12
+    tflops = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    hbm = float(pk["hbm_gbs"])
+    ridge = tflops * 1e12 / (hbm * 1e9)
+    memory_bound = fl / max(nb, 1.0) < ridge
+    t_launch = ms / n / 1e3
+    if memory_bound:
+        achieved, peak, unit, bound = nb / n / t_launch / 1e9, hbm, "GB/s", "hbm"
+        src = f"{pk_kind} HBM copy bandwidth"
+    else:
+        achieved, peak, unit, bound = fl / n / t_launch / 1e12, tflops, "TFLOP/s", "tensor"
+        src = f"{pk_kind} bf16/fp16 dense sustained"
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get(dom)
+        d = json.loads(tf.read_text())
+        c = d.get("classes", {}).get(dom)
+        if c:
+            traffic = c["dram_bytes"] / c["launches"] * frames_per_call / d.get("frames_per_call", 1)
     return {
-        "kernel": {"attention": "window_attn_kernel", "trans_fused": "trans32_kernel + trans64_kernel",
-                   "head": "head_tc_kernel", "tail": "tail_conv_kernel"}.get(dom, f"gemm_tc_kernel [{dom}]"),
-        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-        "peak_source": f"{pk_kind} bf16/fp16 dense sustained", "traffic": traffic,
-        "launches": cls[dom][2], "share_of_forward": cls[dom][1] / tot_ms,
-        "classes_ms_share": {k: round(v[1] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][1])},
+        "kernel": KERNEL_OF_CLASS.get(dom, f"gemm_tc_kernel [{dom}]"), "class": dom,
+        "bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+        "peak_source": src, "traffic": traffic, "algorithmic_bytes_per_launch": nb / n,
+        "flops_per_launch": fl / n, "launches": n, "share_of_forward": ms / tot_ms,
+        "classes_ms_share": {k: round(v[2] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][2])},
         "whole_forward_tflops": sum(v[0] for v in cls.values()) / (tot_ms / 1e3) / 1e12,
     }
+
+
+def read_ncu_csv(path):
+    """ncu --csv --log-file output -> [(kernel name, {metric: value})] in launch order."""
+    import csv
+    rows = list(csv.reader(l for l in Path(path).read_text().splitlines() if l.startswith('"')))
+    h = rows[0]
+    iid, iname, im, iv = h.index("ID"), h.index("Kernel Name"), h.index("Metric Name"), h.index("Metric Value")
+    launches = {}
+    for r in rows[1:]:
+        d = launches.setdefault(int(r[iid]), [r[iname], {}])
+        d[1][r[im]] = float(r[iv].replace(",", ""))
+    return [launches[k] for k in sorted(launches)]
+
+
+def ncu_launch_summary(path):
+    """Markdown table: per kernel, launches, total device time and share."""
+    ls = read_ncu_csv(path)
+    per = {}
+    for name, m in ls:
+        k = name.split("(")[0]
+        t = m.get("gpu__time_duration.sum", 0.0)
+        e = per.setdefault(k, [0, 0.0])
+        e[0] += 1
+        e[1] += t
+    tot = sum(v[1] for v in per.values())
+    out = ["| kernel | launches | total (ms) | share |", "|---|---|---|---|"]
+    for k, (n, t) in sorted(per.items(), key=lambda kv: -kv[1][1]):
+        out.append(f"| `{k}` | {n} | {t / 1e6:.3f} | {100 * t / tot:.1f} % |")
+    out.append(f"| all | {len(ls)} | {tot / 1e6:.3f} | |")
+    return "\n".join(out)
+
+
+def ncu_traffic(path):
+    """Align an ncu capture of one 1-frame forward (gpu__time_duration.sum,
+    dram__bytes_read.sum, dram__bytes_write.sum per launch) with a profiled forward of
+    the same configuration; write profiles/traffic.json; print the per-class table."""
+    import torch
+    scb = importlib.import_module("scunet-rs_b200")
+    ls = read_ncu_csv(path)
+    be = scb.B200(scb.Weights.seeded(3, 0), device=0)
+    fr = torch.from_numpy(scb.synth.frames(4000, 1, H, W)).cuda()
+    y = torch.empty((1, C, H, W), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    be.set_profiling(True)
+    be.forward_dev(fr.data_ptr(), scb.SCB_U8, 1, C, H, W, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
+    torch.cuda.synchronize()
+    prof = be.profile()
+    be.close()
+    if len(prof) != len(ls):
+        raise SystemExit(f"{len(ls)} captured launches, {len(prof)} ops in a forward")
+    cls = {}
+    for (name, m), (c, fl, nb, ms) in zip(ls, prof):
+        e = cls.setdefault(c, {"launches": 0, "dram_bytes": 0.0, "algorithmic_bytes": 0.0, "flops": 0.0,
+                               "ncu_ms": 0.0, "kernels": set()})
+        e["launches"] += 1
+        e["dram_bytes"] += m["dram__bytes_read.sum"] + m["dram__bytes_write.sum"]
+        e["algorithmic_bytes"] += nb
+        e["flops"] += fl
+        e["ncu_ms"] += m["gpu__time_duration.sum"] / 1e6
+        e["kernels"].add(name.split("(")[0].split("<")[0].replace("void ", ""))
+    for e in cls.values():
+        e["kernels"] = sorted(e["kernels"])
+    out = {"workload": "one 1920x1080 frame per call (padded 1920x1088), config-4 frame, seeded weights",
+           "frames_per_call": 1, "classes": cls}
+    (ROOT / "profiles" / "traffic.json").write_text(json.dumps(out, indent=1) + "\n")
+    lines = ["| class | launches | kernels | DRAM bytes / algorithmic | DRAM MB per launch | ncu ms (serialised) |",
+             "|---|---|---|---|---|---|"]
+    for c, e in sorted(cls.items(), key=lambda kv: -kv[1]["ncu_ms"]):
+        lines.append(f"| {c} | {e['launches']} | {', '.join(e['kernels'])} | "
+                     f"{e['dram_bytes'] / max(e['algorithmic_bytes'], 1):.2f} | "
+                     f"{e['dram_bytes'] / e['launches'] / 1e6:.1f} | {e['ncu_ms']:.3f} |")
+    print("\n".join(lines))
 
 
 class Job:
@@ -273,7 +379,7 @@ def frames_workload(a, job, scb):
     be.set_profiling(True)
     be.forward_dev(x_dev[0].data_ptr(), scb.SCB_U8, micro, C, H, W, y_dev[0].data_ptr(), scb.SCB_F32, sp)
     torch.cuda.synchronize()
-    roofline = roofline_from_profile(be.profile())
+    roofline = roofline_from_profile(be.profile(), micro)
     be.set_profiling(False)
 
     # ---- end to end through the host-pointer C ABI ----
@@ -364,7 +470,8 @@ def band_workload(a, job, scb):
     be.set_profiling(True)
     step()
     torch.cuda.synchronize()
-    roofline = roofline_from_profile(be.profile())
+    roofline = roofline_from_profile(be.profile(), 1)
+    roofline["traffic"] = None  # traffic.json is a frame capture, not a band
     be.set_profiling(False)
     job.barrier()
 
@@ -412,6 +519,12 @@ def band_workload(a, job, scb):
 
 def main():
     a = args_()
+    if a.ncu_launches:
+        print(ncu_launch_summary(a.ncu_launches))
+        return
+    if a.ncu_traffic:
+        ncu_traffic(a.ncu_traffic)
+        return
     rank, world, local = dist_env()
     if a.impl == "reference":
         reference_arm(a, rank, world)

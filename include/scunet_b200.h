@@ -198,6 +198,11 @@ int scb_set_profiling(scb_ctx* ctx, int on);
  * events). Returns the number of entries written (<= max). */
 int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max);
 
+/* For the same launches: algorithmic HBM bytes (every operand read once, every
+ * result written once, weights included), the numerator of a memory roofline. No
+ * counterpart in the reference, whose profile reports times only. */
+int scb_profile_bytes(const scb_ctx* ctx, double* bytes, int max);
+
 #ifdef __cplusplus
 }
 #endif

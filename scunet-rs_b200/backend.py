@@ -29,7 +29,7 @@ SYMBOLS = [
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
-    "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band",
+    "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes",
 ]
 SCB_OPT_FUSE_TRANS = 1
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
@@ -69,6 +69,7 @@ def load_library(path=None):
     lib.scb_band_unique_id.argtypes = [vp]
     lib.scb_band_init.argtypes = [vp, vp, i, i]
     lib.scb_forward_band.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
+    lib.scb_profile_bytes.argtypes = [vp, ctypes.POINTER(ctypes.c_double), i]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_footprint.restype = None
@@ -216,12 +217,15 @@ class B200:
         self._check(self.lib.scb_set_profiling(self.ctx, int(bool(on))), "scb_set_profiling")
 
     def profile(self, max_ops=4096):
-        """[(class, flops, ms)] for every launch of the last profiled forward."""
+        """[(class, flops, bytes, ms)] for every launch of the last profiled forward:
+        algorithmic FLOPs and HBM bytes, device time."""
         tags = (ctypes.c_int * max_ops)()
         flops = (ctypes.c_double * max_ops)()
+        nbytes = (ctypes.c_double * max_ops)()
         ms = (ctypes.c_float * max_ops)()
         n = self.lib.scb_profile_read(self.ctx, tags, flops, ms, max_ops)
-        return [(OP_CLASSES[tags[k]], flops[k], ms[k]) for k in range(n)]
+        self.lib.scb_profile_bytes(self.ctx, nbytes, max_ops)
+        return [(OP_CLASSES[tags[k]], flops[k], nbytes[k], ms[k]) for k in range(n)]
 
     def last_launch_count(self):
         return self.lib.scb_last_launch_count(self.ctx)

@@ -630,6 +630,7 @@ struct scb_ctx {
   std::vector<cudaEvent_t> events;
   std::vector<int> prof_tags;
   std::vector<double> prof_flops;
+  std::vector<double> prof_bytes;
   std::vector<float> prof_ms;
 };
 
@@ -876,6 +877,54 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
   return cudaErrorInvalidValue;
 }
 
+// Algorithmic HBM bytes of one launch - every operand read once, every result
+// written once, weights included: the numerator of its memory roofline.
+double op_bytes(const Arena& A, const Op& op, const Io& io) {
+  switch (op.kind) {
+    case Op::GEMM:
+    case Op::TAIL: {
+      const GemmOp& o = op.gemm;
+      const GemmGeom& g = o.g;
+      const GemmEpi& e = o.e;
+      double px = g.M, px_in = g.M;  // GEMM rows (output pixels; UP2: input pixels), pixels read
+      if (is_conv3(o.geo)) {
+        px = (double)g.M / g.H * g.rows_out;
+        px_in = px;
+      } else if (o.geo == GEO_DOWN2) {
+        px_in = 4.0 * g.M;
+      }
+      const double cin = (double)g.kb_per_tap * o.bk;
+      const double taps = is_conv3(o.geo) ? 9 : o.geo == GEO_DOWN2 ? 4 : 1;
+      const double n_cols = g.n_total;
+      double per_elem = 0;
+      if (e.out16) per_elem += 2;
+      if (e.out32) per_elem += 4;
+      if (e.res16) per_elem += 2;
+      if (e.res32) per_elem += 4;
+      if (e.skip32) per_elem += 4;
+      double b = px_in * cin * 2 + n_cols * cin * taps * 2 + px * n_cols * per_elem;
+      if (e.ln_out) b += px * e.ln_n * 2;
+      if (op.kind == Op::TAIL) b += (double)A.n * io.h * io.w * io.c * (io.y_u8 ? 1 : 4);
+      return b;
+    }
+    case Op::TRANS: {
+      const double t = op.trans_t, tokens = 64.0 * op.trans.win.n_windows;
+      return tokens * t * 2 * 2 + 12.0 * t * t * 2;
+    }
+    case Op::ATTN:
+      return 64.0 * op.attn.win.n_windows * (3.0 * op.attn.t + op.attn.t) * 2;
+    case Op::HEAD: {
+      const Region R = region_of(A, 0);
+      return (double)R.px() * (io.c * (io.x_u8 ? 1 : 4) + 64 * (4 + 2));
+    }
+    case Op::XCHG:
+      return 4.0 * kHalo * op.xchg_row;  // up to two halos sent and two received
+    case Op::ZERO:
+      return (double)op.zero_bytes;
+  }
+  return 0;
+}
+
 int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w,
             cudaStream_t st, bool allow_profile = true) {
   // (a banded arena here is one rank of a NCCL band group)
@@ -905,9 +954,11 @@ int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, 
   if (profiling) {
     ctx->prof_tags.clear();
     ctx->prof_flops.clear();
+    ctx->prof_bytes.clear();
     for (const Op& op : A.ops) {
       ctx->prof_tags.push_back(op.tag);
       ctx->prof_flops.push_back(op.flops);
+      ctx->prof_bytes.push_back(op_bytes(A, op, io));
     }
     ctx->prof_ms.assign(A.ops.size(), -1.f);  // filled by scb_profile_read after a sync
   }
@@ -1799,6 +1850,14 @@ int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max)
     if (flops) flops[i] = ctx->prof_flops[i];
     if (ms) ms[i] = t;
   }
+  return n;
+}
+
+int scb_profile_bytes(const scb_ctx* ctx, double* bytes, int max) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!ctx->profiling || ctx->prof_bytes.empty()) return 0;
+  const int n = (int)std::min<size_t>(ctx->prof_bytes.size(), (size_t)std::max(max, 0));
+  for (int i = 0; i < n && bytes; ++i) bytes[i] = ctx->prof_bytes[i];
   return n;
 }
 
