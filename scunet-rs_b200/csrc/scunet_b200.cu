@@ -1808,14 +1808,24 @@ int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes) {
 
 void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_bytes) {
   if (weights_bytes) *weights_bytes = ctx ? ctx->wbytes : 0;
-  if (scratch_bytes) *scratch_bytes = ctx ? ctx->arena.bytes : 0;
+  if (scratch_bytes) {
+    size_t s = 0;
+    if (ctx) {
+      s = ctx->arena.bytes + ctx->band_arena.bytes;
+      for (const Arena& A : ctx->vbands) s += A.bytes;
+    }
+    *scratch_bytes = s;
+  }
 }
 
 void scb_release_scratch(scb_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
-  if (ctx->arena.base) cudaFree(ctx->arena.base);
-  ctx->arena = Arena{};
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  free_arena(ctx->arena);
+  free_arena(ctx->band_arena);
+  for (Arena& A : ctx->vbands) free_arena(A);
+  ctx->vbands.clear();
 }
 
 int scb_set_option(scb_ctx* ctx, int option, int value) {
