@@ -16,8 +16,8 @@ float32 out, copies inside the timed region). `roofline` is the dominant op clas
 from a live per-launch event profile (`scb_set_profiling` / `scb_profile_bytes`),
 against HBM or the tensor pipe by its arithmetic intensity, with the DRAM traffic
 ncu measured for it (`profiles/traffic.json`, written by `--ncu-traffic`). `cpu_baseline` times
-the CPU oracle (`oracle/scunet_np.py`, the reference's algorithm restated in
-numpy) on a bounded crop.
+the CPU oracle port (`oracle/scunet_torch.py`, the reference's algorithm restated in
+torch float32, all host threads) on a bounded 512x512 crop.
 
 `--workload band` measures BASELINE.json config 5 instead: one seeded 8192x8192
 RGB uint8 image split into 64-row-aligned row bands, one band per rank
@@ -27,7 +27,7 @@ fixed as N grows (strong scaling).
 
 `--impl reference` times the reference's CPU implementation of the path. The
 reference's own CPU code is Rust and cannot be built here (no cargo, unvendored
-crates), so the arm runs the oracle port on all host cores, rank 0 only.
+crates), so the arm runs the oracle port (torch float32) on all host cores, rank 0 only.
 """
 from __future__ import annotations
 
@@ -122,43 +122,54 @@ class Clocks:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
 
 
+CPU_SAMPLE = 512  # side of the square crop of a config-4 frame the CPU legs time
+
+
 def cpu_oracle_mps(img_u8, size, reps=1):
-    """The CPU oracle on a size x size crop; returns (MP/s, seconds, threads)."""
+    """The CPU oracle port (`oracle/scunet_torch.py`: the reference forward restated
+    in torch float32, strict FP32, every host thread) on a size x size crop; returns
+    (MP/s, seconds per forward, threads)."""
     sys.path.insert(0, str(ROOT / "oracle"))
-    import scunet_np
+    import torch
+    import scunet_torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     scb = importlib.import_module("scunet-rs_b200")
     wt = scb.Weights.seeded(3, 0).tensors
     x = img_u8[None, :, :size, :size].astype(np.float32) / 255.0
     t0 = time.perf_counter()
     for _ in range(reps):
-        scunet_np.forward(x, wt)
+        scunet_torch.forward(x, wt, device="cpu")
     dt = (time.perf_counter() - t0) / reps
-    return size * size / 1e6 / dt, dt, os.cpu_count()
+    return size * size / 1e6 / dt, dt, threads
 
 
 def reference_arm(a, rank, world):
-    """Rank 0 times the CPU implementation of the path; other ranks exit."""
+    """Rank 0 times the CPU implementation of the path; other ranks exit. The
+    reference's own CPU path is Rust and cannot be built here, so this is the oracle
+    port (the same arithmetic, torch float32 on every host thread)."""
     if rank != 0:
         return
     scb = importlib.import_module("scunet-rs_b200")
     img = scb.synth.frames(4000, 1, H, W)[0]
-    size = 128
+    size = CPU_SAMPLE
     times = []
+    cores = 1
     for i in range(a.warmup + a.steps):
         mps, dt, cores = cpu_oracle_mps(img, size)
         if i >= a.warmup:
             times.append(dt)
     tot = sum(times)
     value = a.steps * size * size / 1e6 / tot
-    sample = (f"{size}x{size} crop of a config-4 frame per step (CPU oracle port of the reference's forward, "
-              f"numpy float32, all BLAS threads)")
+    sample = (f"one {size}x{size} crop of a config-4 frame per step: the oracle port of the reference forward "
+              f"(oracle/scunet_torch.py, torch float32 on the CPU, {cores} threads)")
     print(json.dumps({
-        "impl": "reference", "metric": "megapixels/sec", "value": value, "unit": "MP/s", "n_gpus": world,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot / a.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config4 1920x1080 RGB frames (bounded CPU sample)", "sample": sample},
-        "cpu_baseline": {"value": value, "unit": "MP/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": sample},
+        "impl": "reference", "metric": "megapixels/sec (device-timed, max over ranks)", "value": value,
+        "unit": "MP/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: 1920x1080 RGB uint8 frames -> 1920x1088 padded, colour SCUNet "
+                               "(bounded CPU sample)", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "MP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "MP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -407,9 +418,10 @@ def frames_workload(a, job, scb):
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        mps, dt, cores = cpu_oracle_mps(frames[0], 256)
+        mps, dt, cores = cpu_oracle_mps(frames[0], CPU_SAMPLE, reps=2)
         cpu = {"value": mps, "unit": "MP/s", "cores": cores, "kind": "port",
-               "sample": f"one 256x256 crop of frame 0 ({dt:.1f} s), numpy oracle of the reference forward"}
+               "sample": f"two forwards of a {CPU_SAMPLE}x{CPU_SAMPLE} crop of frame 0 ({dt:.1f} s each): the "
+                         f"oracle port of the reference forward, torch float32 on {cores} CPU threads"}
 
     if rank == 0:
         print(json.dumps({
