@@ -184,7 +184,13 @@ int scb_last_launch_count(const scb_ctx* ctx);
  * the blocks whose trans width is 32 or 64 (full and half resolution) as one fused
  * kernel; 0 runs it as separate qkv / attention / proj / mlp launches (the
  * reference's op sequence, src/cuda.rs:1104-1131). Takes effect at the next forward. */
-enum { SCB_OPT_FUSE_TRANS = 1 };
+/* SCB_OPT_RESIDUAL32 (default 0): keep the residual stream inside a stage in fp32
+ * (the reference's precision) with an fp16 copy as the next GEMM's operand; 0 keeps
+ * it in fp16 only, which is that operand already (the four U-Net skips stay fp32
+ * either way). Measured cost of fp16: max |diff| vs the FP32 reference 1.0e-3 ->
+ * 1.2e-3 at 256x256, inside the 2e-3 acceptance bar; it saves 6 of the 16 bytes per
+ * channel a block moves through its 1x1 convs. */
+enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2 };
 int scb_set_option(scb_ctx* ctx, int option, int value);
 
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,

@@ -32,6 +32,7 @@ SYMBOLS = [
     "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes",
 ]
 SCB_OPT_FUSE_TRANS = 1
+SCB_OPT_RESIDUAL32 = 2
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
               "trans_fused", "halo"]
 

@@ -615,6 +615,7 @@ struct scb_ctx {
   Arena arena;
   int last_launches = 0;
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
+  bool residual32 = false; // SCB_OPT_RESIDUAL32
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
   // context's device (looked up on the first call) and the plan laid out in it.
   void* noalloc_base = nullptr;
@@ -1170,13 +1171,21 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       ops.push_back(op);
     }
   }
-  // 9. x = x + conv1_2(z) + b  (fp32) and its shadow (or the shadow of x + skip)
+  // 9. x = x + conv1_2(z) + b and its fp16 copy (or that of x + skip). The residual
+  //    x is `xin` (fp32) when given, else the fp16 plane xs itself, updated in place
+  //    (every tile reads its residual slab before storing that slab); fp32 x is
+  //    written only when `xout` is given.
   {
     GemmOp g{};
     if (!mk.flat(g, A.z + R.off(c), P, c, c, bw.w12, c)) return false;
     g.e.bias = bw.b12;
-    g.e.res32 = xin + R.off(c);
-    g.e.res32_ld = c;
+    if (xin) {
+      g.e.res32 = xin + R.off(c);
+      g.e.res32_ld = c;
+    } else {
+      g.e.res16 = xs + R.off(c);
+      g.e.res16_ld = c;
+    }
     g.e.out32 = xout ? xout + R.off(c) : nullptr;
     g.e.out32_ld = c;
     g.e.out16 = xs + R.off(c);
@@ -1239,7 +1248,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       GemmOp g{};
       if (!mk.up2(g, A.xs[lvl + 1] + Rn.off(2 * c), Rn.n, Rn.rows, Rn.W, 2 * c, ctx->wup[s - 4], c))
         return fail(ctx, SCB_EINVAL, err);
-      g.e.out32 = A.xw + R.off(c);
+      g.e.out32 = ctx->residual32 ? A.xw + R.off(c) : nullptr;
       g.e.out32_ld = c;
       g.e.out16 = A.xs[lvl] + R.off(c);
       g.e.out16_ld = c;
@@ -1251,11 +1260,13 @@ int build_plan(scb_ctx* ctx, Arena& A) {
     }
     const int nb = ctx->config[s];
     for (int i = 0; i < nb; ++i) {
-      const float* xin = (!up && i == 0) ? A.skip[lvl] : A.xw;
+      // the residual stream: fp16 in xs (default), or fp32 in xw with xs its copy
+      // (SCB_OPT_RESIDUAL32); a down stage starts from the fp32 skip plane either way
+      const float* xin = (!up && i == 0) ? A.skip[lvl] : ctx->residual32 ? A.xw : nullptr;
       const bool last = i == nb - 1;
       const float* skip = nullptr;
-      float* xout = A.xw;
-      if (last && s >= 3) {  // body, up3, up2, up1: shadow of (x + skip) only
+      float* xout = ctx->residual32 ? A.xw : nullptr;
+      if (last && s >= 3) {  // body, up3, up2, up1: the fp16 plane holds x + skip
         skip = A.skip[lvl];
         xout = nullptr;
       }
@@ -1830,8 +1841,8 @@ void scb_release_scratch(scb_ctx* ctx) {
 
 int scb_set_option(scb_ctx* ctx, int option, int value) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
-  if (option == SCB_OPT_FUSE_TRANS) {
-    ctx->fuse_trans = value != 0;
+  if (option == SCB_OPT_FUSE_TRANS || option == SCB_OPT_RESIDUAL32) {
+    (option == SCB_OPT_FUSE_TRANS ? ctx->fuse_trans : ctx->residual32) = value != 0;
     ctx->arena.ops.clear();
     ctx->arena.n = 0;  // re-plan on the next forward
     ctx->noalloc.ops.clear();

@@ -46,6 +46,20 @@ def test_forward_unfused_transformer_matches_golden(goldens, oracle, scb, be3):
     check_parity(oracle, "unfused 80x64", g["y"][0], got)
 
 
+@pytest.mark.parametrize("stem", ["color_80x64", "color_128x128"])
+def test_forward_fp32_residual_matches_golden(goldens, oracle, scb, be3, stem):
+    """The residual stream kept in fp32 (SCB_OPT_RESIDUAL32 = 1), the reference's
+    precision, end to end; the default keeps it in fp16."""
+    _gpu()
+    g = goldens[stem]
+    be3.set_option(scb.backend.SCB_OPT_RESIDUAL32, 1)
+    try:
+        got = scb.run(be3, g["x"][0], 3, g["h"], g["w"], be3.weights)
+    finally:
+        be3.set_option(scb.backend.SCB_OPT_RESIDUAL32, 0)
+    check_parity(oracle, f"fp32 residual {stem}", g["y"][0], got)
+
+
 def test_forward_host_batched_uint8(scb, oracle, be3, weights3):
     """uint8 in, the pad/crop fused on the device, two different images in one
     call; each must match the oracle."""
