@@ -524,23 +524,35 @@ size_t plane_px(int n, int hp, int wp, const Band* band, int l) {
   return (size_t)n * (hp >> l) * (wp >> l);
 }
 
-size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band = nullptr) {
+// What the plan needs besides the geometry: the fp32 residual plane only with
+// SCB_OPT_RESIDUAL32, the separate-launch transformer buffers (LN output, attention
+// output, qkv / MLP hidden) only at the levels that do not run a fused kernel.
+struct ArenaOpts {
+  bool residual32 = false;
+  bool fuse_trans = true;
+};
+
+size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band = nullptr,
+                    ArenaOpts opt = ArenaOpts{}) {
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
     off += (bytes + 1023) & ~size_t(1023);
     return o;
   };
-  size_t px[4], wmax = 0;  // wmax: the largest (stored pixels x 64-channel units) over levels
+  // wmax: the largest (stored pixels x 64-channel units) over levels; umax: the same
+  // over the levels whose transformer half runs as separate launches
+  size_t px[4], wmax = 0, umax = 0;
   for (int l = 0; l < 4; ++l) {
     px[l] = plane_px(n, hp, wp, band, l);
     wmax = std::max(wmax, px[l] << l);
+    if (!opt.fuse_trans || l >= 2) umax = std::max(umax, px[l] << l);
   }
   size_t o_skip[4], o_xs[4];
   for (int l = 0; l < 4; ++l) o_skip[l] = take((px[l] << l) * 256);
   for (int l = 0; l < 4; ++l) o_xs[l] = take((px[l] << l) * 128);
-  size_t o_xw = take(wmax * 256), o_y = take(wmax * 128), o_hc = take(wmax * 64), o_z = take(wmax * 128),
-         o_a = take(wmax * 64), o_o = take(wmax * 64), o_qh = take(wmax * 256);
+  size_t o_xw = take(opt.residual32 ? wmax * 256 : 0), o_y = take(wmax * 128), o_hc = take(wmax * 64),
+         o_z = take(wmax * 128), o_a = take(umax * 64), o_o = take(umax * 64), o_qh = take(umax * 256);
   size_t o_in = take(px[0] * in_nc * 4), o_out = take(px[0] * in_nc * 4);
   if (A) {
     char* b = A->base;
@@ -634,6 +646,13 @@ struct scb_ctx {
   std::vector<double> prof_bytes;
   std::vector<float> prof_ms;
 };
+
+ArenaOpts arena_opts(const scb_ctx* ctx) {
+  ArenaOpts o;
+  o.residual32 = ctx->residual32;
+  o.fuse_trans = ctx->fuse_trans;
+  return o;
+}
 
 namespace {
 
@@ -1312,7 +1331,7 @@ int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
   Arena& A = ctx->arena;
   if (A.base && A.n == n && A.hp == hp && A.wp == wp) return SCB_OK;
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-  const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr);
+  const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr, nullptr, arena_opts(ctx));
   if (A.base && A.bytes < need) {
     cudaFree(A.base);
     A.base = nullptr;
@@ -1337,7 +1356,7 @@ int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
   A.n = n;
   A.hp = hp;
   A.wp = wp;
-  arena_layout(n, ctx->in_nc, hp, wp, &A);
+  arena_layout(n, ctx->in_nc, hp, wp, &A, nullptr, arena_opts(ctx));
   return build_plan(ctx, A);
 }
 
@@ -1394,7 +1413,7 @@ int ensure_band_arena(scb_ctx* ctx, Arena& A, const Band& band, int hp, int wp) 
   if (A.base && A.banded && A.hp == hp && A.wp == wp && A.band.R0 == band.R0 && A.band.rows == band.rows &&
       A.band.nranks == band.nranks && !A.ops.empty())
     return SCB_OK;
-  const size_t need = arena_layout(1, ctx->in_nc, hp, wp, nullptr, &band);
+  const size_t need = arena_layout(1, ctx->in_nc, hp, wp, nullptr, &band, arena_opts(ctx));
   if (A.base && A.bytes < need) {
     cudaFree(A.base);
     A.base = nullptr;
@@ -1415,7 +1434,7 @@ int ensure_band_arena(scb_ctx* ctx, Arena& A, const Band& band, int hp, int wp) 
   A.wp = wp;
   A.banded = true;
   A.band = band;
-  arena_layout(1, ctx->in_nc, hp, wp, &A, &band);
+  arena_layout(1, ctx->in_nc, hp, wp, &A, &band, arena_opts(ctx));
   return build_plan(ctx, A);
 }
 
@@ -1663,7 +1682,7 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
   }
   Arena& A = ctx->noalloc;
   if (!(A.n == n && A.hp == hp && A.wp == wp && !A.ops.empty())) {
-    const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr);
+    const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr, nullptr, arena_opts(ctx));
     if (need > kNoAllocBytes) return fail(ctx, SCB_EINVAL, "no-allocation scratch is too small for this geometry");
     A = Arena{};
     A.base = static_cast<char*>(ctx->noalloc_base);
@@ -1671,7 +1690,7 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
     A.n = n;
     A.hp = hp;
     A.wp = wp;
-    arena_layout(n, ctx->in_nc, hp, wp, &A);
+    arena_layout(n, ctx->in_nc, hp, wp, &A, nullptr, arena_opts(ctx));
     int r = build_plan(ctx, A);
     if (r) {
       A.ops.clear();

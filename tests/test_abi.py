@@ -85,7 +85,7 @@ def test_create_without_device_fails_loudly(scb):
 def test_need_bytes(scb):
     a = scb.need_bytes(1, 3, 1088, 1920)
     b = scb.need_bytes(2, 3, 1088, 1920)
-    assert 1.4e3 < a / (1088 * 1920) < 2.5e3      # ~1.7 KB per padded pixel
+    assert 1.0e3 < a / (1088 * 1920) < 1.4e3      # ~1.16 KB per padded pixel (default options)
     assert abs(b - 2 * a) < 64 * 1024
     with pytest.raises(Exception):
         scb.need_bytes(1, 3, 100, 64)             # not padded
