@@ -76,6 +76,11 @@ struct GemmEpi {
   long skip_ld;
   __half* out16;
   long out16_ld;
+  // if set, GEMM columns [out16_split, N) go to out16b[p*out16b_ld + (col - out16_split)]
+  // instead (two planes, e.g. the conv and the trans half of conv1_1's output)
+  __half* out16b;
+  long out16b_ld;
+  int out16_split;
   float* out32;
   long out32_ld;
   // LayerNorm over global columns [ln_lo, ln_lo + ln_n) of the final value v,
@@ -101,7 +106,7 @@ struct GemmEpi {
 // Tensor maps of the epilogue streams (TMA epilogue only); box = 32 columns x the
 // M tile's pixel block.
 struct EpiMaps {
-  CUtensorMap res16, res32, skip, out16, out32, lnout;
+  CUtensorMap res16, res32, skip, out16, out32, lnout, out16b;
 };
 
 
@@ -138,7 +143,11 @@ struct GemmSmem {
   static constexpr int A_BYTES = A_ROWS * BK * 2;
   static constexpr int B_BYTES = B_TAPS * BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  // TMEM accumulator buffers: four for narrow tiles (so the loads and MMAs of the next
+  // tiles run ahead while the epilogue drains one), two otherwise
+  static constexpr int NACC = BN <= 64 ? 4 : 2;
+  static constexpr int TMEM_COLS = (NACC * BN <= 32) ? 32 : (NACC * BN <= 64) ? 64 : (NACC * BN <= 128) ? 128
+                                   : (NACC * BN <= 256) ? 256 : 512;
   __host__ __device__ static constexpr int bar_off(int stages) { return stages * STAGE_BYTES; }
   __host__ __device__ static constexpr int staging_off(int stages) { return stages * STAGE_BYTES + 1024; }
 };
@@ -244,8 +253,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* res_full = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + L::NACC;
+  uint64_t* res_full = acc_empty + L::NACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
   uint8_t* staging = smem + L::staging_off(STAGES);
 
@@ -257,11 +266,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < L::NACC; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
-      mbar_init(&res_full[a], 1);
     }
+    for (int b = 0; b < 2; ++b) mbar_init(&res_full[b], 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -320,7 +329,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t it = 0, t = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t) {
-        const uint32_t a = t & 1, aph = (t >> 1) & 1;
+        const uint32_t a = t % L::NACC, aph = (t / L::NACC) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, SCB_ERR_WAIT_ACC_FREE)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
@@ -375,7 +384,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
       const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
       const int n0 = nt * BN;
-      const uint32_t a = t & 1, aph = (t >> 1) & 1;
+      const uint32_t a = t % L::NACC, aph = (t / L::NACC) & 1;
       if (!mbar_wait(&acc_full[a], aph, SCB_ERR_WAIT_ACC)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
@@ -526,7 +535,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         epi_bar();  // staging complete; also every thread is done with this slab's residuals
         if (elected) {
           if (e.st_out32 >= 0) epi_slab_store<GEO>(&em.out32, ob + e.st_out32, n, mt, g);
-          if (e.st_out16 >= 0) epi_slab_store<GEO>(&em.out16, ob + e.st_out16, n, mt, g);
+          if (e.st_out16 >= 0) {
+            if (e.out16b && n >= e.out16_split)
+              epi_slab_store<GEO>(&em.out16b, ob + e.st_out16, n - e.out16_split, mt, g);
+            else
+              epi_slab_store<GEO>(&em.out16, ob + e.st_out16, n, mt, g);
+          }
           if (ln_slab) epi_slab_store<GEO>(&em.lnout, ob + e.st_ln, n - e.ln_lo, mt, g);
           bulk_commit_group();
         }
@@ -545,7 +559,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
       const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
       const int n0 = nt * BN;
-      const uint32_t a = t & 1, aph = (t >> 1) & 1;
+      const uint32_t a = t % L::NACC, aph = (t / L::NACC) & 1;
       int col0;
       const long p = row_pixel<GEO>(g, mt, r, n0, col0);
       ResChunk cur, nxt;
@@ -630,7 +644,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 s[4 * h + 2] += cur.sk[h].z; s[4 * h + 3] += cur.sk[h].w;
               }
             }
-            uint4* dst = reinterpret_cast<uint4*>(e.out16 + p * e.out16_ld + oc);
+            uint4* dst = (e.out16b && oc >= e.out16_split)
+                             ? reinterpret_cast<uint4*>(e.out16b + p * e.out16b_ld + (oc - e.out16_split))
+                             : reinterpret_cast<uint4*>(e.out16 + p * e.out16_ld + oc);
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               dst[h] = make_uint4(pack_half2(s[8 * h], s[8 * h + 1]), pack_half2(s[8 * h + 2], s[8 * h + 3]),

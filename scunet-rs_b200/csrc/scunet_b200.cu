@@ -398,6 +398,10 @@ struct Maker {
     e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = e.st_ln = -1;
     e.st_res_bytes = e.st_out_bytes = 0;
     op.tma_epi = false;
+    if (e.out16b && (e.out16_split % 32 || e.out16_split <= 0 || e.out16_split >= op.g.n_total)) {
+      *err = "a split fp16 output must split at a multiple of 32 columns";
+      return false;
+    }
     if (e.ln_out && (e.ln_lo % op.bn) + e.ln_n > op.bn) {
       *err = "LayerNorm columns [" + std::to_string(e.ln_lo) + ", +" + std::to_string(e.ln_n) + ") span two " +
              std::to_string(op.bn) + "-column tiles";
@@ -431,7 +435,8 @@ struct Maker {
       off += 128 * 128;
     }
     if (e.out16) {
-      if (!stream_map(op, &op.em.out16, e.out16, e.out16_ld, N, 2)) return false;
+      if (!stream_map(op, &op.em.out16, e.out16, e.out16_ld, e.out16b ? e.out16_split : N, 2)) return false;
+      if (e.out16b && !stream_map(op, &op.em.out16b, e.out16b, e.out16b_ld, N - e.out16_split, 2)) return false;
       e.st_out16 = off;
       off += 128 * 64;
     }
@@ -512,7 +517,8 @@ struct Arena {
   float* skip[4] = {};
   __half* xs[4] = {};
   float* xw = nullptr;
-  __half *y = nullptr, *hc = nullptr, *z = nullptr, *a = nullptr, *o = nullptr, *qh = nullptr;
+  __half *y = nullptr, *yt = nullptr;  // conv1_1 output: conv half, trans half (two planes)
+  __half *hc = nullptr, *z = nullptr, *a = nullptr, *o = nullptr, *qh = nullptr;
   float* io_in = nullptr;  // staging for host-pointer forwards
   float* io_out = nullptr;
   std::vector<Op> ops;     // head .. tail
@@ -551,7 +557,8 @@ size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band
   size_t o_skip[4], o_xs[4];
   for (int l = 0; l < 4; ++l) o_skip[l] = take((px[l] << l) * 256);
   for (int l = 0; l < 4; ++l) o_xs[l] = take((px[l] << l) * 128);
-  size_t o_xw = take(opt.residual32 ? wmax * 256 : 0), o_y = take(wmax * 128), o_hc = take(wmax * 64),
+  size_t o_xw = take(opt.residual32 ? wmax * 256 : 0), o_y = take(wmax * 64), o_yt = take(wmax * 64),
+         o_hc = take(wmax * 64),
          o_z = take(wmax * 128), o_a = take(umax * 64), o_o = take(umax * 64), o_qh = take(umax * 256);
   size_t o_in = take(px[0] * in_nc * 4), o_out = take(px[0] * in_nc * 4);
   if (A) {
@@ -562,6 +569,7 @@ size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band
     }
     A->xw = reinterpret_cast<float*>(b + o_xw);
     A->y = reinterpret_cast<__half*>(b + o_y);
+    A->yt = reinterpret_cast<__half*>(b + o_yt);
     A->hc = reinterpret_cast<__half*>(b + o_hc);
     A->z = reinterpret_cast<__half*>(b + o_z);
     A->a = reinterpret_cast<__half*>(b + o_a);
@@ -1043,8 +1051,13 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     GemmOp g{};
     if (!mk.flat(g, xs + R.off(c), P, c, c, bw.w11, c, GEO_FLAT, fused ? 0 : t)) return false;
     g.e.bias = bw.b11;
-    g.e.out16 = A.y + R.off(c);
-    g.e.out16_ld = c;
+    // the conv half and the trans half to separate planes: their readers (the 3x3
+    // pair, the transformer) then read whole contiguous pixel rows
+    g.e.out16 = A.y + R.off(cc);
+    g.e.out16_ld = cc;
+    g.e.out16b = A.yt + R.off(t);
+    g.e.out16b_ld = t;
+    g.e.out16_split = cc;
     if (!fused) {  // the fused transformer kernel normalises its own input
       g.e.ln_g = bw.ln1g;
       g.e.ln_b = bw.ln1b;
@@ -1062,7 +1075,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   if (R.banded) {
     // the one exchange of the block: Y's boundary rows (3x3 pair and SW windows),
     // and for the separate-launch transformer path also LN1's
-    ops.push_back(xchg_op(A.y, R, c, 2));
+    ops.push_back(xchg_op(A.y, R, cc, 2));
+    ops.push_back(xchg_op(A.yt, R, t, 2));
     if (!fused) ops.push_back(xchg_op(A.a, R, t, 2));
   }
   // 2. h = relu(conv3x3(y_c)), on the working rows plus one halo row on each side
@@ -1071,7 +1085,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     const int lo = R.banded && !R.top ? R.row0 - 1 : R.row0;
     const int hi = R.banded && !R.bottom ? R.row0 + R.rows + 1 : R.row0 + R.rows;
     GemmOp g{};
-    if (!mk.conv3(g, A.y, n, H, W, cc, c, bw.wc0, cc, true, lo, hi - lo)) return false;
+    if (!mk.conv3(g, A.y, n, H, W, cc, cc, bw.wc0, cc, true, lo, hi - lo)) return false;
     g.e.act = ACT_RELU;
     g.e.out16 = A.hc;
     g.e.out16_ld = cc;
@@ -1086,7 +1100,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     GemmOp g{};
     if (!mk.conv3(g, A.hc, n, H, W, cc, cc, bw.wc2, cc, true, R.row0, R.rows)) return false;
     g.e.res16 = A.y;
-    g.e.res16_ld = c;
+    g.e.res16_ld = cc;
     g.e.out16 = A.z;
     g.e.out16_ld = c;
     if (!mk.finish_epi(g)) return false;
@@ -1105,7 +1119,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     tr.flops = 2.0 * P * (3.0 * t * t + 2.0 * 64 * t + t * t + 8.0 * t * t);
     TransGeom& tg = tr.trans;
     tg.win = wg;
-    tg.y = A.y;
+    tg.y = A.yt;
     tg.z = A.z;
     tg.wqkv = bw.wqkv; tg.wproj = bw.wproj; tg.w0 = bw.w0; tg.w2 = bw.w2;
     tg.bqkv = bw.bqkv; tg.bproj = bw.bproj; tg.b0 = bw.b0; tg.b2 = bw.b2;
@@ -1144,8 +1158,8 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       GemmOp g{};
       if (!mk.flat(g, A.o + R.off(t), P, t, t, bw.wproj, t, GEO_FLAT, t, true)) return false;
       g.e.bias = bw.bproj;
-      g.e.res16 = A.y + R.off(c) + cc;
-      g.e.res16_ld = c;
+      g.e.res16 = A.yt + R.off(t);
+      g.e.res16_ld = t;
       g.e.out16 = A.z + R.off(c) + cc;
       g.e.out16_ld = c;
       g.e.ln_g = bw.ln2g;
@@ -1242,20 +1256,20 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       // as zero (conv zero padding) although other levels wrote that memory
       // (every band gets the same ops - lockstep execution pairs them by index - and
       // the interior sides clear nothing)
-      const size_t rb_y = (size_t)R.W * c * 2, rb_h = (size_t)R.W * (c / 2) * 2;
+      // (the trans half's halo rows are only read by masked shifted-window keys, but
+      // they must be finite: a zero attention weight times NaN is NaN)
+      const size_t rb = (size_t)R.W * (c / 2) * 2;  // one row of Y_c, Y_t or Hc
       for (int side = 0; side < 2; ++side) {
         const bool edge = side == 0 ? R.top : R.bottom;
         const int r = side == 0 ? 0 : R.row0 + R.rows;
-        Op zy{};
-        zy.kind = Op::ZERO;
-        zy.tag = TAG_HALO;
-        zy.zero_ptr = reinterpret_cast<char*>(A.y) + r * rb_y;
-        zy.zero_bytes = edge ? kHalo * rb_y : 0;
-        ops.push_back(zy);
-        Op zh = zy;
-        zh.zero_ptr = reinterpret_cast<char*>(A.hc) + r * rb_h;
-        zh.zero_bytes = edge ? kHalo * rb_h : 0;
-        ops.push_back(zh);
+        for (__half* plane : {A.y, A.yt, A.hc}) {
+          Op zp{};
+          zp.kind = Op::ZERO;
+          zp.tag = TAG_HALO;
+          zp.zero_ptr = reinterpret_cast<char*>(plane) + r * rb;
+          zp.zero_bytes = edge ? kHalo * rb : 0;
+          ops.push_back(zp);
+        }
       }
     }
     if (up) {
@@ -2028,7 +2042,7 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
   Arena tmp;
   const long P = (long)n * H * W;
-  const size_t bytes = (size_t)P * (c * 2 /*xs*/ + c * 2 /*y*/ + c /*hc*/ + c * 2 /*z*/ + c /*a*/ + c /*o*/ + c * 4 /*qh*/) + 16 * 1024;
+  const size_t bytes = (size_t)P * (c * 2 /*xs*/ + c * 2 /*y, yt*/ + c /*hc*/ + c * 2 /*z*/ + c /*a*/ + c /*o*/ + c * 4 /*qh*/) + 16 * 1024;
   char* base = nullptr;
   CKC(ctx, cudaMalloc(&base, bytes), "probe scratch");
   size_t off = 0;
@@ -2038,7 +2052,8 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
     return p;
   };
   __half* xs = reinterpret_cast<__half*>(take((size_t)P * c * 2));
-  tmp.y = reinterpret_cast<__half*>(take((size_t)P * c * 2));
+  tmp.y = reinterpret_cast<__half*>(take((size_t)P * c));
+  tmp.yt = reinterpret_cast<__half*>(take((size_t)P * c));
   tmp.hc = reinterpret_cast<__half*>(take((size_t)P * c));
   tmp.z = reinterpret_cast<__half*>(take((size_t)P * c * 2));
   tmp.a = reinterpret_cast<__half*>(take((size_t)P * c));

@@ -3,7 +3,7 @@
 // the whole transformer half of a ConvTransBlock on pairs of 8x8 windows (128
 // tokens, one UMMA M tile):
 //
-//   x  = y_t                                   (fp16 plane, columns [T, 2T) of Y)
+//   x  = y_t                                   (fp16 plane Y_t, T channels)
 //   x1 = x + proj(WMSA(LN1(x)))                (tools/network_scunet.py:134-135)
 //   z  = x1 + mlp2(GELU(mlp0(LN2(x1))))        (tools/network_scunet.py:128-136)
 //   -> columns [T, 2T) of Z (fp16), the conv1_2 operand.
@@ -20,7 +20,7 @@ namespace scb {
 
 struct TransGeom {
   WinGeom win;
-  const __half* y;    // Y plane, pixel stride 2T, trans half at column T
+  const __half* y;    // Y_t plane (conv1_1's trans half), pixel stride T
   __half* z;          // Z plane, pixel stride 2T, output at column T
   const __half* wqkv; // [3T][T]
   const __half* wproj;// [T][T]

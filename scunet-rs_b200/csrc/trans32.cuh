@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
   auto load_half = [&](long pix, uint4* dst) {
 #pragma unroll
     for (int c = 0; c < 2; ++c)
-      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * (2 * T) + T + hf * 16) + c)
+      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * T + hf * 16) + c)
                         : make_uint4(0, 0, 0, 0);
   };
 
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
     load_half(pix, ycur);
     // the next pair's tokens are pulled into L2 while this pair computes
     pix_n = locate(pair + gridDim.x, lr_n, lc_n, st_n);
-    if (pix_n >= 0) prefetch_l2(g.y + pix_n * (2 * T) + T + hf * 16);
+    if (pix_n >= 0) prefetch_l2(g.y + pix_n * T + hf * 16);
 
     // ---- LN1 -> A1; qkv = A1 . Wqkv^T -> TMEM [0, 96) ----
     {

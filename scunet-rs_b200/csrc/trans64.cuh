@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
   auto load_y = [&](long pix, uint4* dst) {
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * (2 * T) + T + hf * 32) + c)
+      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * T + hf * 32) + c)
                         : make_uint4(0, 0, 0, 0);
   };
 
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
     uint4 ycur[4];  // y_t stays packed (fp16 data)
     load_y(pix, ycur);
     pix_n = locate(pair + stride, lr_n, lc_n, st_n);
-    if (pix_n >= 0) prefetch_l2(g.y + pix_n * (2 * T) + T + hf * 32);
+    if (pix_n >= 0) prefetch_l2(g.y + pix_n * T + hf * 32);
 
     // ---- LN1 -> A1; qkv -> TMEM [0, 192) ----
     {
