@@ -740,8 +740,11 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const unsigned grid = (unsigned)((op.attn.win.n_windows + 1) / 2);
-  window_attn_kernel<<<grid, 128, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
+  int dev_sms = 148;
+  cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, dev);
+  const long pairs = (op.attn.win.n_windows + 1) / 2;
+  const unsigned grid = (unsigned)std::max(1L, std::min(pairs, (long)dev_sms * ATT_CTAS));
+  window_attn_kernel<<<grid, 256, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
   return cudaGetLastError();
 }
 
