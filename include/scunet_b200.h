@@ -171,6 +171,11 @@ int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, c
 int scb_probe_attention(scb_ctx* ctx, const void* qkv16, int n, int H, int W, int t, int shift, const float* rp,
                         void* out16);
 
+/* The fused MLP of block (stage, index) of a 1/4 or 1/8 resolution stage (trans
+ * width t = 128 or 256): a16 [tokens][t] fp16 (the LN2 output) in; z16 [tokens][t]
+ * holds x1 and receives z = x1 + mlp2(GELU(mlp0(a))) (tools/network_scunet.py:128-136). */
+int scb_probe_mlp(scb_ctx* ctx, int stage, int index, const void* a16, void* z16, int tokens);
+
 /* One ConvTransBlock with the context's weights: `stage` 0..6 (down1, down2,
  * down3, body, up3, up2, up1), `index` 0..3 within the stage; x32 [n][H][W][c]
  * float32 is read and y32 written (may alias). shift follows the block index
@@ -200,7 +205,8 @@ int scb_set_profiling(scb_ctx* ctx, int on);
 
 /* For the last profiled forward: per launch, its op class (0 head, 1 tail,
  * 2 conv1x1, 3 conv3x3, 4 qkv, 5 attention, 6 proj, 7 mlp0, 8 mlp2, 9 down,
- * 10 up, 11 fused transformer half, 12 band halo exchange or edge-halo clear), its algorithmic FLOPs and its device time in ms (waits for the
+ * 10 up, 11 fused transformer half, 12 band halo exchange or edge-halo clear, 13 fused MLP of a
+ * separate-launch transformer half), its algorithmic FLOPs and its device time in ms (waits for the
  * events). Returns the number of entries written (<= max). */
 int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max);
 

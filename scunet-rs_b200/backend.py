@@ -29,12 +29,12 @@ SYMBOLS = [
     "scb_release_scratch", "scb_last_error", "scb_destroy", "scb_probe_gemm", "scb_probe_conv3x3",
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
-    "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes",
+    "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes", "scb_probe_mlp",
 ]
 SCB_OPT_FUSE_TRANS = 1
 SCB_OPT_RESIDUAL32 = 2
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
-              "trans_fused", "halo"]
+              "trans_fused", "halo", "mlp"]
 
 
 class BackendError(RuntimeError):
@@ -71,6 +71,7 @@ def load_library(path=None):
     lib.scb_band_init.argtypes = [vp, vp, i, i]
     lib.scb_forward_band.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
     lib.scb_profile_bytes.argtypes = [vp, ctypes.POINTER(ctypes.c_double), i]
+    lib.scb_probe_mlp.argtypes = [vp, i, i, vp, vp, i]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_footprint.restype = None

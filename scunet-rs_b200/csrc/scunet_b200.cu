@@ -35,6 +35,7 @@
 #include "trans.cuh"
 #include "trans32.cuh"
 #include "trans64.cuh"
+#include "mlp.cuh"
 
 using namespace scb;
 
@@ -473,11 +474,11 @@ const int kStageLevel[7] = {0, 1, 2, 3, 2, 1, 0};
 // classes (docs/TECH_NOTES.md:346-367).
 enum OpTag : int {
   TAG_HEAD = 0, TAG_TAIL = 1, TAG_CONV1X1 = 2, TAG_CONV3X3 = 3, TAG_QKV = 4, TAG_ATTN = 5, TAG_PROJ = 6,
-  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10, TAG_TRANS = 11, TAG_HALO = 12
+  TAG_MLP0 = 7, TAG_MLP2 = 8, TAG_DOWN = 9, TAG_UP = 10, TAG_TRANS = 11, TAG_HALO = 12, TAG_MLP = 13
 };
 
 struct Op {
-  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS, XCHG, ZERO } kind;
+  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS, XCHG, ZERO, MLP } kind;
   // XCHG (row bands): swap kHalo boundary rows of a stored plane with the
   // neighbouring bands; xchg_base is the plane, xchg_row the bytes of one row
   char* xchg_base = nullptr;
@@ -496,6 +497,10 @@ struct Op {
   const __half* attn_in = nullptr;
   __half* attn_out = nullptr;
   const float* attn_rp = nullptr;
+  // MLP: the fused mlp0 + GELU + mlp2 of a t = 128 / 256 transformer half
+  int mlp_t = 0;
+  MlpGeom mlp{};
+  CUtensorMap mlp_a, mlp_w0, mlp_w2;
 };
 
 // A row band of one image (config 5): full-resolution rows [R0, R0 + rows) of the
@@ -782,6 +787,28 @@ cudaError_t launch_trans64(const Op& op, int sms, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <int T>
+cudaError_t launch_mlp_t(const Op& op, int sms, cudaStream_t st) {
+  using L = MlpLayout<T>;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(mlp_fused_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int grid = std::max(1, std::min(op.mlp.m_tiles, sms));
+  mlp_fused_kernel<T><<<grid, MLP_THREADS, L::SMEM, st>>>(op.mlp_a, op.mlp_w0, op.mlp_w2, op.mlp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mlp(const Op& op, int sms, cudaStream_t st) {
+  if (op.mlp_t == 128) return launch_mlp_t<128>(op, sms, st);
+  if (op.mlp_t == 256) return launch_mlp_t<256>(op, sms, st);
+  return cudaErrorInvalidConfiguration;
+}
+
 cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
   if (op.trans_t == 32) return launch_trans32(op, sms, st);
   if (op.trans_t == 64) return launch_trans64(op, sms, st);
@@ -900,6 +927,8 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
       return launch_attn(op, st);
     case Op::TRANS:
       return launch_trans(op, ctx->sms, st);
+    case Op::MLP:
+      return launch_mlp(op, ctx->sms, st);
     case Op::XCHG:
       return cudaSuccess;  // handled by the caller (it needs the other bands)
     case Op::ZERO:
@@ -944,6 +973,8 @@ double op_bytes(const Arena& A, const Op& op, const Io& io) {
     }
     case Op::ATTN:
       return 64.0 * op.attn.win.n_windows * (3.0 * op.attn.t + op.attn.t) * 2;
+    case Op::MLP:  // a in, x1 in, z out; both weight matrices
+      return (double)op.mlp.M * op.mlp_t * 2 * 3 + 16.0 * op.mlp_t * op.mlp_t;
     case Op::HEAD: {
       const Region R = region_of(A, 0);
       return (double)R.px() * (io.c * (io.x_u8 ? 1 : 4) + 64 * (4 + 2));
@@ -1040,6 +1071,33 @@ WinGeom win_geom(const Region& R, bool shifted) {
 //   xin (fp32, its fp16 shadow already in xs) -> xout (fp32, may alias xin; may be
 //   null when `skip` is given: then only the fp16 shadow of (x + skip) is written).
 // Plane pointers are the stored planes; FLAT ops address the working rows.
+// The fused MLP of a t = 128 / 256 transformer half over P tokens: a = LN2(x1) [P][t]
+// (ld t) in, x1 in and z = x1 + mlp2(GELU(mlp0(a))) out at z[p * z_ld + col].
+bool mlp_op(Op& mo, const BlockW& bw, const __half* a, __half* z, long z_ld, long P, std::string& err) {
+  const int t = bw.c / 2;
+  if (t != 128 && t != 256) {
+    err = "the fused MLP is built for trans widths 128 and 256";
+    return false;
+  }
+  mo.kind = Op::MLP;
+  mo.tag = TAG_MLP;
+  mo.mlp_t = t;
+  mo.flops = 2.0 * 2.0 * P * t * 4 * t;
+  mo.mlp.M = (int)P;
+  mo.mlp.m_tiles = (int)((P + 127) / 128);
+  mo.mlp.z = z;
+  mo.mlp.z_ld = z_ld;
+  mo.mlp.b0 = bw.b0;
+  mo.mlp.b2 = bw.b2;
+  const uint64_t da[2] = {(uint64_t)t, (uint64_t)P}, sa[1] = {(uint64_t)t * 2};
+  const uint64_t d0[2] = {(uint64_t)t, (uint64_t)(4 * t)}, s0[1] = {(uint64_t)t * 2};
+  const uint64_t d2[2] = {(uint64_t)(4 * t), (uint64_t)t}, s2[1] = {(uint64_t)(4 * t) * 2};
+  const uint32_t ba[2] = {64, 128}, b2b[2] = {64, (uint32_t)t};
+  return encode_map(&mo.mlp_a, a, 2, da, sa, ba, 2, 128, err) &&
+         encode_map(&mo.mlp_w0, bw.w0, 2, d0, s0, ba, 2, 128, err) &&
+         encode_map(&mo.mlp_w2, bw.w2, 2, d2, s2, b2b, 2, 128, err);
+}
+
 bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena& A, const Region& R,
                const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err) {
   const int c = bw.c, t = c / 2, cc = c / 2, heads = t / 32;
@@ -1177,34 +1235,42 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
       op.flops = 2.0 * P * t * t;
       ops.push_back(op);
     }
-    // 7. hid = gelu(LN2 W0^T + b0)
-    {
-      GemmOp g{};
-      if (!mk.flat(g, A.a + R.off(t), P, t, t, bw.w0, 4 * t)) return false;
-      g.e.bias = bw.b0;
-      g.e.act = ACT_GELU;
-      g.e.out16 = A.qh + R.off(4 * t);
-      g.e.out16_ld = 4 * t;
-      if (!mk.finish_epi(g)) return false;
-      op.gemm = g;
-      op.tag = TAG_MLP0;
-      op.flops = 2.0 * P * t * 4 * t;
-      ops.push_back(op);
-    }
-    // 8. z[:, cc:] = hid W2^T + b2 + x1t
-    {
-      GemmOp g{};
-      if (!mk.flat(g, A.qh + R.off(4 * t), P, 4 * t, 4 * t, bw.w2, t)) return false;
-      g.e.bias = bw.b2;
-      g.e.res16 = A.z + R.off(c) + cc;
-      g.e.res16_ld = c;
-      g.e.out16 = A.z + R.off(c) + cc;
-      g.e.out16_ld = c;
-      if (!mk.finish_epi(g)) return false;
-      op.gemm = g;
-      op.tag = TAG_MLP2;
-      op.flops = 2.0 * P * t * 4 * t;
-      ops.push_back(op);
+    if (t == 128 || t == 256) {
+      // 7-8. z[:, cc:] = x1t + mlp2(GELU(mlp0(LN2(x1t)))) in one kernel: the 4t-wide
+      //      hidden layer stays on chip (mlp.cuh)
+      Op mo{};
+      if (!mlp_op(mo, bw, A.a + R.off(t), A.z + R.off(c) + cc, c, P, err)) return false;
+      ops.push_back(mo);
+    } else {
+      // 7. hid = gelu(LN2 W0^T + b0)
+      {
+        GemmOp g{};
+        if (!mk.flat(g, A.a + R.off(t), P, t, t, bw.w0, 4 * t)) return false;
+        g.e.bias = bw.b0;
+        g.e.act = ACT_GELU;
+        g.e.out16 = A.qh + R.off(4 * t);
+        g.e.out16_ld = 4 * t;
+        if (!mk.finish_epi(g)) return false;
+        op.gemm = g;
+        op.tag = TAG_MLP0;
+        op.flops = 2.0 * P * t * 4 * t;
+        ops.push_back(op);
+      }
+      // 8. z[:, cc:] = hid W2^T + b2 + x1t
+      {
+        GemmOp g{};
+        if (!mk.flat(g, A.qh + R.off(4 * t), P, 4 * t, 4 * t, bw.w2, t)) return false;
+        g.e.bias = bw.b2;
+        g.e.res16 = A.z + R.off(c) + cc;
+        g.e.res16_ld = c;
+        g.e.out16 = A.z + R.off(c) + cc;
+        g.e.out16_ld = c;
+        if (!mk.finish_epi(g)) return false;
+        op.gemm = g;
+        op.tag = TAG_MLP2;
+        op.flops = 2.0 * P * t * 4 * t;
+        ops.push_back(op);
+      }
     }
   }
   // 9. x = x + conv1_2(z) + b and its fp16 copy (or that of x + skip). The residual
@@ -2018,6 +2084,19 @@ int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, c
   return probe_finish(ctx, launch_gemm(g, ctx->sms, ctx->stream));
 }
 
+int scb_probe_mlp(scb_ctx* ctx, int stage, int index, const void* a16, void* z16, int tokens) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (stage < 0 || stage > 6 || index < 0 || index >= ctx->config[stage] || tokens <= 0)
+    return fail(ctx, SCB_EINVAL, "block index / token count");
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  const BlockW& bw = ctx->blocks[stage][index];
+  std::string err;
+  Op mo{};
+  if (!mlp_op(mo, bw, static_cast<const __half*>(a16), static_cast<__half*>(z16), bw.c / 2, tokens, err))
+    return fail(ctx, SCB_EINVAL, err);
+  return probe_finish(ctx, launch_mlp(mo, ctx->sms, ctx->stream));
+}
+
 int scb_probe_attention(scb_ctx* ctx, const void* qkv16, int n, int H, int W, int t, int shift, const float* rp,
                         void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
@@ -2084,12 +2163,12 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
   }
   int r = SCB_OK;
   for (const Op& op : ops) {
-    if (op.kind == Op::GEMM) {
-      e = launch_gemm(op.gemm, ctx->sms, ctx->stream);
-    } else if (op.kind == Op::TRANS) {
-      e = launch_trans(op, ctx->sms, ctx->stream);
-    } else {
-      e = launch_attn(op, ctx->stream);
+    switch (op.kind) {
+      case Op::GEMM: e = launch_gemm(op.gemm, ctx->sms, ctx->stream); break;
+      case Op::TRANS: e = launch_trans(op, ctx->sms, ctx->stream); break;
+      case Op::ATTN: e = launch_attn(op, ctx->stream); break;
+      case Op::MLP: e = launch_mlp(op, ctx->sms, ctx->stream); break;
+      default: e = cudaErrorInvalidValue;  // a block builds none of the other kinds
     }
     if (e != cudaSuccess) break;
   }

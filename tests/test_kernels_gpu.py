@@ -184,3 +184,31 @@ def test_block(be3, weights3, oracle, scb, stage, index, n, H, W, fused):
     assert rc == 0, be3.lib.scb_last_error(be3.ctx)
     r = close(f"block {prefix} {n}x{H}x{W}", want, ty.cpu().numpy(), 1e-3)
     print(f"block {prefix}: rel err {r:.2e}")
+
+
+@pytest.mark.parametrize("stage,tokens", [(2, 128), (2, 300), (3, 128), (3, 1000), (4, 4096)])
+def test_fused_mlp(be3, weights3, stage, tokens):
+    """The fused mlp0 + GELU + mlp2 (hidden layer on chip) of the t = 128 / 256 blocks
+    against fp32 numpy on the same fp16 operands; GELU in the kernel is the fp16 tanh
+    form and the hidden layer is stored fp16, so the bar is fp16 accuracy."""
+    torch = _torch()
+    t = 32 << [0, 1, 2, 3, 2, 1, 0][stage]
+    prefix = f"m_{STAGES[stage]}.{1 if stage >= 4 else 0}.trans_block.mlp"
+    w = weights3.tensors
+    w0 = w[prefix + ".0.weight"].astype(np.float16).astype(np.float32)
+    w2 = w[prefix + ".2.weight"].astype(np.float16).astype(np.float32)
+    rng = np.random.default_rng(stage * 1000 + tokens)
+    a = h16(rng, (tokens, t))
+    x1 = h16(rng, (tokens, t))
+    hid = a.astype(np.float32) @ w0.T + w[prefix + ".0.bias"]
+    hid = np.asarray(torch.nn.functional.gelu(torch.from_numpy(hid))).astype(np.float16).astype(np.float32)
+    want = x1.astype(np.float32) + hid @ w2.T + w[prefix + ".2.bias"]
+    ta = torch.from_numpy(a).cuda()
+    tz = torch.from_numpy(x1).cuda()
+    rc = be3.lib.scb_probe_mlp(be3.ctx, stage, 0, ta.data_ptr(), tz.data_ptr(), tokens)
+    assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+    got = tz.float().cpu().numpy()
+    d = np.abs(got - want)
+    print(f"mlp stage {stage} ({tokens} tokens): worst |diff| {d.max():.3e}; rows with errors "
+          f"{np.unique(np.nonzero(d > 0.05)[0])[:12]}, columns {np.unique(np.nonzero(d > 0.05)[1])[:12]}")
+    close(f"fused mlp stage {stage} x {tokens}", want, got, 4e-3)
