@@ -21,18 +21,23 @@ struct HeadGeom {
 
 // m_head on tcgen05: each 128-pixel tile's im2col rows (27 taps, zero-padded to
 // K = 32, order ci, ky, kx) are built by the threads straight into a 64B-swizzled
-// K-major smem tile, then D[128 x 64] = A . Wh^T is one UMMA chain into TMEM and
-// the epilogue writes x1 (f32) and its fp16 shadow. The replicate pad is the
+// K-major smem tile, then D[128 x 64] = A . Wh^T is one UMMA chain into TMEM. The
+// epilogue stages x1 (f32) and its fp16 shadow in 128B-swizzled smem and sends them
+// with three TMA tensor stores per tile (whole 128-byte pixel rows, coalesced); rows
+// past the last pixel are clipped by the tensor maps. The replicate pad is the
 // clamped read; the conv's own zero pad is the bounds test.
-constexpr int HEAD_SMEM = 8192 + 4096 + 64 + 1024;
+constexpr int HEAD_ST = 8192 + 4096;               // staging: 2 f32 slabs + 1 fp16 slab of [128 x 128 B]
+constexpr int HEAD_BAR = HEAD_ST + 3 * 16384;
+constexpr int HEAD_SMEM = HEAD_BAR + 64 + 1024;
 
 __global__ void __launch_bounds__(128)
 head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][32] K-major*/,
-               float* __restrict__ out32, __half* __restrict__ out16, const HeadGeom g) {
+               const __grid_constant__ CUtensorMap m32, const __grid_constant__ CUtensorMap m16, const HeadGeom g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 12288);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + HEAD_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  uint8_t* st = sm + HEAD_ST;
   const int tid = threadIdx.x, warp = tid >> 5;
   for (int idx = tid; idx < 64 * 4; idx += 128) {
     const int r = idx >> 2, j = idx & 3;
@@ -41,6 +46,8 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
   if (tid == 0) {
     mbar_init(bar, 1);
     mbar_fence_init();
+    tma_prefetch_desc(&m32);
+    tma_prefetch_desc(&m16);
   }
   if (warp == 0) tmem_alloc(tmem_slot, 64);
   fence_proxy_async_smem();
@@ -100,25 +107,37 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
     mbar_wait(bar, phase, SCB_ERR_WAIT_ATTN);
     phase ^= 1;
     tc_fence_after();
+    // the previous tile's stores must have finished reading the staging buffers
+    if (tid == 0) bulk_wait_group_read<0>();
+    __syncthreads();
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
       float v[16];
       tmem_ld16(trow + c, v);
-      if (p < npx) {
-        float4* d32 = reinterpret_cast<float4*>(out32 + p * 64 + c);
+      // f32 slab c / 32, 16-byte chunks (c % 32) / 4 .. + 3; fp16 slab, chunks c / 8, c / 8 + 1
+      uint8_t* s32 = st + (c >> 5) * 16384;
 #pragma unroll
-        for (int h4 = 0; h4 < 4; ++h4) d32[h4] = make_float4(v[4 * h4], v[4 * h4 + 1], v[4 * h4 + 2], v[4 * h4 + 3]);
-        uint4* d16 = reinterpret_cast<uint4*>(out16 + p * 64 + c);
+      for (int h4 = 0; h4 < 4; ++h4)
+        *reinterpret_cast<float4*>(s32 + swz_off(tid, ((c & 31) >> 2) + h4, 128)) =
+            make_float4(v[4 * h4], v[4 * h4 + 1], v[4 * h4 + 2], v[4 * h4 + 3]);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2)
-          d16[h2] = make_uint4(pack_half2(v[8 * h2], v[8 * h2 + 1]), pack_half2(v[8 * h2 + 2], v[8 * h2 + 3]),
-                               pack_half2(v[8 * h2 + 4], v[8 * h2 + 5]), pack_half2(v[8 * h2 + 6], v[8 * h2 + 7]));
-      }
+      for (int h2 = 0; h2 < 2; ++h2)
+        *reinterpret_cast<uint4*>(st + 2 * 16384 + swz_off(tid, (c >> 3) + h2, 128)) =
+            make_uint4(pack_half2(v[8 * h2], v[8 * h2 + 1]), pack_half2(v[8 * h2 + 2], v[8 * h2 + 3]),
+                       pack_half2(v[8 * h2 + 4], v[8 * h2 + 5]), pack_half2(v[8 * h2 + 6], v[8 * h2 + 7]));
     }
+    fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();  // the A tile and TMEM are reused by the next tile
+    __syncthreads();  // staging complete; the A tile and TMEM are free for the next tile
     tc_fence_after();
+    if (tid == 0) {
+      tma_store_2d(&m32, st, 0, (int)(tile * 128));
+      tma_store_2d(&m32, st + 16384, 32, (int)(tile * 128));
+      tma_store_2d(&m16, st + 2 * 16384, 0, (int)(tile * 128));
+      bulk_commit_group();
+    }
   }
+  if (tid == 0) bulk_wait_group<0>();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 }

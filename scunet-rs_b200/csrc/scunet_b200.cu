@@ -501,6 +501,8 @@ struct Op {
   int mlp_t = 0;
   MlpGeom mlp{};
   CUtensorMap mlp_a, mlp_w0, mlp_w2;
+  // HEAD: the x1 (f32) and shadow (fp16) planes as TMA store maps
+  CUtensorMap head_m32, head_m16;
 };
 
 // A row band of one image (config 5): full-resolution rows [R0, R0 + rows) of the
@@ -753,7 +755,7 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* out32, __half* out16, cudaStream_t st);
+cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, const Op& op, cudaStream_t st);
 
 cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
   using L = Trans32Layout;
@@ -815,7 +817,7 @@ cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
   return cudaErrorInvalidConfiguration;
 }
 
-cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* out32, __half* out16, cudaStream_t st) {
+cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, const Op& op, cudaStream_t st) {
   static bool attr_set[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -824,9 +826,9 @@ cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, float* o
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const long tiles = ((long)g.n * g.hp * g.wp + 127) / 128;
-  const int grid = (int)std::max(1L, std::min(tiles, (long)ctx->sms * 6));
-  head_tc_kernel<<<grid, 128, HEAD_SMEM, st>>>(x, ctx->whead16, out32, out16, g);
+  const long tiles = ((long)g.n * g.rows * g.wp + 127) / 128;
+  const int grid = (int)std::max(1L, std::min(tiles, (long)ctx->sms * 3));
+  head_tc_kernel<<<grid, 128, HEAD_SMEM, st>>>(x, ctx->whead16, op.head_m32, op.head_m16, g);
   return cudaGetLastError();
 }
 
@@ -910,7 +912,7 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
     case Op::HEAD: {
       const Region R = region_of(A, 0);
       HeadGeom g{R.n, io.c, io.h, io.w, A.hp, A.wp, io.x_u8, R.grow0, R.rows};
-      return launch_head(ctx, io.x, g, A.skip[0] + R.off(64), A.xs[0] + R.off(64), st);
+      return launch_head(ctx, io.x, g, op, st);
     }
     case Op::TAIL: {
       GemmOp t = op.gemm;  // the 3x3 implicit GEMM over the (y + x1) shadow, N = 16
@@ -1314,6 +1316,13 @@ int build_plan(scb_ctx* ctx, Arena& A) {
   head.kind = Op::HEAD;
   head.tag = TAG_HEAD;
   head.flops = 2.0 * P0 * 9 * ctx->in_nc * 64;
+  {
+    const uint64_t d[2] = {64, (uint64_t)P0}, s32[1] = {256}, s16[1] = {128};
+    const uint32_t b32[2] = {32, 128}, b16[2] = {64, 128};
+    if (!encode_map(&head.head_m32, A.skip[0] + R0.off(64), 2, d, s32, b32, 4, 128, err) ||
+        !encode_map(&head.head_m16, A.xs[0] + R0.off(64), 2, d, s16, b16, 2, 128, err))
+      return fail(ctx, SCB_EINVAL, err);
+  }
   ops.push_back(head);
   for (int s = 0; s < 7; ++s) {
     const int lvl = kStageLevel[s];
