@@ -63,6 +63,9 @@ struct GemmGeom {
   // UP2: input width and c_out
   int up_w, up_cout;
   int stages;       // pipeline depth (runtime)
+  // 1: all of B (every k block of the op's single N tile) is loaded into shared
+  // memory once per CTA and stays there; the pipeline stages then carry A only
+  int b_res;
 };
 
 struct GemmEpi {
@@ -143,13 +146,20 @@ struct GemmSmem {
   static constexpr int A_BYTES = A_ROWS * BK * 2;
   static constexpr int B_BYTES = B_TAPS * BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // layout: stages (A, or A + B) | resident B (num_kb x B_BYTES, when b_res) | barriers | staging
+  __host__ __device__ static constexpr int stage_bytes(bool b_res) { return b_res ? A_BYTES : STAGE_BYTES; }
   // TMEM accumulator buffers: four for narrow tiles (so the loads and MMAs of the next
   // tiles run ahead while the epilogue drains one), two otherwise
   static constexpr int NACC = BN <= 64 ? 4 : 2;
   static constexpr int TMEM_COLS = (NACC * BN <= 32) ? 32 : (NACC * BN <= 64) ? 64 : (NACC * BN <= 128) ? 128
                                    : (NACC * BN <= 256) ? 256 : 512;
-  __host__ __device__ static constexpr int bar_off(int stages) { return stages * STAGE_BYTES; }
-  __host__ __device__ static constexpr int staging_off(int stages) { return stages * STAGE_BYTES + 1024; }
+  __host__ __device__ static constexpr int bres_off(int stages, bool b_res) { return stages * stage_bytes(b_res); }
+  __host__ __device__ static constexpr int bar_off(int stages, bool b_res, int num_kb) {
+    return bres_off(stages, b_res) + (b_res ? num_kb * B_BYTES : 0);
+  }
+  __host__ __device__ static constexpr int staging_off(int stages, bool b_res, int num_kb) {
+    return bar_off(stages, b_res, num_kb) + 1024;
+  }
 };
 
 // Where accumulator row `r` of M tile `mt` lives: returns the output pixel index
@@ -247,16 +257,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   constexpr uint32_t SWZ = (BK == 64) ? SW_128B : SW_64B;
   constexpr uint32_t IDESC = make_idesc_f16(128, BN);
   const int STAGES = g.stages;
+  const bool b_res = g.b_res != 0;
+  const int SBYTES = L::stage_bytes(b_res);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES));
+  uint8_t* bres = smem + L::bres_off(STAGES, b_res);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES, b_res, g.num_kb));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + L::NACC;
   uint64_t* res_full = acc_empty + L::NACC;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
-  uint8_t* staging = smem + L::staging_off(STAGES);
+  uint64_t* bres_full = res_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
+  uint8_t* staging = smem + L::staging_off(STAGES, b_res, g.num_kb);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = g.m_tiles * g.n_tiles;
@@ -271,6 +285,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(&acc_empty[a], 128);
     }
     for (int b = 0; b < 2; ++b) mbar_init(&res_full[b], 1);
+    mbar_init(bres_full, 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -286,6 +301,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      // B's B_TAPS boxes of k block kb (N tile n0) -> dst
+      auto load_b = [&](uint8_t* dst, uint64_t* bar, int kb, int n0) {
+        if (GEO == GEO_CONV3X) {
+          const int kx = kb % 3, ch = kb / 3;
+          const int cin = g.kb_per_tap * BK;
+#pragma unroll
+          for (int ky = 0; ky < 3; ++ky)
+            tma_load_2d(dst + ky * (BN * BK * 2), &tmB, bar, (ky * 3 + kx) * cin + ch * BK, n0);
+        } else {
+          tma_load_2d(dst, &tmB, bar, kb * BK, n0);
+        }
+      };
+      if (b_res && (int)blockIdx.x < total_tiles) {
+        mbar_arrive_expect_tx(bres_full, g.num_kb * L::B_BYTES);
+        for (int kb = 0; kb < g.num_kb; ++kb) load_b(bres + kb * L::B_BYTES, bres_full, kb, 0);
+      }
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
         const int n0 = nt * BN;
@@ -294,9 +325,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
-          uint8_t* sa = smem + s * L::STAGE_BYTES;
-          uint8_t* sb = sa + L::A_BYTES;
-          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          uint8_t* sa = smem + s * SBYTES;
+          mbar_arrive_expect_tx(&full[s], SBYTES);
           if (GEO == GEO_FLAT || GEO == GEO_UP2) {
             tma_load_2d(sa, &tmA, &full[s], kb * BK, mt * 128);
           } else if (GEO == GEO_CONV3) {
@@ -311,15 +341,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
             tma_load_5d(sa, &tmA, &full[s], ch * BK, tap & 1, x0, tap >> 1, y0);
           }
-          if (GEO == GEO_CONV3X) {
-            const int kx = kb % 3, ch = kb / 3;
-            const int cin = g.kb_per_tap * BK;
-#pragma unroll
-            for (int ky = 0; ky < 3; ++ky)
-              tma_load_2d(sb + ky * (BN * BK * 2), &tmB, &full[s], (ky * 3 + kx) * cin + ch * BK, n0);
-          } else {
-            tma_load_2d(sb, &tmB, &full[s], kb * BK, n0);
-          }
+          if (!b_res) load_b(sa + L::A_BYTES, &full[s], kb, n0);
         }
       }
     }
@@ -328,6 +350,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       uint32_t it = 0, t = 0;
       bool ok = true;
+      if (b_res && (int)blockIdx.x < total_tiles) {
+        ok = mbar_wait(bres_full, 0, SCB_ERR_WAIT_FULL);
+        tc_fence_after();
+      }
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t) {
         const uint32_t a = t % L::NACC, aph = (t / L::NACC) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, SCB_ERR_WAIT_ACC_FREE)) break;
@@ -337,8 +363,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, SCB_ERR_WAIT_FULL)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
-          const uint32_t sb = sa + L::A_BYTES;
+          const uint32_t sa = smem_u32(smem + s * SBYTES);
+          const uint32_t sb = b_res ? smem_u32(bres + kb * L::B_BYTES) : sa + L::A_BYTES;
           if (GEO == GEO_CONV3X) {
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky)

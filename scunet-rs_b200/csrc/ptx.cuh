@@ -218,6 +218,21 @@ __device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// The store counterpart: thread t writes row (lane base + t), columns [col, col + 16).
+// tmem_wait_st() before anything (an MMA, after a barrier) reads the columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_fence16(uint32_t* r) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
@@ -299,11 +314,20 @@ __device__ __forceinline__ uint32_t swz_off(uint32_t row, uint32_t chunk, uint32
   return row * row_bytes + (((chunk ^ phase) & mask) << 4);
 }
 
-// 2^x, hardware approximation (relative error ~2^-22, far below the fp16 rounding
-// every consumer of these values applies).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
+
+// 16-byte asynchronous global -> shared copy by this thread (bypassing L1); when
+// `valid` is false nothing is read and the 16 bytes are zero-filled. Completion is
+// per thread: cp_async_wait_all() makes this thread's copies visible to itself.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ __half2 tanh_approx_h2(__half2 x) {
   uint32_t y;
@@ -327,6 +351,8 @@ __device__ __forceinline__ __half2 gelu_tanh_h2(__half2 x) {
   return __hfma2(hx, t, hx);
 }
 
+// 2^x, hardware approximation (relative error ~2^-22, far below the fp16 rounding
+// every consumer of these values applies).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -121,19 +121,26 @@ struct GemmOp {
 
 // Pipeline depth and CTAs per SM for one op: GEMMs whose two accumulators fit in
 // half of TMEM (BN <= 128) try for two CTAs per SM (more epilogue warps in
-// flight); stages fill what shared memory is left after the epilogue staging.
-void plan_launch(int bn, int bk, int geo, int staging_bytes, int& stages, int& ctas, int& smem) {
-  const int stage_bytes = geo == GEO_CONV3X ? (160 + 3 * bn) * bk * 2 : (128 + bn) * bk * 2;
+// flight); stages fill what shared memory is left after the epilogue staging and,
+// when B is resident (`bres_bytes` > 0), after the whole of B.
+void plan_launch(int bn, int bk, int geo, int staging_bytes, int bres_bytes, int& stages, int& ctas, int& smem) {
+  const int a_bytes = (geo == GEO_CONV3X ? 160 : 128) * bk * 2;
+  const int stage_bytes = bres_bytes ? a_bytes : a_bytes + (geo == GEO_CONV3X ? 3 : 1) * bn * bk * 2;
   ctas = bn <= 128 ? 2 : 1;
   for (;;) {
-    const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes;
+    const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes -
+                       bres_bytes;
     stages = std::min(8, budget / stage_bytes);
     if (stages >= 2 || ctas == 1) break;
     ctas = 1;
   }
   stages = std::max(stages, 2);
-  smem = stages * stage_bytes + 1024 + staging_bytes + 1024;
+  smem = stages * stage_bytes + bres_bytes + 1024 + staging_bytes + 1024;
 }
+
+// B stays resident in shared memory when the op has one N tile and all of its k
+// blocks take at most this much (the 3x3 convs and 1x1 convs of the wide levels).
+constexpr int kMaxResidentB = 40 * 1024;
 
 template <int BN, int BK, int GEO, bool TMAEPI>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
@@ -148,10 +155,11 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const int staging = TMAEPI ? 2 * (op.e.st_res_bytes + op.e.st_out_bytes) : 0;
-  int stages, ctas, smem;
-  plan_launch(BN, BK, GEO, staging, stages, ctas, smem);
-  (void)L::STAGE_BYTES;
   GemmGeom g = op.g;
+  const int bres_bytes = g.num_kb * L::B_BYTES;
+  g.b_res = g.n_tiles == 1 && bres_bytes <= kMaxResidentB;
+  int stages, ctas, smem;
+  plan_launch(BN, BK, GEO, staging, g.b_res ? bres_bytes : 0, stages, ctas, smem);
   g.stages = stages;
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = std::max(1, std::min(tiles, sms * ctas));

@@ -15,7 +15,7 @@
 //    window s reads columns [32 s, 32 s + 32) of O', the product with its own V.
 //  * Shared memory: one 24 KB region holds, in turn, LN1 | Q | K, then P', then O,
 //    then LN2 | hidden chunk. With the resident weights (24 KB), V^T (8 KB) and the
-//    parameters that is ~64 KB per CTA.
+//    parameters and an 8 KB y_t staging buffer that is ~72 KB per CTA.
 //  * The hidden layer runs in two 64-wide chunks; the second chunk's mlp0 MMA is
 //    issued with the first chunk's mlp2 MMA, so the MLP costs three MMA round trips.
 //  * Scores carry log2(e): the relative-position table is staged pre-multiplied and
@@ -23,8 +23,11 @@
 //    The shifted-window mask is only evaluated for windows on the image's last
 //    window row or column (a warp's 32 tokens share one window).
 //
-// z = acc + y_t + b_proj + b_2 with acc = O.Wproj^T + GELU(hid).W2^T accumulated in
-// fp32 in TMEM, i.e. x1 + mlp with x1 = y_t + proj + b_proj.
+// x1 = y_t + O.Wproj^T + b_proj is written back into the proj accumulator's TMEM
+// columns, the mlp2 MMAs accumulate GELU(hid).W2^T onto it in fp32, and z = acc + b_2.
+// y_t reaches shared memory by per-thread cp.async: the next pair's copy is issued
+// once this pair has read it for the last time (x1), so its latency hides behind the
+// MLP and no register holds it across the softmax.
 #pragma once
 #include "trans.cuh"
 
@@ -46,7 +49,8 @@ struct Trans32Layout {
   static constexpr int P_BQKV = 0, P_BPROJ = 3 * T, P_B0 = 4 * T, P_B2 = 8 * T, P_L1G = 9 * T, P_L1B = 10 * T,
                        P_L2G = 11 * T, P_L2B = 12 * T, P_RP = 13 * T, P_N = 13 * T + 225;
   static constexpr int RED = (PAR + P_N * 4 + 15) & ~15;  // 2 x [2 halves x 128 rows] float2
-  static constexpr int BAR = RED + 2 * 256 * 8;
+  static constexpr int YB = RED + 2 * 256 * 8;       // y_t: 2 x [256 threads x 16 B], thread-private
+  static constexpr int BAR = YB + 2 * 256 * 16;
   static constexpr int SMEM = BAR + 64 + 1024;
   static constexpr int TMEM_COLS = 128;
   static constexpr int C_HID = 64;
@@ -102,16 +106,6 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
   const int qi = tok >> 3, qj = tok & 7;
   const long n_pairs = (g.win.n_windows + 1) / 2;
   constexpr float kScaleLog2e = 0.17677669529663687f * 1.4426950408889634f;  // 32^-1/2 log2(e)
-  // this token's mask pattern over its thread's 32 keys (bit j: key hf*32 + j) when
-  // its window is on the last window row / column: the cyclic shift put tokens from
-  // opposite image edges into one window (cuda/scunet.cu:137-147)
-  uint32_t mrow = 0, mcol = 0;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int kt = hf * 32 + j;
-    mrow |= (uint32_t)((qi < 4) != ((kt >> 3) < 4)) << j;
-    mcol |= (uint32_t)((qj < 4) != ((kt & 7) < 4)) << j;
-  }
 
   auto locate = [&](long pr, bool& lr, bool& lc, bool& st) -> long {
     const long win = 2 * pr + slot;
@@ -178,31 +172,33 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
       }
     }
   };
-  auto load_half = [&](long pix, uint4* dst) {
+  // this thread's 16 channels of the token's y_t row, fetched asynchronously into
+  // its private 32 bytes of YB (zeros past the image) and read back where used
+  auto fetch_y = [&](long pix) {
+    const __half* src = pix >= 0 ? g.y + pix * T + hf * 16 : g.y;
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
-      dst[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * T + hf * 16) + c)
-                        : make_uint4(0, 0, 0, 0);
+    for (int c = 0; c < 2; ++c) cp_async16(sm + L::YB + c * 4096 + tid * 16, src + 8 * c, pix >= 0);
+    cp_async_commit();
+  };
+  auto read_y = [&](float* yt) {
+    uint4 u[2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) u[c] = *reinterpret_cast<const uint4*>(sm + L::YB + c * 4096 + tid * 16);
+    unpack16(u, yt);
   };
 
   long pair = blockIdx.x;
-  bool lr_n, lc_n, st_n;
-  long pix_n = locate(pair, lr_n, lc_n, st_n);
+  bool last_row, last_col, store;
+  long pix = locate(pair, last_row, last_col, store);
+  fetch_y(pix);
 
   for (; pair < n_pairs; pair += gridDim.x) {
-    const long pix = pix_n;
-    const bool last_row = lr_n, last_col = lc_n, store = st_n;
-    // y_t stays packed (it is fp16 data) and is unpacked where it is used
-    uint4 ycur[2];
-    load_half(pix, ycur);
-    // the next pair's tokens are pulled into L2 while this pair computes
-    pix_n = locate(pair + gridDim.x, lr_n, lc_n, st_n);
-    if (pix_n >= 0) prefetch_l2(g.y + pix_n * T + hf * 16);
+    cp_async_wait_all();
 
     // ---- LN1 -> A1; qkv = A1 . Wqkv^T -> TMEM [0, 96) ----
     {
       float yt[16], o[16];
-      unpack16(ycur, yt);
+      read_y(yt);
       layer_norm16(yt, L::P_L1G, L::P_L1B, o);
       put16(L::R_A1, o);
     }
@@ -270,9 +266,14 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
         s[j] = fmaf(s[j], kScaleLog2e, bh[-((kt >> 3) * 15 + (kt & 7))]);
       }
       if (last_row || last_col) {  // warp-uniform: the warp's tokens share a window
-        const uint32_t m = (last_row ? mrow : 0u) | (last_col ? mcol : 0u);
+        // the cyclic shift put tokens from opposite image edges into windows of the
+        // last window row / column; a token attends only to keys from its own side
+        // (cuda/scunet.cu:137-147). Key hf*32 + j sits in window row 4 hf + j / 8
+        // (top half iff hf = 0) and column j % 8.
+        const bool rmask = last_row && ((qi < 4) != (hf == 0));
+        const bool qleft = qj < 4;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s[j] = (m >> j) & 1u ? -INFINITY : s[j];
+        for (int j = 0; j < 32; ++j) s[j] = (rmask || (last_col && (qleft != ((j & 7) < 4)))) ? -INFINITY : s[j];
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) mx = fmaxf(mx, s[j]);
@@ -325,11 +326,14 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
     }
     wait_mma();
 
-    // ---- x1 = proj + y_t + b_proj; LN2 -> A1; hid_0 = A1 . W0[0:64]^T -> TMEM [64, 128) ----
+    // ---- x1 = proj + y_t + b_proj, back into TMEM [0, 32) where mlp2 accumulates
+    //      onto it; LN2 -> A1; hid_0 = A1 . W0[0:64]^T -> TMEM [64, 128) ----
+    bool lr_n, lc_n, st_n;
+    long pix_n;
     {
       float x1[16], o[16], yt[16];
       tmem_ld16(trow + hf * 16, x1);
-      unpack16(ycur, yt);
+      read_y(yt);
       const float4* bp4 = reinterpret_cast<const float4*>(par + L::P_BPROJ + hf * 16);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -339,8 +343,13 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
         x1[4 * q + 2] += yt[4 * q + 2] + b.z;
         x1[4 * q + 3] += yt[4 * q + 3] + b.w;
       }
+      tmem_st16(trow + hf * 16, x1);
       layer_norm16(x1, L::P_L2G, L::P_L2B, o);
       put16(L::R_A1, o);
+      tmem_wait_st();
+      // the next pair's y_t is fetched while this pair's MLP runs (YB is free now)
+      pix_n = locate(pair + gridDim.x, lr_n, lc_n, st_n);
+      fetch_y(pix_n);
     }
     sync_mma();
     if (tid == 0) {
@@ -397,21 +406,19 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
       wait_mma();
     }
 
-    // ---- z = acc + y_t + b_proj + b_2 -> Z[:, 32:64) ----
+    // ---- z = acc + b_2 (acc = x1 + mlp2) -> Z[:, 32:64) ----
     {
-      float m[16], yt[16];
+      float m[16];
       tmem_ld16(trow + hf * 16, m);
-      unpack16(ycur, yt);
       if (pix >= 0 && store) {
-        const float4* bp4 = reinterpret_cast<const float4*>(par + L::P_BPROJ + hf * 16);
         const float4* b24 = reinterpret_cast<const float4*>(par + L::P_B2 + hf * 16);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float4 bp = bp4[q], b2 = b24[q];
-          m[4 * q] += yt[4 * q] + bp.x + b2.x;
-          m[4 * q + 1] += yt[4 * q + 1] + bp.y + b2.y;
-          m[4 * q + 2] += yt[4 * q + 2] + bp.z + b2.z;
-          m[4 * q + 3] += yt[4 * q + 3] + bp.w + b2.w;
+          const float4 b2 = b24[q];
+          m[4 * q] += b2.x;
+          m[4 * q + 1] += b2.y;
+          m[4 * q + 2] += b2.z;
+          m[4 * q + 3] += b2.w;
         }
         uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * 16);
 #pragma unroll
@@ -423,7 +430,12 @@ __global__ void __launch_bounds__(256, Trans32Layout::CTAS) trans32_kernel(const
     tc_fence_before();
     __syncthreads();  // TMEM and shared memory are reused by the next pair
     tc_fence_after();
+    pix = pix_n;
+    last_row = lr_n;
+    last_col = lc_n;
+    store = st_n;
   }
+  cp_async_wait_all();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, L::TMEM_COLS);
 }

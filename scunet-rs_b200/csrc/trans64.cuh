@@ -366,7 +366,8 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
     }
     wait_mma();
 
-    // ---- x1 = proj + y_t + b_proj; LN2 -> A1; hid_0 ----
+    // ---- x1 = proj + y_t + b_proj, back into TMEM [0, 64) where mlp2 accumulates
+    //      onto it; LN2 -> A1; hid_0 ----
     {
       float x1[32], yt[32];
       tmem_ld16x2(trow + hf * 32, x1, trow + hf * 32 + 16, x1 + 16);
@@ -380,8 +381,11 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
         x1[4 * q + 2] += yt[4 * q + 2] + b.z;
         x1[4 * q + 3] += yt[4 * q + 3] + b.w;
       }
+      tmem_st16(trow + hf * 32, x1);
+      tmem_st16(trow + hf * 32 + 16, x1 + 16);
       layer_norm32(x1, L::P_L2G, L::P_L2B);
       put32(L::R, x1);
+      tmem_wait_st();
     }
     sync_mma();
     if (issuer) {
@@ -424,21 +428,19 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
       wait_mma();
     }
 
-    // ---- z = acc + y_t + b_proj + b_2 -> Z[:, 64:128) ----
+    // ---- z = acc + b_2 (acc = x1 + mlp2) -> Z[:, 64:128) ----
     {
-      float m[32], yt[32];
+      float m[32];
       tmem_ld16x2(trow + hf * 32, m, trow + hf * 32 + 16, m + 16);
-      unpack32(ycur, yt);
       if (pix >= 0 && store) {
-        const float4* bp4 = reinterpret_cast<const float4*>(par + L::P_BPROJ + hf * 32);
         const float4* b24 = reinterpret_cast<const float4*>(par + L::P_B2 + hf * 32);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float4 bp = bp4[q], b2 = b24[q];
-          m[4 * q] += yt[4 * q] + bp.x + b2.x;
-          m[4 * q + 1] += yt[4 * q + 1] + bp.y + b2.y;
-          m[4 * q + 2] += yt[4 * q + 2] + bp.z + b2.z;
-          m[4 * q + 3] += yt[4 * q + 3] + bp.w + b2.w;
+          const float4 b2 = b24[q];
+          m[4 * q] += b2.x;
+          m[4 * q + 1] += b2.y;
+          m[4 * q + 2] += b2.z;
+          m[4 * q + 3] += b2.w;
         }
         uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * 32);
 #pragma unroll
