@@ -40,13 +40,25 @@
 
 namespace scb {
 
-enum Geo : int { GEO_FLAT = 0, GEO_CONV3 = 1, GEO_DOWN2 = 2, GEO_UP2 = 3, GEO_CONV3X = 4 };
+enum Geo : int { GEO_FLAT = 0, GEO_CONV3 = 1, GEO_DOWN2 = 2, GEO_UP2 = 3, GEO_CONV3X = 4, GEO_CONV3W = 5 };
 
 // GEO_CONV3X: the 3x3 conv with 8-row x 16-column output tiles and one TMA box per
 // column shift kx: the box covers the tile's 10 input rows (halo included), and the
 // three row taps ky are 16-row views into it (UMMA descriptors at +16*ky rows). A
 // tile reads 3 x 160 instead of 9 x 128 input pixel-rows.
-__host__ __device__ constexpr bool is_conv3(int geo) { return geo == GEO_CONV3 || geo == GEO_CONV3X; }
+//
+// GEO_CONV3W: the 3x3 conv with 16-row x 8-column output tiles and ONE TMA box per
+// channel chunk: the box covers the tile's 18 x 10 input pixels (halo rows and
+// columns), and each of the nine taps (ky, kx) is a view into it: output row m =
+// (r, c) of the tile reads box pixel (r + ky, c + kx), i.e. the operand's 8-row
+// groups (one tile row each) start at box row 10 (r + ky) + kx and lie 10 box rows
+// apart. The box is 20 rows high (two unused) so that it holds a whole number of
+// 8-row swizzle atoms. A tile reads 200 input pixel-rows instead of 480 (CONV3X)
+// or 1152 (CONV3).
+__host__ __device__ constexpr bool is_conv3(int geo) {
+  return geo == GEO_CONV3 || geo == GEO_CONV3X || geo == GEO_CONV3W;
+}
+constexpr int kConv3wTW = 8, kConv3wTH = 16, kConv3wBoxRows = kConv3wTH + 4;
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
 
 struct GemmGeom {
@@ -104,6 +116,7 @@ struct GemmEpi {
   // (GEO_FLAT, no activation, fp16 residual at most).
   int st_res16, st_res32, st_skip, st_out16, st_out32, st_ln;
   int st_res_bytes, st_out_bytes;  // bytes of one buffer of all residual / output slabs
+  int res_bufs;                    // residual buffers (2..4): slabs are requested res_bufs - 1 ahead
 };
 
 // Tensor maps of the epilogue streams (TMA epilogue only); box = 32 columns x the
@@ -141,9 +154,12 @@ __device__ __forceinline__ void load_res(const GemmEpi& e, long p, int oc, ResCh
 // smem: [stages x (A tile | B tile)] [barriers, tmem slot: 1 KB] [TMA-epilogue staging]
 template <int BN, int BK, int GEO = GEO_FLAT>
 struct GemmSmem {
-  static constexpr int A_ROWS = GEO == GEO_CONV3X ? 160 : 128;  // CONV3X: 10 input rows x 16 columns
-  static constexpr int B_TAPS = GEO == GEO_CONV3X ? 3 : 1;      // CONV3X: the three ky taps of one kx
-  static constexpr int A_BYTES = A_ROWS * BK * 2;
+  // CONV3X: 10 input rows x 16 columns; CONV3W: 20 x 10
+  static constexpr int A_ROWS = GEO == GEO_CONV3X ? 160 : GEO == GEO_CONV3W ? kConv3wBoxRows * (kConv3wTW + 2) : 128;
+  // CONV3X: the three ky taps of one kx; CONV3W: all nine taps
+  static constexpr int B_TAPS = GEO == GEO_CONV3X ? 3 : GEO == GEO_CONV3W ? 9 : 1;
+  static constexpr int A_TX = A_ROWS * BK * 2;                    // bytes one A box delivers
+  static constexpr int A_BYTES = (A_TX + 1023) / 1024 * 1024;      // its slot: stages stay 1024-aligned
   static constexpr int B_BYTES = B_TAPS * BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // layout: stages (A, or A + B) | resident B (num_kb x B_BYTES, when b_res) | barriers | staging
@@ -268,7 +284,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + L::NACC;
   uint64_t* res_full = acc_empty + L::NACC;
-  uint64_t* bres_full = res_full + 2;
+  uint64_t* bres_full = res_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
   uint8_t* staging = smem + L::staging_off(STAGES, b_res, g.num_kb);
 
@@ -284,7 +300,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
     }
-    for (int b = 0; b < 2; ++b) mbar_init(&res_full[b], 1);
+    for (int b = 0; b < 4; ++b) mbar_init(&res_full[b], 1);
     mbar_init(bres_full, 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
@@ -309,6 +325,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int ky = 0; ky < 3; ++ky)
             tma_load_2d(dst + ky * (BN * BK * 2), &tmB, bar, (ky * 3 + kx) * cin + ch * BK, n0);
+        } else if (GEO == GEO_CONV3W) {
+          const int cin = g.kb_per_tap * BK;
+#pragma unroll
+          for (int tap = 0; tap < 9; ++tap) tma_load_2d(dst + tap * (BN * BK * 2), &tmB, bar, tap * cin + kb * BK, n0);
         } else {
           tma_load_2d(dst, &tmB, bar, kb * BK, n0);
         }
@@ -326,7 +346,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
           uint8_t* sa = smem + s * SBYTES;
-          mbar_arrive_expect_tx(&full[s], SBYTES);
+          mbar_arrive_expect_tx(&full[s], b_res ? L::A_TX : L::A_TX + L::B_BYTES);
           if (GEO == GEO_FLAT || GEO == GEO_UP2) {
             tma_load_2d(sa, &tmA, &full[s], kb * BK, mt * 128);
           } else if (GEO == GEO_CONV3) {
@@ -337,6 +357,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // k block = (channel chunk, kx): one 10 x 16 box, three weight taps
             const int kx = kb % 3, ch = kb / 3;
             tma_load_4d(sa, &tmA, &full[s], ch * BK, x0 + kx - 1, y0 - 1, img);
+          } else if (GEO == GEO_CONV3W) {
+            // k block = channel chunk: one 20 x 10 box, all nine weight taps
+            tma_load_4d(sa, &tmA, &full[s], kb * BK, x0 - 1, y0 - 1, img);
           } else {  // GEO_DOWN2
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
             tma_load_5d(sa, &tmA, &full[s], ch * BK, tap & 1, x0, tap >> 1, y0);
@@ -372,6 +395,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               for (int k = 0; k < BK / 16; ++k)
                 umma_f16(d_tmem, make_sdesc(sa + ky * 16 * ROWB + k * 32, ROWB, SWZ),
                          make_sdesc(sb + ky * (BN * BK * 2) + k * 32, ROWB, SWZ), IDESC, (kb | ky | k) != 0);
+          } else if (GEO == GEO_CONV3W) {
+            constexpr uint32_t BW = kConv3wTW + 2;  // box row pitch in pixels
+#pragma unroll
+            for (int tap = 0; tap < 9; ++tap)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                umma_f16(d_tmem,
+                         make_sdesc_sbo(sa + ((tap / 3) * BW + tap % 3) * ROWB + k * 32, BW * ROWB, SWZ),
+                         make_sdesc(sb + tap * (BN * BK * 2) + k * 32, ROWB, SWZ), IDESC, (kb | tap | k) != 0);
           } else {
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
@@ -391,22 +423,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool elected = (warp == 2 && lane == 0);
     const bool has_res = e.st_res16 >= 0 || e.st_res32 >= 0 || e.st_skip >= 0;
     uint32_t t = 0, rs = 0, os = 0;  // tiles, residual slabs consumed, output slabs stored
-    uint8_t* out_stage = staging + 2 * e.st_res_bytes;
+    const uint32_t NRES = (uint32_t)e.res_bufs;
+    uint8_t* out_stage = staging + NRES * e.st_res_bytes;
     auto issue_res = [&](int mt, int col, uint32_t idx) {
-      const uint32_t b = idx & 1;
+      const uint32_t b = idx % NRES;
       uint8_t* base = staging + b * e.st_res_bytes;
       mbar_arrive_expect_tx(&res_full[b], e.st_res_bytes);
       if (e.st_res16 >= 0) epi_slab_load<GEO>(base + e.st_res16, &em.res16, &res_full[b], col, mt, g);
       if (e.st_res32 >= 0) epi_slab_load<GEO>(base + e.st_res32, &em.res32, &res_full[b], col, mt, g);
       if (e.st_skip >= 0) epi_slab_load<GEO>(base + e.st_skip, &em.skip, &res_full[b], col, mt, g);
     };
-    // Residual slabs are requested one slab ahead, across tile boundaries: the last
-    // slab of a tile requests slab 0 of the CTA's next tile, so the first slab of a
-    // tile never waits a full DRAM round trip.
-    if (has_res && elected && (int)blockIdx.x < total_tiles) {
-      const int mt0 = blockIdx.x / g.n_tiles;
-      issue_res(mt0, (blockIdx.x - mt0 * g.n_tiles) * BN, 0);
-    }
+    // Residual slabs are requested NRES - 1 slabs ahead, across tile boundaries:
+    // slab j of this CTA is 32-column slab j % (BN / 32) of its tile j / (BN / 32),
+    // so the first slabs of a tile never wait a full DRAM round trip.
+    constexpr uint32_t SPT = BN >= 32 ? BN / 32 : 1;  // slabs per tile
+    auto issue_slab = [&](uint32_t j) {
+      const int tile = (int)blockIdx.x + (int)(j / SPT) * (int)gridDim.x;
+      if (tile >= total_tiles) return;
+      const int mt = tile / g.n_tiles;
+      issue_res(mt, (tile - mt * g.n_tiles) * BN + (int)(j % SPT) * 32, j);
+    };
+    if (has_res && elected)
+      for (uint32_t j = 0; j + 1 < NRES; ++j) issue_slab(j);
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
       const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
       const int n0 = nt * BN;
@@ -459,15 +497,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32, ++os) {
-        if (has_res && elected) {
-          // buffer (rs + 1) & 1 was released by the previous slab's second barrier
-          if (c + 32 < BN) {
-            issue_res(mt, n0 + c + 32, rs + 1);
-          } else if (tile + (int)gridDim.x < total_tiles) {
-            const int nxt = tile + gridDim.x, mtn = nxt / g.n_tiles;
-            issue_res(mtn, (nxt - mtn * g.n_tiles) * BN, rs + 1);
-          }
-        }
+        // buffer (rs + NRES - 1) % NRES held slab rs - 1, which every thread finished
+        // reading before the previous slab's second barrier
+        if (has_res && elected) issue_slab(rs + NRES - 1);
         float v[32];
         tmem_ld16x2(tbase + c, v, tbase + c + 16, v + 16);
         const int n = n0 + c;
@@ -490,8 +522,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         float sk[32];
         if (has_res) {
-          const uint32_t b = rs & 1;
-          mbar_wait(&res_full[b], (rs >> 1) & 1, SCB_ERR_WAIT_ACC);
+          const uint32_t b = rs % NRES;
+          mbar_wait(&res_full[b], (rs / NRES) & 1, SCB_ERR_WAIT_ACC);
           const uint8_t* base = staging + b * e.st_res_bytes;
           if (e.st_res16 >= 0) {
 #pragma unroll

@@ -296,6 +296,18 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t row_byte
   return d;
 }
 
+// The same with an explicit 8-row group stride (bytes): an operand whose rows are
+// gathered from a larger swizzled tile, groups `sbo` apart.
+__device__ __forceinline__ uint64_t make_sdesc_sbo(uint32_t saddr, uint32_t sbo, uint32_t swz) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)swz << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major.
 __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
   return (1u << 4)                       // D format: f32

@@ -123,9 +123,9 @@ struct GemmOp {
 // half of TMEM (BN <= 128) try for two CTAs per SM (more epilogue warps in
 // flight); stages fill what shared memory is left after the epilogue staging and,
 // when B is resident (`bres_bytes` > 0), after the whole of B.
-void plan_launch(int bn, int bk, int geo, int staging_bytes, int bres_bytes, int& stages, int& ctas, int& smem) {
-  const int a_bytes = (geo == GEO_CONV3X ? 160 : 128) * bk * 2;
-  const int stage_bytes = bres_bytes ? a_bytes : a_bytes + (geo == GEO_CONV3X ? 3 : 1) * bn * bk * 2;
+void plan_launch(int bn, int a_bytes, int b_bytes, int staging_bytes, int bres_bytes, int& stages, int& ctas,
+                 int& smem) {
+  const int stage_bytes = bres_bytes ? a_bytes : a_bytes + b_bytes;
   ctas = bn <= 128 ? 2 : 1;
   for (;;) {
     const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes -
@@ -142,6 +142,10 @@ void plan_launch(int bn, int bk, int geo, int staging_bytes, int bres_bytes, int
 // blocks take at most this much (the 3x3 convs and 1x1 convs of the wide levels).
 constexpr int kMaxResidentB = 40 * 1024;
 
+// Residual slab buffers of the TMA epilogue. Four (three slabs of lookahead) were
+// measured slower than two: the extra staging costs the 1x1 convs pipeline stages.
+constexpr int kResBufs = 2;
+
 template <int BN, int BK, int GEO, bool TMAEPI>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   using L = GemmSmem<BN, BK, GEO>;
@@ -154,16 +158,18 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int staging = TMAEPI ? 2 * (op.e.st_res_bytes + op.e.st_out_bytes) : 0;
+  GemmEpi e = op.e;
+  e.res_bufs = e.st_res_bytes ? kResBufs : 2;
+  const int staging = TMAEPI ? e.res_bufs * e.st_res_bytes + 2 * e.st_out_bytes : 0;
   GemmGeom g = op.g;
   const int bres_bytes = g.num_kb * L::B_BYTES;
   g.b_res = g.n_tiles == 1 && bres_bytes <= kMaxResidentB;
   int stages, ctas, smem;
-  plan_launch(BN, BK, GEO, staging, g.b_res ? bres_bytes : 0, stages, ctas, smem);
+  plan_launch(BN, L::A_BYTES, L::B_BYTES, staging, g.b_res ? bres_bytes : 0, stages, ctas, smem);
   g.stages = stages;
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = std::max(1, std::min(tiles, sms * ctas));
-  kfn<<<grid, 192, smem, st>>>(op.ta, op.tb, g, op.e, op.em);
+  kfn<<<grid, 192, smem, st>>>(op.ta, op.tb, g, e, op.em);
   return cudaGetLastError();
 }
 
@@ -181,6 +187,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_TCASE(256, 64, GEO_FLAT)
   SCB_GEMM_TCASE(128, 32, GEO_FLAT)
   SCB_GEMM_TCASE(32, 32, GEO_CONV3X)
+  SCB_GEMM_TCASE(32, 32, GEO_CONV3W)
   SCB_GEMM_TCASE(64, 64, GEO_CONV3X)
   SCB_GEMM_TCASE(128, 64, GEO_CONV3X)
   SCB_GEMM_TCASE(256, 64, GEO_CONV3)
@@ -209,7 +216,7 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
 
 bool tma_epi_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{64, 64, GEO_FLAT},   {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
-                               {128, 32, GEO_FLAT},  {32, 32, GEO_CONV3X}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
+                               {128, 32, GEO_FLAT},  {32, 32, GEO_CONV3X}, {32, 32, GEO_CONV3W}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
                                {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}};
   for (auto& r : tab)
     if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
@@ -298,8 +305,9 @@ struct Maker {
 
   // 3x3 implicit GEMM over n images of H x W, input channels [0, cin) of an fp16
   // NHWC buffer whose pixel stride is pix_ld elements.
-  // `kx_boxes`: use the GEO_CONV3X schedule (8 x 16 tiles, one box per column
-  // shift); only compiled with the TMA epilogue, for cout <= 128.
+  // `kx_boxes`: use a schedule with fewer, larger input boxes: GEO_CONV3W (16 x 8
+  // tiles, one box per channel chunk) where compiled, else GEO_CONV3X (8 x 16
+  // tiles, one box per column shift); both only with the TMA epilogue.
   // Output rows [row0, row0 + rows_out) of each image's H stored rows (default:
   // all of them); rows outside are read as input (halo) but never written.
   bool conv3(GemmOp& op, const __half* x, int n, int H, int W, int cin, long pix_ld, const __half* w, int cout,
@@ -307,7 +315,10 @@ struct Maker {
     if (rows_out < 0) rows_out = H - row0;
     op.bk = (cin % 64 == 0) ? 64 : 32;
     op.bn = cout;
-    op.geo = (kx_boxes && tma_epi_supported(GEO_CONV3X, op.bn, op.bk)) ? GEO_CONV3X : GEO_CONV3;
+    op.geo = !kx_boxes                                                 ? GEO_CONV3
+             : tma_epi_supported(GEO_CONV3W, op.bn, op.bk)              ? GEO_CONV3W
+             : tma_epi_supported(GEO_CONV3X, op.bn, op.bk)              ? GEO_CONV3X
+                                                                         : GEO_CONV3;
     if ((op.geo == GEO_CONV3 && !gemm_supported(op.geo, op.bn, op.bk)) || cin % 32) {
       *err = "no conv3x3 variant for cin=" + std::to_string(cin) + " cout=" + std::to_string(cout);
       return false;
@@ -316,19 +327,25 @@ struct Maker {
     if (op.geo == GEO_CONV3X) {
       TW = 16;
       TH = 8;
+    } else if (op.geo == GEO_CONV3W) {
+      TW = kConv3wTW;
+      TH = kConv3wTH;
     } else {
       pick_tile(W, TW, TH);
     }
-    const int box_rows = op.geo == GEO_CONV3X ? TH + 2 : TH;
+    const int box_rows = op.geo == GEO_CONV3X ? TH + 2 : op.geo == GEO_CONV3W ? kConv3wBoxRows : TH;
+    const int box_cols = op.geo == GEO_CONV3W ? TW + 2 : TW;
     const uint64_t dims[4] = {(uint64_t)cin, (uint64_t)W, (uint64_t)H, (uint64_t)n};
     const uint64_t str[3] = {(uint64_t)pix_ld * 2, (uint64_t)W * pix_ld * 2, (uint64_t)H * W * pix_ld * 2};
-    const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)box_rows, 1};
+    const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)box_cols, (uint32_t)box_rows, 1};
     if (!encode_map(&op.ta, x, 4, dims, str, box, 2, op.bk * 2, *err)) return false;
     if (!mapB(op, w, cout, 9 * cin)) return false;
     op.g.M = n * H * W;
     op.g.n_total = cout;
     op.g.kb_per_tap = cin / op.bk;
-    op.g.num_kb = op.geo == GEO_CONV3X ? 3 * op.g.kb_per_tap : 9 * op.g.kb_per_tap;
+    op.g.num_kb = op.geo == GEO_CONV3X ? 3 * op.g.kb_per_tap
+                  : op.geo == GEO_CONV3W ? op.g.kb_per_tap
+                                         : 9 * op.g.kb_per_tap;
     op.g.row0 = row0;
     op.g.rows_out = rows_out;
     op.g.H = H;
@@ -384,7 +401,7 @@ struct Maker {
       const uint64_t str[1] = {(uint64_t)ld * es};
       const uint32_t box[2] = {32, 128};
       return encode_map(m, base, 2, dims, str, box, es, sw, *err);
-    } else if (op.geo == GEO_CONV3 || op.geo == GEO_CONV3X) {
+    } else if (is_conv3(op.geo)) {
       // rows past the op's output range are clipped on store and read as zero
       const uint64_t n = (uint64_t)g.M / ((uint64_t)g.H * g.W);
       const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)(g.row0 + g.rows_out), n};

@@ -76,6 +76,7 @@ def conv3_ref(torch, x16, w, act, r16):
 @pytest.mark.parametrize("n,H,W,cin,act,res", [
     (2, 16, 24, 32, 1, False), (1, 8, 8, 64, 0, True), (1, 16, 32, 128, 1, False), (1, 8, 16, 256, 0, True),
     (2, 64, 64, 32, 0, True), (1, 8, 136, 64, 1, False), (1, 12, 40, 64, 1, True), (3, 20, 24, 128, 0, True),
+    (1, 20, 44, 32, 1, True), (2, 36, 18, 32, 0, False),
 ])
 def test_conv3x3(be3, n, H, W, cin, act, res):
     torch = _torch()
