@@ -33,7 +33,7 @@
 #include "gemm.cuh"
 #include "io_kernels.cuh"
 #include "trans.cuh"
-#include "trans32.cuh"
+#include "trans32ws.cuh"
 #include "trans64.cuh"
 #include "mlp.cuh"
 
@@ -490,6 +490,9 @@ struct BlockW {
   int c = 0;
   __half *w11, *w12, *wc0, *wc2, *wqkv, *wproj, *w0, *w2;
   float *b11, *b12, *bqkv, *bproj, *b0, *b2, *ln1g, *ln1b, *ln2g, *ln2b, *rp;
+  // LayerNorm-folded copies for the fused transformer kernels (null where t > 64)
+  __half *wqkv_f = nullptr, *w0_f = nullptr;
+  float *bqkv_f = nullptr, *b0_f = nullptr;
 };
 
 const char* kStageName[7] = {"down1", "down2", "down3", "body", "up3", "up2", "up1"};
@@ -783,18 +786,18 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
 cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, const Op& op, cudaStream_t st);
 
 cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
-  using L = Trans32Layout;
+  using L = T32;
   static bool attr_set[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(trans32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(trans32_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const long pairs = (op.trans.win.n_windows + 1) / 2;
-  const int grid = (int)std::max(1L, std::min(pairs, (long)sms * L::CTAS));
-  trans32_kernel<<<grid, 256, L::SMEM, st>>>(op.trans);
+  const int grid = (int)std::max(1L, std::min(pairs, (long)sms));  // one CTA per SM, persistent over pairs
+  trans32_ws_kernel<<<grid, L::THREADS, L::SMEM, st>>>(op.trans);
   return cudaGetLastError();
 }
 
@@ -1212,6 +1215,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     tg.wqkv = bw.wqkv; tg.wproj = bw.wproj; tg.w0 = bw.w0; tg.w2 = bw.w2;
     tg.bqkv = bw.bqkv; tg.bproj = bw.bproj; tg.b0 = bw.b0; tg.b2 = bw.b2;
     tg.ln1g = bw.ln1g; tg.ln1b = bw.ln1b; tg.ln2g = bw.ln2g; tg.ln2b = bw.ln2b; tg.rp = bw.rp;
+    tg.wqkv_f = bw.wqkv_f; tg.w0_f = bw.w0_f; tg.bqkv_f = bw.bqkv_f; tg.b0_f = bw.b0_f;
     ops.push_back(tr);
   } else {
     // 4. qkv = LN1(y_t) W^T + b; a band needs it on its halo rows too (SW windows)
@@ -1611,6 +1615,7 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
   Blob blob;
   struct Pending {
     size_t w11, w12, wc0, wc2, wqkv, wproj, w0, w2, b11, b12, bqkv, bproj, b0, b2, l1g, l1b, l2g, l2b, rp;
+    size_t wqkv_f, w0_f, bqkv_f, b0_f;
     int c;
   };
   std::vector<Pending> pend[7];
@@ -1685,6 +1690,36 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
                 half_of(tb + ".mlp.0.weight", {4 * t, t}, pd.w0) && f32_of(tb + ".mlp.0.bias", {4 * t}, pd.b0) &&
                 half_of(tb + ".mlp.2.weight", {t, 4 * t}, pd.w2) && f32_of(tb + ".mlp.2.bias", {t}, pd.b2);
       if (!ok) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
+      if (t <= 64) {
+        // LN1 -> qkv and LN2 -> mlp0 with the LayerNorm affine folded into the
+        // linear: W (gamma x_hat + beta) + b = (W diag gamma) x_hat + (b + W beta),
+        // computed from the fp32 tensors; the q rows also take the attention scale
+        // 32^-1/2 (tools/network_scunet.py:73) and log2(e) (softmax in base 2)
+        const float qs = 0.17677669529663687f * 1.4426950408889634f;
+        auto fold = [&](const std::string& wn, const std::string& bn, const std::string& gn, const std::string& be,
+                        int rows, int qrows, size_t& ow, size_t& ob) {
+          const float* W = tab.get(wn, {rows, t});
+          const float* B = tab.get(bn, {rows});
+          const float* G = tab.get(gn, {t});
+          const float* Be = tab.get(be, {t});
+          std::vector<float> w((size_t)rows * t), b(rows);
+          for (int o = 0; o < rows; ++o) {
+            const float sc = o < qrows ? qs : 1.f;
+            double acc = B[o];
+            for (int i = 0; i < t; ++i) {
+              w[(size_t)o * t + i] = W[(size_t)o * t + i] * G[i] * sc;
+              acc += (double)W[(size_t)o * t + i] * Be[i];
+            }
+            b[o] = (float)(acc * sc);
+          }
+          ow = blob.half(w);
+          ob = blob.f32(b.data(), b.size());
+        };
+        fold(tb + ".msa.embedding_layer.weight", tb + ".msa.embedding_layer.bias", tb + ".ln1.weight",
+             tb + ".ln1.bias", 3 * t, t, pd.wqkv_f, pd.bqkv_f);
+        fold(tb + ".mlp.0.weight", tb + ".mlp.0.bias", tb + ".ln2.weight", tb + ".ln2.bias", 4 * t, 0, pd.w0_f,
+             pd.b0_f);
+      }
       pend[s].push_back(pd);
     }
     if (s < 3) {  // m_down{k}.{cfg}: [2c][c][2][2] -> [co][dy][dx][ci]
@@ -1753,6 +1788,9 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
       bw.b11 = F(pd.b11); bw.b12 = F(pd.b12); bw.bqkv = F(pd.bqkv); bw.bproj = F(pd.bproj);
       bw.b0 = F(pd.b0); bw.b2 = F(pd.b2); bw.ln1g = F(pd.l1g); bw.ln1b = F(pd.l1b);
       bw.ln2g = F(pd.l2g); bw.ln2b = F(pd.l2b); bw.rp = F(pd.rp);
+      if (pd.c / 2 <= 64) {
+        bw.wqkv_f = H16(pd.wqkv_f); bw.w0_f = H16(pd.w0_f); bw.bqkv_f = F(pd.bqkv_f); bw.b0_f = F(pd.b0_f);
+      }
       ctx->blocks[s].push_back(bw);
     }
   g_create_error.clear();

@@ -1,4 +1,4 @@
-// Shared pieces of the fused transformer-half kernels (trans32.cuh for trans width
+// Shared pieces of the fused transformer-half kernels (trans32ws.cuh for trans width
 // T = 32 at full resolution, trans64.cuh for T = 64 at half resolution). Each runs
 // the whole transformer half of a ConvTransBlock on pairs of 8x8 windows (128
 // tokens, one UMMA M tile):
@@ -27,6 +27,11 @@ struct TransGeom {
   const __half* w0;   // [4T][T]
   const __half* w2;   // [T][4T]
   const float *bqkv, *bproj, *b0, *b2, *ln1g, *ln1b, *ln2g, *ln2b, *rp;
+  // LayerNorm affine maps folded into the following linear (W diag(gamma),
+  // b + W beta; the q rows of wqkv_f/bqkv_f also carry 32^-1/2 log2(e)): used by
+  // the warp-specialised T = 32 kernel, which stores (x - mu) rstd only
+  const __half *wqkv_f, *w0_f;
+  const float *bqkv_f, *b0_f;
 };
 
 // Copy a row-major fp16 [R][K] matrix into K-major swizzled tiles: K split into

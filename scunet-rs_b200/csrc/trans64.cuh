@@ -12,7 +12,7 @@
 // share the resident weights: while one pipeline waits on the tensor core the other
 // runs its CUDA-core work.
 //
-// Per pipeline, as in trans32_kernel (trans32.cuh): accumulators are read out before
+// Per pipeline: accumulators are read out before
 // the MMA that overwrites them is issued (qkv [0, 192) -> S [0, 128), O'_0 [128, 192),
 // O'_1 [192, 256) -> proj/acc [0, 64), hidden [64, 128)); one 32 KB region holds in
 // turn LN1, Q|K of both heads, P'_0 | P'_1, O | P'_1, LN2 | hidden chunk; P'_h . [V_0 |
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(512, 1) trans64_kernel(const TransGeom g) {
   const int qi = tok >> 3, qj = tok & 7;
   const long n_pairs = (g.win.n_windows + 1) / 2;
   constexpr float kScaleLog2e = 0.17677669529663687f * 1.4426950408889634f;  // 32^-1/2 log2(e)
-  uint32_t mrow = 0, mcol = 0;  // shifted-window mask over this thread's 32 keys (see trans32.cuh)
+  uint32_t mrow = 0, mcol = 0;  // shifted-window mask over this thread's 32 keys
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const int kt = hf * 32 + j;
