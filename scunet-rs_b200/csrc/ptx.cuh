@@ -71,6 +71,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or about `ns` nanoseconds pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete; false (and the error word set to
 // `code`) after ~1 s.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
@@ -197,6 +211,19 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// The same with A read from tensor memory: `a_tmem` addresses a [128 lanes x K]
+// operand whose 32-bit columns each hold two fp16 K elements (lower K in the low
+// half); one K step of 16 spans 8 columns. Only B is read from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every UMMA this thread issued so far has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -232,6 +259,25 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Raw 32-bit stores of 8 / 16 / 32 consecutive columns of this thread's row.
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* r) {
+  tmem_st16u(taddr, r);
+  tmem_st16u(taddr + 16, r + 16);
+}
 
 __device__ __forceinline__ void tmem_fence16(uint32_t* r) {
 #pragma unroll
@@ -308,6 +354,19 @@ __device__ __forceinline__ uint64_t make_sdesc_sbo(uint32_t saddr, uint32_t sbo,
   return d;
 }
 
+// The general form: leading-dimension and stride byte offsets given explicitly. For
+// an MN-major SW128 operand, LBO is the stride between 64-element MN atoms and SBO
+// the stride between groups of 8 K rows (128-byte rows, swizzled within 1 KB).
+__device__ __forceinline__ uint64_t make_sdesc_lbo_sbo(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t swz) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)swz << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major.
 __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
   return (1u << 4)                       // D format: f32
@@ -316,6 +375,9 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
+
+// The same with B read MN-major (N contiguous in shared memory).
+__host__ __device__ constexpr uint32_t make_idesc_f16_bmn(int M, int N) { return make_idesc_f16(M, N) | (1u << 16); }
 
 // Byte offset of 16-byte chunk `chunk` of row `row` inside a K-major tile whose
 // rows are `row_bytes` (= swizzle span: 128, 64 or 32) long, with the tile base
@@ -355,6 +417,16 @@ __device__ __forceinline__ __half2 tanh_approx_h2(__half2 x) {
 // where the result is stored as fp16 (the MLP hidden layer); six packed operations
 // and one tanh.approx.f16x2 per two values. Large |x| saturates: x^2 -> inf gives
 // tanh -> +-1 and GELU -> x or 0.
+// 2 GELU(x) = x (1 + tanh(x (a + b x^2))), the form above without its factor 1/2
+// (callers fold the 1/2 into the next linear map, exactly, in fp16): five packed
+// operations and one tanh.approx.f16x2 per two values.
+__device__ __forceinline__ __half2 gelu2_tanh_h2(__half2 x) {
+  const __half2 x2 = __hmul2(x, x);
+  const __half2 p = __hfma2(__float2half2_rn(0.03470089f), x2, __float2half2_rn(0.80015708f));
+  const __half2 t = tanh_approx_h2(__hmul2(x, p));
+  return __hfma2(x, t, x);
+}
+
 __device__ __forceinline__ __half2 gelu_tanh_h2(__half2 x) {
   const __half2 x2 = __hmul2(x, x);
   const __half2 p = __hfma2(__float2half2_rn(0.03470089f), x2, __float2half2_rn(0.80015708f));
@@ -365,6 +437,13 @@ __device__ __forceinline__ __half2 gelu_tanh_h2(__half2 x) {
 
 // 2^x, hardware approximation (relative error ~2^-22, far below the fp16 rounding
 // every consumer of these values applies).
+// 2^x on two fp16 values (one MUFU operation for both).
+__device__ __forceinline__ uint32_t ex2_approx_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -421,6 +500,56 @@ __device__ __forceinline__ long win_token_pixel(const WinGeom& g, long win, int 
   store = y >= g.store_lo && y < g.store_hi;
   return ((long)img * g.H + y) * g.W + x;
 }
+
+// A thread's window within a persistent loop whose window index grows by a fixed
+// step: the image / window-row / window-column split is carried from one pair to
+// the next instead of being divided out again (win_token_pixel's arithmetic).
+struct WinCursor {
+  long win;
+  int img, wr, wc;
+  __device__ __forceinline__ void init(const WinGeom& g, long w) {
+    win = w;
+    const unsigned per_img = (unsigned)(g.nwr * g.nwc);
+    const unsigned uw = (unsigned)w;
+    img = (int)(uw / per_img);
+    const unsigned rem = uw - (unsigned)img * per_img;
+    wr = (int)(rem / (unsigned)g.nwc);
+    wc = (int)rem - wr * g.nwc;
+  }
+  // step < nwc * nwr is not required: each loop runs step / nwc + 1 times at most
+  __device__ __forceinline__ void advance(const WinGeom& g, int step) {
+    win += step;
+    wc += step;
+    while (wc >= g.nwc) {
+      wc -= g.nwc;
+      if (++wr == g.nwr) {
+        wr = 0;
+        ++img;
+      }
+    }
+  }
+  // the token's pixel, or -1 past the last window; flags as win_token_pixel
+  __device__ __forceinline__ long pixel(const WinGeom& g, int qi, int qj, bool& last_row, bool& last_col,
+                                        bool& store) const {
+    last_row = last_col = store = false;
+    if (win >= g.n_windows) return -1;
+    int y;
+    if (g.wrap) {
+      y = wr * 8 + qi + g.shift;
+      if (y >= g.H) y -= g.H;
+    } else {
+      y = g.row_base + wr * 8 + qi;
+    }
+    int x = wc * 8 + qj + g.shift;
+    if (x >= g.W) x -= g.W;
+    int gwr = g.gwr0 + wr;
+    if (gwr >= g.nwr_global) gwr -= g.nwr_global;
+    last_row = g.shift && gwr == g.nwr_global - 1;
+    last_col = g.shift && wc == g.nwc - 1;
+    store = y >= g.store_lo && y < g.store_hi;
+    return ((long)img * g.H + y) * g.W + x;
+  }
+};
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);

@@ -1,43 +1,49 @@
 // The transformer half of a full-resolution ConvTransBlock (trans width T = 32, one
 // head), warp-specialised: one CTA per SM streams pairs of 8x8 windows (128 tokens,
-// one UMMA M tile) through three warp groups that work on different pairs at the
-// same time, each issuing the UMMAs its own output feeds:
+// one UMMA M tile) through four warp groups that work on different pairs at the
+// same time, each issuing the UMMAs its own output feeds ([..] = a UMMA):
 //
-//   G1 (warps 0-3, one thread per token row): y_t rows by cp.async (two pairs
-//      ahead) -> LN1 -> A1 -> [qkv = A1.Wqkv'^T + b] -> Q, K rows and V^T columns
-//      -> [S = Q.K^T + E.F^T]
-//   G2 (warps 4-7, one thread per row): softmax of its window's 64 scores -> P'
-//      -> [O' = P'.[V0|V1], rowsum = P'.1] -> O = O'/rowsum
-//      -> [x1 = O.Wproj^T + y_t.I + b_proj]
-//   G3 (warps 8-15, two threads per row, one per column half): LN2(x1) -> A2
-//      -> [hid = A2.W0'^T + b0'] -> GELU -> H -> [acc = x1 + H.W2^T + b2] -> z
+//   G1 (4 warps, one thread per token row): y_t rows by cp.async (a pair ahead)
+//      -> LN1 -> A1 -> [qkv = A1.Wqkv'^T + b] -> Q (TMEM), K rows and V rows
+//      (shared memory) -> [S = Q.K^T]
+//   G2 (8 warps, two threads per row, 32 keys each): + rel-pos bias, mask, max
+//      (exchanged through shared memory), P' = 2^(s - max) -> [O' | rowsum =
+//      P'.[V0 | V1 | 1]] -> O = O' / rowsum -> [x1 = O.Wproj^T + y_t.I + b_proj]
+//   G3 (4 warps, one thread per row): LN2(x1) -> A2 -> [hid = A2.W0'^T + b0'] for
+//      the next pair while G4 works on this one; z = acc + b2 -> Z
+//   G4 (8 warps, two threads per row, 64 hidden columns each): 2 GELU(hid) -> H
+//      -> [acc = x1 + H.(W2/2)^T]
 //
 //   x  = y_t;  x1 = x + proj(WMSA(LN1(x)));  z = x1 + mlp2(GELU(mlp0(LN2(x1))))
 //   (tools/network_scunet.py:128-136; WMSA as tools/network_scunet.py:69-102)
 //
-// Everything that is linear in a UMMA operand runs on the tensor cores:
-//  * biases: every A operand gets one extra K step from a resident "ones" tile
-//    (K elements 0 and 1 = 1) whose B partner holds the bias split into an fp16
-//    high part and an fp16 remainder, so the bias reaches fp32 accumulation intact;
+// Operands the threads produce (A1, Q, P', O, A2, H) are written to tensor memory
+// with tcgen05.st as packed fp16 and read by the UMMAs as their A operand, so a
+// UMMA reads only its B operand from shared memory. Measured on B200: an M = 128,
+// K = 16 UMMA with A in shared memory costs ~32 + N/4 cycles of shared-memory
+// bandwidth (2.5x its tensor time at N = 32); one issuing thread sustains one UMMA
+// per ~50 cycles, so the groups issue their own UMMAs.
+//
+// Work moved onto the tensor cores:
+//  * biases (qkv, proj, mlp0): one extra K step from a resident "ones" tile (K
+//    elements 0 and 1 = 1) whose B partner holds the bias split into an fp16 high
+//    part and an fp16 remainder, so the bias reaches fp32 accumulation intact;
 //  * the LayerNorm affine maps are folded into the next weights on the host
-//    (W' = W diag(gamma), b' = b + W beta): the kernels store (x - mu) rstd only;
+//    (W' = W diag(gamma), b' = b + W beta): the kernel stores (x - mu) rstd only;
 //  * the attention scale 32^-1/2 and log2(e) are folded into the q rows of Wqkv';
-//  * the relative-position bias is E.F^T: E is the one-hot [128 x 64] of each query
-//    token's position in its window, F[key][m] = B(m, key) log2(e) (fp16), so S
-//    arrives in TMEM with the bias added and in base 2;
-//  * the softmax denominator is the row sum of the fp16 P' that the P.V product
-//    uses, from one N = 16 UMMA against a row of ones;
-//  * x1 = y_t + ...: the proj UMMA adds y_t through an identity B operand.
-// The CUDA cores keep only LN statistics, the softmax max/exp2, GELU and the fp16
-// packing. The shifted-window mask (cuda/scunet.cu:137-147) is applied in
-// registers on the image's last window row/column only.
+//  * the softmax denominator is the row sum of the fp16 P' that P.V uses: the
+//    MN-major V operand carries a ones column (N = 80);
+//  * x1 = y_t + ...: the proj UMMA adds y_t through an identity B operand;
+//  * the GELU's factor 1/2 is folded into W2 (exact in fp16).
+// The shifted-window mask (cuda/scunet.cu:137-147) is applied in registers on the
+// image's last window row/column only.
 //
 // Hand-offs between groups are mbarriers (UMMA commits, or thread arrivals for
 // "TMEM read, columns free"); inside a group, one leader thread waits on the
-// mbarrier and a named barrier releases the others. Every wait is bounded: a wait
-// that times out records an error code and raises a CTA-wide abort flag, every
-// other wait gives up as soon as it sees the flag, and each issuing thread drains
-// its UMMAs before the CTA frees its TMEM and exits.
+// mbarrier (sleeping in hardware) and a named barrier releases the others. Every
+// wait is bounded: a wait that times out records an error code and raises a
+// CTA-wide abort flag, every other wait gives up as soon as it sees the flag, and
+// each issuing thread drains its UMMAs before the CTA frees its TMEM and exits.
 #pragma once
 #include "trans.cuh"
 
@@ -45,8 +51,8 @@ namespace scb {
 
 struct T32 {
   static constexpr int T = 32;
-  // resident tiles (offsets from the 1024-aligned base); SW64 tiles have 64-byte
-  // rows, SW128 tiles 128-byte rows
+  // resident shared-memory tiles (offsets from the 1024-aligned base); SW64 tiles
+  // have 64-byte rows, SW128 tiles 128-byte rows
   static constexpr int W_QKV = 0;                  // [96 x 64 B]  Wqkv' (LN1 gamma, q scale folded)
   static constexpr int B_QKV = W_QKV + 96 * 64;    // [96 x 64 B]  bias hi/lo in K elements 0, 1
   static constexpr int W_PROJ = B_QKV + 96 * 64;   // [32 x 64 B]
@@ -54,27 +60,37 @@ struct T32 {
   static constexpr int IDENT = B_PROJ + 32 * 64;   // [32 x 64 B]  identity (x1 += y_t)
   static constexpr int W_0 = IDENT + 32 * 64;      // [128 x 64 B] W0' (LN2 gamma folded)
   static constexpr int B_0 = W_0 + 128 * 64;       // [128 x 64 B]
-  static constexpr int W_2 = B_0 + 128 * 64;       // 2 K blocks of [32 x 128 B], SW128
-  static constexpr int B_2 = W_2 + 2 * 32 * 128;   // [32 x 64 B]
-  static constexpr int ONES = B_2 + 32 * 64;       // [128 x 64 B] K elements 0, 1 = 1
-  static constexpr int E1H = ONES + 128 * 64;      // [128 x 128 B] one-hot query position, SW128
-  static constexpr int FB = E1H + 128 * 128;       // [128 x 128 B] rel-pos bias, key x query position
-  static constexpr int ONES_B = FB + 128 * 128;    // [16 x 128 B] row 0 = 1 (softmax row sums)
-  // pipeline buffers
-  static constexpr int Y = ONES_B + 16 * 128;      // 3 x [128 x 64 B] y_t rows (A of the identity step)
-  static constexpr int A1 = Y + 3 * 8192;          // [128 x 64 B] LN1 output
-  static constexpr int Q = A1 + 8192;              // [128 x 64 B]
-  static constexpr int K = Q + 8192;               // [128 x 64 B]
-  static constexpr int VT = K + 8192;              // [64 x 128 B] rows (window, d), K = key, SW128
-  static constexpr int P = VT + 8192;              // [128 x 128 B] P' (own window's 64 keys), SW128
-  static constexpr int O = P + 16384;              // [128 x 64 B]
-  static constexpr int A2 = O + 8192;              // [128 x 64 B] LN2 output
-  static constexpr int H = A2 + 8192;              // 2 K blocks of [128 x 128 B] GELU(hidden), SW128
-  static constexpr int BAR = H + 32768;
+  static constexpr int W_2 = B_0 + 128 * 64;       // 2 K blocks of [32 x 128 B], SW128: W2 / 2
+  static constexpr int ONES = W_2 + 2 * 32 * 128;  // [128 x 64 B] K elements 0, 1 = 1
+  // relative-position bias in log2 units, fp32 [64 query positions][64 keys]; the
+  // 16-byte chunks of row q are XOR-swizzled by q % 8 within each 128-byte half
+  static constexpr int RPB = ONES + 128 * 64;
+  // pipeline buffers (B operands and the y_t rows)
+  static constexpr int Y = RPB + 64 * 64 * 4;      // 3 x [128 x 64 B] y_t rows (A of the identity step)
+  static constexpr int K = Y + 3 * 8192;           // 2 x [128 x 64 B] keys
+  // V as the MN-major B operand of P.V (N = (window, d) contiguous per key): per
+  // buffer an atom [64 keys x 128 B] holding [V_0 | V_1] and an atom whose first N
+  // element is 1 (N = 64: the softmax row sums)
+  static constexpr int V = K + 2 * 8192;
+  static constexpr int V_BYTES = 2 * 8192;
+  static constexpr int B2F = V + 2 * V_BYTES;      // mlp2 bias, 32 floats
+  static constexpr int RED = B2F + 128;            // [2 halves x 128 rows] softmax partial maxima
+  static constexpr int BAR = RED + 1024;
   static constexpr int SMEM = BAR + 256 + 1024;    // + alignment slack
-  // TMEM columns
-  static constexpr uint32_t C_QKV = 0, C_S = 128, C_OP = 128, C_SUM = 192, C_ACC = 256, C_HID = 384;
-  static constexpr int THREADS = 512;
+  // TMEM columns. UMMA A operands written by the threads (tcgen05.st) are packed
+  // fp16 pairs, 8 columns per K step of 16. Pair i uses score buffer SB(i & 1):
+  // its qkv accumulator [0, 96), then S [0, 128), then P' [0, 32) (A of P.V) with
+  // O' [32, 96) and the row sums at 96 (N = 80).
+  static constexpr uint32_t C_SB = 0;     // 2 x 128
+  static constexpr uint32_t C_A1 = 256;   // LN1 output, A of qkv (16)
+  static constexpr uint32_t C_Q = 272;    // Q, A of S (16)
+  static constexpr uint32_t C_A2 = 288;   // LN2 output, A of mlp0 (16)
+  static constexpr uint32_t C_O = 304;    // O / rowsum, A of proj (16)
+  static constexpr uint32_t C_ACC = 320;  // 2 x 32: x1, then x1 + mlp2 (z)
+  static constexpr uint32_t C_HID = 384;  // hidden accumulator (128); GELU(hidden) (A of
+                                          // mlp2) overwrites the first 32 of each half
+  static constexpr int G1_WARPS = 4, G2_WARPS = 8, G3_WARPS = 4, G4_WARPS = 8;
+  static constexpr int THREADS = 32 * (G1_WARPS + G2_WARPS + G3_WARPS + G4_WARPS);
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) {
@@ -99,16 +115,15 @@ __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t pari
                                                     unsigned code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    __nanosleep(32);  // a spinning leader would take issue slots from its SMSP's other warps
-    if ((i & 63u) == 63u) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > 1000000000ull) {
-        record_error(code);
-        *abort_flag = 1u;
-        return false;
-      }
+  for (;;) {
+    // sleeps in hardware (no issue slots taken from the SMSP's other warps) until
+    // the phase completes or ~20 us pass
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > 1000000000ull) {
+      record_error(code);
+      *abort_flag = 1u;
+      return false;
     }
   }
 }
@@ -159,14 +174,16 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   uint64_t* bar_o = bars + 2;
   uint64_t* bar_hid = bars + 3;
   uint64_t* bar_out = bars + 4;
-  uint64_t* x1_done = bars + 5;   // [2], per x1 accumulator buffer
-  uint64_t* so_free = bars + 7;   // G2 has read O' and the row sums (128 arrivals)
-  uint64_t* acc_free = bars + 8;  // [2] G3 has read z (256 arrivals)
-  uint64_t* drain = bars + 10;    // [3] one per issuing group
-  uint32_t* misc = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* x1_done = bars + 5;   // [2] per x1 accumulator buffer: proj committed
+  uint64_t* acc_free = bars + 7;  // [2] G3 has read z (128 arrivals)
+  uint64_t* so_free = bars + 9;   // [2] per score buffer: G2 has read O' and the row sums (256 arrivals)
+  uint64_t* drain = bars + 11;    // [4] one per issuing group
+  constexpr int NBAR = 15;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(bars + NBAR);
   uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
-  volatile uint32_t* status = misc + 2;  // [3][2]
+  volatile uint32_t* status = misc + 2;  // [4][2]
+  float* red = reinterpret_cast<float*>(sm + L::RED);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = (warp & 3) * 32 + lane;  // TMEM lane = token row of the pair
@@ -176,10 +193,19 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   stage_kmajor(sm + L::W_QKV, g.wqkv_f, 3 * T, T, T);
   stage_kmajor(sm + L::W_PROJ, g.wproj, T, T, T);
   stage_kmajor(sm + L::W_0, g.w0_f, 4 * T, T, T);
-  stage_kmajor(sm + L::W_2, g.w2, T, 4 * T, 64);
+  // W2 / 2 (exact in fp16): the GELU below returns 2 GELU(x)
+  for (int idx = tid; idx < T * (4 * T / 8); idx += blockDim.x) {
+    const int r = idx >> 4, j = idx & 15, blk = j >> 3;
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(g.w2 + (long)r * 4 * T + j * 8));
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __hmul2(h[e], __float2half2_rn(0.5f));
+    *reinterpret_cast<uint4*>(sm + L::W_2 + blk * T * 128 + swz_off(r, j & 7, 128)) = u;
+  }
+  if (tid < T) reinterpret_cast<float*>(sm + L::B2F)[tid] = g.b2[tid];
   {
-    // SW64 side tiles: bias hi/lo (qkv 96, proj 32, mlp0 128, mlp2 32 rows), ones, identity
-    constexpr int R_BQ = 0, R_BP = 96, R_B0 = 128, R_B2 = 256, R_ONE = 288, R_ID = 416, R_END = 448;
+    // SW64 side tiles: bias hi/lo (qkv 96, proj 32, mlp0 128 rows), ones, identity
+    constexpr int R_BQ = 0, R_BP = 96, R_B0 = 128, R_ONE = 256, R_ID = 384, R_END = 416;
     for (int i = tid; i < R_END * 4; i += blockDim.x) {
       const int r = i >> 2, c = i & 3;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -191,12 +217,9 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       } else if (r < R_B0) {
         base = sm + L::B_PROJ, rr = r - R_BP;
         if (c == 0) v.x = bias_hilo(g.bproj[rr]);
-      } else if (r < R_B2) {
+      } else if (r < R_ONE) {
         base = sm + L::B_0, rr = r - R_B0;
         if (c == 0) v.x = bias_hilo(g.b0_f[rr]);
-      } else if (r < R_ONE) {
-        base = sm + L::B_2, rr = r - R_B2;
-        if (c == 0) v.x = bias_hilo(g.b2[rr]);
       } else if (r < R_ID) {
         base = sm + L::ONES, rr = r - R_ONE;
         if (c == 0) v.x = 0x3C003C00u;
@@ -206,35 +229,22 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       }
       *reinterpret_cast<uint4*>(base + swz_off(rr, c, 64)) = v;
     }
-    // SW128 tiles: one-hot query position (128 rows), rel-pos bias (128 key rows), row sums
-    for (int i = tid; i < (128 + 128 + 16) * 8; i += blockDim.x) {
-      const int r = i >> 3, c = i & 7;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      uint8_t* base;
-      int rr;
-      if (r < 128) {
-        base = sm + L::E1H, rr = r;
-        const int m = rr & 63;
-        if (c == (m >> 3)) set_half(v, m & 7, 0x3C00);
-      } else if (r < 256) {
-        base = sm + L::FB, rr = r - 128;
-        const int kp = rr & 63, ki = kp >> 3, kj = kp & 7;
-        // query position m = (c, e): B(m, key) = rp[(mi - ki + 7) * 15 + (mj - kj + 7)]
-        const float* rp = g.rp + (c - ki + 7) * 15 + (7 - kj);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) set_half(v, e, half_bits(rp[e] * 1.4426950408889634f));
-      } else {
-        base = sm + L::ONES_B, rr = r - 256;
-        if (rr == 0) v = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
-      }
-      *reinterpret_cast<uint4*>(base + swz_off(rr, c, 128)) = v;
+    // the ones atoms of both V buffers (64 key rows each: N element 64 = 1)
+    for (int i = tid; i < 128 * 8; i += blockDim.x) {
+      const int q = i >> 3, c = i & 7;  // buffer q / 64, key row q % 64
+      *reinterpret_cast<uint4*>(sm + L::V + (q >> 6) * L::V_BYTES + 8192 + swz_off(q & 63, c, 128)) =
+          make_uint4(c == 0 ? 0x3C00u : 0u, 0u, 0u, 0u);
+    }
+    // rel-pos bias B(query m, key k) = rp[(mi - ki + 7) * 15 + (mj - kj + 7)] log2(e)
+    float* rpb = reinterpret_cast<float*>(sm + L::RPB);
+    for (int i = tid; i < 64 * 64; i += blockDim.x) {
+      const int m = i >> 6, k = i & 63, c = k >> 2;
+      const float v = g.rp[((m >> 3) - (k >> 3) + 7) * 15 + ((m & 7) - (k & 7) + 7)] * 1.4426950408889634f;
+      rpb[m * 64 + (((c & 8) | ((c ^ m) & 7)) << 2) + (k & 3)] = v;
     }
   }
   if (tid == 0) {
-    for (int i = 0; i < 13; ++i) {
-      const uint32_t cnt = (bars + i == so_free) ? 128u : ((bars + i == acc_free || bars + i == acc_free + 1) ? 256u : 1u);
-      mbar_init(bars + i, cnt);
-    }
+    for (int i = 0; i < NBAR; ++i) mbar_init(bars + i, (i == 7 || i == 8) ? 128u : ((i == 9 || i == 10) ? 256u : 1u));
     mbar_fence_init();
     *abort_flag = 0u;
   }
@@ -250,12 +260,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   const long n_pairs = (g.win.n_windows + 1) / 2;
   const long first = blockIdx.x;
   const int n_local = first < n_pairs ? (int)((n_pairs - 1 - first) / gridDim.x + 1) : 0;
-  auto locate = [&](int li, bool& lr, bool& lc, bool& st) -> long {
-    const long win = 2 * (first + (long)li * gridDim.x) + slot;
-    lr = lc = st = false;
-    if (win >= g.win.n_windows) return -1;
-    return win_token_pixel(g.win, win, qi, qj, lr, lc, st);
-  };
+  const int win_step = 2 * (int)gridDim.x;  // a thread's window advances by this per pair
   auto pack8 = [](const float* f) -> uint4 {
     return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
   };
@@ -269,17 +274,19 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
     }
   };
   constexpr uint32_t ID_QKV = make_idesc_f16(128, 3 * T), ID_S = make_idesc_f16(128, 128),
-                     ID_PV = make_idesc_f16(128, 64), ID_SUM = make_idesc_f16(128, 16),
-                     ID_T = make_idesc_f16(128, T), ID_HID = make_idesc_f16(128, 4 * T);
+                     ID_PV = make_idesc_f16_bmn(128, 80), ID_T = make_idesc_f16(128, T),
+                     ID_HID = make_idesc_f16(128, 4 * T);
   auto d64 = [&](int off) { return make_sdesc(sb + off, 64, SW_64B); };
   auto d128 = [&](int off) { return make_sdesc(sb + off, 128, SW_128B); };
 
-  if (warp < 4) {
-    // ======================= G1: y_t -> LN1 -> qkv -> Q, K, V^T -> S =======================
-    GroupSync gs{1, 128, tid == 0, status, abort_flag, 0u};
-    auto fetch = [&](int li) {
+  if (warp < L::G1_WARPS) {
+    // ====== G1: y_t -> LN1 -> [qkv] -> Q (TMEM), K, V^T (smem) -> [S] ======
+    GroupSync gs{1, 32 * L::G1_WARPS, tid == 0, status, abort_flag, 0u};
+    WinCursor cur;
+    cur.init(g.win, 2 * first + slot);
+    auto fetch = [&](int li) {  // the cursor stands at pair li
       bool lr, lc, st;
-      const long pix = locate(li, lr, lc, st);
+      const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
       uint8_t* dst = sm + L::Y + (li % 3) * 8192;
       const __half* src = pix >= 0 ? g.y + pix * T : g.y;
 #pragma unroll
@@ -288,9 +295,11 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
     if (n_local > 0) fetch(0);
     cp_async_commit();
     for (int li = 0; li < n_local; ++li) {
+      const uint32_t sbuf = L::C_SB + (li & 1) * 128;
       if (li + 1 < n_local) {
         // buffer (li + 1) % 3 last held pair li - 2's y_t, an operand of its proj UMMA
         if (li >= 2 && !gs.wait(x1_done + ((li - 2) & 1), ((li - 2) >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
+        cur.advance(g.win, win_step);
         fetch(li + 1);
       }
       cp_async_commit();
@@ -311,60 +320,65 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         const float mu = (s0 + s1) * (1.f / T);
         const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
         const float nmr = -mu * rstd;
+        uint32_t a[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = fmaf(x[j], rstd, nmr);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sm + L::A1 + swz_off(row, c, 64)) = pack8(x + 8 * c);
+        for (int j = 0; j < 16; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+        tmem_st16u(trow + L::C_A1, a);  // (pair li - 1's qkv UMMA has completed)
+        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      fence_proxy_async_smem();  // the y_t rows (cp.async) are read by proj's identity step
+      tc_fence_before();
       gs.sync();
       if (gs.leader) {
-        tc_fence_after();
-        umma_f16(tmem + L::C_QKV, d64(L::A1), d64(L::W_QKV), ID_QKV, 0);
-        umma_f16(tmem + L::C_QKV, d64(L::A1 + 32), d64(L::W_QKV + 32), ID_QKV, 1);
-        umma_f16(tmem + L::C_QKV, d64(L::ONES), d64(L::B_QKV), ID_QKV, 1);
-        umma_commit(bar_qkv);
+        // score buffer li & 1 held pair li - 2 until G2 read its O' (after its P.V)
+        const bool ok = li < 2 || mbar_wait_abortable(so_free + (li & 1), ((li - 2) >> 1) & 1, abort_flag,
+                                                        SCB_ERR_WAIT_ATTN);
+        if (ok) {
+          tc_fence_after();
+          umma_f16_ts(tmem + sbuf, tmem + L::C_A1, d64(L::W_QKV), ID_QKV, 0);
+          umma_f16_ts(tmem + sbuf, tmem + L::C_A1 + 8, d64(L::W_QKV + 32), ID_QKV, 1);
+          umma_f16(tmem + sbuf, d64(L::ONES), d64(L::B_QKV), ID_QKV, 1);
+          umma_commit(bar_qkv);
+        }
       }
       if (!gs.wait(bar_qkv, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      // Q, K, V^T of pair li - 1 are free once its P.V product has completed
-      if (li >= 1 && !gs.wait(bar_o, (li - 1) & 1, SCB_ERR_WAIT_ATTN)) break;
+      // Q of pair li - 1 is an operand of its S UMMA (K and V^T buffers li & 1 were
+      // freed with score buffer li & 1)
+      if (li >= 1 && !gs.wait(bar_s, (li - 1) & 1, SCB_ERR_WAIT_ATTN)) break;
       tc_fence_after();
       {
         float q[32];
-        tmem_ld16x2(trow + L::C_QKV, q, trow + L::C_QKV + 16, q + 16);
+        tmem_ld16x2(trow + sbuf, q, trow + sbuf + 16, q + 16);
+        uint32_t pq[16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sm + L::Q + swz_off(row, c, 64)) = pack8(q + 8 * c);
+        for (int j = 0; j < 16; ++j) pq[j] = pack_half2(q[2 * j], q[2 * j + 1]);
+        tmem_st16u(trow + L::C_Q, pq);
       }
       {
         float k[32];
-        tmem_ld16x2(trow + L::C_QKV + 32, k, trow + L::C_QKV + 48, k + 16);
+        tmem_ld16x2(trow + sbuf + 32, k, trow + sbuf + 48, k + 16);
+        uint8_t* kb = sm + L::K + (li & 1) * 8192;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sm + L::K + swz_off(row, c, 64)) = pack8(k + 8 * c);
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(kb + swz_off(row, c, 64)) = pack8(k + 8 * c);
       }
       {
         float v[32];
-        tmem_ld16x2(trow + L::C_QKV + 64, v, trow + L::C_QKV + 80, v + 16);
-        // V^T: row (window slot, d), key = this token
-        uint8_t* vb = sm + L::VT + slot * 32 * 128 + (tok & 7) * 2;
-        const int kc = tok >> 3;
+        tmem_ld16x2(trow + sbuf + 64, v, trow + sbuf + 80, v + 16);
+        // V, MN-major: key row tok, N elements 32 slot .. 32 slot + 31
+        uint8_t* vb = sm + L::V + (li & 1) * L::V_BYTES;
 #pragma unroll
-        for (int d = 0; d < 32; ++d)
-          *reinterpret_cast<__half*>(vb + d * 128 + (((kc ^ d) & 7) << 4)) = __float2half_rn(v[d]);
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(vb + swz_off(tok, 4 * slot + c, 128)) = pack8(v + 8 * c);
       }
+      tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
       gs.sync();
       if (gs.leader) {
-        // S reuses the columns of pair li - 1's O' and row sums: G2 must have read them
-        const bool ok = li == 0 || mbar_wait_abortable(so_free, (li - 1) & 1, abort_flag, SCB_ERR_WAIT_ATTN);
-        if (ok) {
-          tc_fence_after();
-          umma_f16(tmem + L::C_S, d64(L::Q), d64(L::K), ID_S, 0);
-          umma_f16(tmem + L::C_S, d64(L::Q + 32), d64(L::K + 32), ID_S, 1);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16(tmem + L::C_S, d128(L::E1H + 32 * k), d128(L::FB + 32 * k), ID_S, 1);
-          umma_commit(bar_s);
-        }
+        tc_fence_after();
+        const int kb = L::K + (li & 1) * 8192;
+        umma_f16_ts(tmem + sbuf, tmem + L::C_Q, d64(kb), ID_S, 0);
+        umma_f16_ts(tmem + sbuf, tmem + L::C_Q + 8, d64(kb + 32), ID_S, 1);
+        umma_commit(bar_s);
       }
     }
     cp_async_wait_all();
@@ -372,69 +386,92 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       umma_commit(drain + 0);
       mbar_wait(drain + 0, 0, SCB_ERR_WAIT_ATTN);
     }
-  } else if (warp < 8) {
-    // ======================= G2: softmax -> P' -> O'/rowsum -> O -> x1 =======================
-    GroupSync gs{2, 128, tid == 160, status + 2, abort_flag, 0u};  // leaders sit on different SMSPs
-    for (int li = 0; li < n_local; ++li) {
+  } else if (warp < L::G1_WARPS + L::G2_WARPS) {
+    // ====== G2 (two threads per row, 32 keys each): softmax -> P' -> [O', rowsum]
+    //        -> O -> [x1] ======
+    GroupSync gs{2, 32 * L::G2_WARPS, tid == 160, status + 2, abort_flag, 0u};  // leaders sit on different SMSPs
+    const int hf = (warp - L::G1_WARPS) >> 2;
+    WinCursor cur;
+    cur.init(g.win, 2 * first + slot);
+    for (int li = 0; li < n_local; ++li, cur.advance(g.win, win_step)) {
+      const uint32_t sbuf = L::C_SB + (li & 1) * 128;
       if (!gs.wait(bar_s, li & 1, SCB_ERR_WAIT_ATTN)) break;
       tc_fence_after();
       bool last_row, last_col, st;
-      (void)locate(li, last_row, last_col, st);
+      (void)cur.pixel(g.win, qi, qj, last_row, last_col, st);
       {
-        float s[64];
-        tmem_ld16x2(trow + L::C_S + slot * 64, s, trow + L::C_S + slot * 64 + 16, s + 16);
-        tmem_ld16x2(trow + L::C_S + slot * 64 + 32, s + 32, trow + L::C_S + slot * 64 + 48, s + 48);
+        float s[32];  // keys 32 hf .. 32 hf + 31 of the row's own window
+        tmem_ld16x2(trow + sbuf + slot * 64 + hf * 32, s, trow + sbuf + slot * 64 + hf * 32 + 16, s + 16);
+        {
+          const float* rb = reinterpret_cast<const float*>(sm + L::RPB) + tok * 64;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 bb = *reinterpret_cast<const float4*>(rb + ((hf * 8 + ((c ^ tok) & 7)) << 2));
+            s[4 * c] += bb.x;
+            s[4 * c + 1] += bb.y;
+            s[4 * c + 2] += bb.z;
+            s[4 * c + 3] += bb.w;
+          }
+        }
         if (last_row || last_col) {  // warp-uniform: a warp's 32 tokens share one window
           // the cyclic shift put tokens from opposite image edges into the last window
           // row / column; a token attends only to keys from its own side
-          // (cuda/scunet.cu:137-147)
-          const bool qtop = qi < 4, qleft = qj < 4;
+          // (cuda/scunet.cu:137-147). Key 32 hf + j sits in window row 4 hf + j / 8.
+          const bool rmask = last_row && ((qi < 4) != (hf == 0));
+          const bool qleft = qj < 4;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const bool m = (last_row && (qtop != ((j >> 3) < 4))) || (last_col && (qleft != ((j & 7) < 4)));
-            s[j] = m ? -INFINITY : s[j];
-          }
+          for (int j = 0; j < 32; ++j) s[j] = (rmask || (last_col && (qleft != ((j & 7) < 4)))) ? -INFINITY : s[j];
         }
         float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
 #pragma unroll
-        for (int j = 4; j < 64; j += 4) {
+        for (int j = 4; j < 32; j += 4) {
           m0 = fmaxf(m0, s[j]);
           m1 = fmaxf(m1, s[j + 1]);
           m2 = fmaxf(m2, s[j + 2]);
           m3 = fmaxf(m3, s[j + 3]);
         }
-        const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        red[hf * 128 + row] = mx;
+        tmem_wait_ld();
+        tc_fence_before();
+        gs.sync();  // both halves of the row have read S (P' overwrites it) and posted their maxima
+        tc_fence_after();
+        mx = fmaxf(mx, red[(hf ^ 1) * 128 + row]);
+        // P' = 2^(s - max) as packed fp16, the precision the P.V operand has anyway;
+        // the row sum comes from the same fp16 values (the ones row of V^T)
+        uint32_t p[16];
 #pragma unroll
-        for (int j = 0; j < 64; ++j) s[j] = ex2_approx(s[j] - mx);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sm + L::P + swz_off(row, c, 128)) = pack8(s + 8 * c);
+        for (int j = 0; j < 16; ++j) p[j] = ex2_approx_h2(pack_half2(s[2 * j] - mx, s[2 * j + 1] - mx));
+        tmem_st16u(trow + sbuf + hf * 16, p);
+        tmem_wait_st();
       }
       tc_fence_before();
-      fence_proxy_async_smem();
       gs.sync();
       if (gs.leader) {
         tc_fence_after();
+        const uint32_t vb = sb + L::V + (li & 1) * L::V_BYTES;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_f16(tmem + L::C_OP, d128(L::P + 32 * k), d128(L::VT + 32 * k), ID_PV, k);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) umma_f16(tmem + L::C_SUM, d128(L::P + 32 * k), d128(L::ONES_B + 32 * k), ID_SUM, k);
+        for (int k = 0; k < 4; ++k)  // K step k = keys 16k .. 16k + 15 = two 8-row groups
+          umma_f16_ts(tmem + sbuf + 32, tmem + sbuf + 8 * k, make_sdesc_lbo_sbo(vb + 2048 * k, 8192, 1024, SW_128B),
+                      ID_PV, k);
         umma_commit(bar_o);
       }
       if (!gs.wait(bar_o, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      tc_fence_after();
-      float o[32];
-      tmem_ld16x2(trow + L::C_OP + slot * 32, o, trow + L::C_OP + slot * 32 + 16, o + 16);  // own window's half
-      const float sum = tmem_ld1(trow + L::C_SUM);
-      tc_fence_before();
-      mbar_arrive(so_free);
-      const float inv = __fdividef(1.f, sum);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] *= inv;
       // O of pair li - 1 is an operand of its proj UMMA
       if (li >= 1 && !gs.wait(x1_done + ((li - 1) & 1), ((li - 1) >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
+      tc_fence_after();
+      {
+        float o[16];
+        tmem_ld16(trow + sbuf + 32 + slot * 32 + hf * 16, o);  // own window's half of O', this thread's 16 d
+        const float inv = __fdividef(1.f, tmem_ld1(trow + sbuf + 32 + 64));
+        uint32_t po[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sm + L::O + swz_off(row, c, 64)) = pack8(o + 8 * c);
-      fence_proxy_async_smem();
+        for (int j = 0; j < 8; ++j) po[j] = pack_half2(o[2 * j] * inv, o[2 * j + 1] * inv);
+        tmem_st8u(trow + L::C_O + hf * 8, po);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(so_free + (li & 1));
       gs.sync();
       if (gs.leader) {
         const int b = li & 1;
@@ -444,8 +481,8 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
           tc_fence_after();
           const uint32_t d = tmem + L::C_ACC + b * T;
           const int yb = L::Y + (li % 3) * 8192;
-          umma_f16(d, d64(L::O), d64(L::W_PROJ), ID_T, 0);
-          umma_f16(d, d64(L::O + 32), d64(L::W_PROJ + 32), ID_T, 1);
+          umma_f16_ts(d, tmem + L::C_O, d64(L::W_PROJ), ID_T, 0);
+          umma_f16_ts(d, tmem + L::C_O + 8, d64(L::W_PROJ + 32), ID_T, 1);
           umma_f16(d, d64(yb), d64(L::IDENT), ID_T, 1);
           umma_f16(d, d64(yb + 32), d64(L::IDENT + 32), ID_T, 1);
           umma_f16(d, d64(L::ONES), d64(L::B_PROJ), ID_T, 1);
@@ -457,47 +494,97 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       umma_commit(drain + 1);
       mbar_wait(drain + 1, 0, SCB_ERR_WAIT_ATTN);
     }
-  } else {
-    // ======================= G3: LN2 -> hidden -> GELU -> mlp2 -> z =======================
-    GroupSync gs{3, 256, tid == 320, status + 4, abort_flag, 0u};
-    const int hf = (warp - 8) >> 2;  // column half of the row this thread owns
-    for (int li = 0; li < n_local; ++li) {
+  } else if (warp < L::G1_WARPS + L::G2_WARPS + L::G3_WARPS) {
+    // ====== G3 (one thread per row): LN2(x1) -> A2 -> [hidden]; z out ======
+    // It runs a pair ahead of G4: LN2 of pair li + 1 while G4 applies GELU to pair
+    // li, and issues mlp0 of pair li + 1 as soon as mlp2 of pair li (the last reader
+    // of the hidden columns) has completed.
+    GroupSync gs{3, 32 * L::G3_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + 2), status + 4, abort_flag, 0u};
+    WinCursor cur;
+    cur.init(g.win, 2 * first + slot);
+    auto ln2 = [&](int li) -> bool {  // x1 of pair li -> A2 (TMEM)
       const int b = li & 1;
-      const uint32_t acc = L::C_ACC + b * T;
-      if (!gs.wait(x1_done + b, (li >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (!gs.wait(x1_done + b, (li >> 1) & 1, SCB_ERR_WAIT_ATTN)) return false;
       tc_fence_after();
-      {
-        float x[32];
-        tmem_ld16x2(trow + acc, x, trow + acc + 16, x + 16);
-        float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
+      float x[32];
+      tmem_ld16x2(trow + L::C_ACC + b * T, x, trow + L::C_ACC + b * T + 16, x + 16);
+      float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          s0 += x[j];
-          s1 += x[j + 1];
-          q0 = fmaf(x[j], x[j], q0);
-          q1 = fmaf(x[j + 1], x[j + 1], q1);
-        }
-        const float mu = (s0 + s1) * (1.f / T);
-        const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
-        const float nmr = -mu * rstd;
-        float a[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) a[j] = fmaf(hf ? x[16 + j] : x[j], rstd, nmr);  // no runtime index: x stays in registers
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-          *reinterpret_cast<uint4*>(sm + L::A2 + swz_off(row, 2 * hf + c, 64)) = pack8(a + 8 * c);
+      for (int j = 0; j < 32; j += 2) {
+        s0 += x[j];
+        s1 += x[j + 1];
+        q0 = fmaf(x[j], x[j], q0);
+        q1 = fmaf(x[j + 1], x[j + 1], q1);
       }
-      fence_proxy_async_smem();
+      const float mu = (s0 + s1) * (1.f / T);
+      const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
+      const float nmr = -mu * rstd;
+      uint32_t a[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+      tmem_st16u(trow + L::C_A2, a);
+      tmem_wait_st();
+      tc_fence_before();
+      return true;
+    };
+    auto issue_mlp0 = [&]() {
+      tc_fence_after();
+      umma_f16_ts(tmem + L::C_HID, tmem + L::C_A2, d64(L::W_0), ID_HID, 0);
+      umma_f16_ts(tmem + L::C_HID, tmem + L::C_A2 + 8, d64(L::W_0 + 32), ID_HID, 1);
+      umma_f16(tmem + L::C_HID, d64(L::ONES), d64(L::B_0), ID_HID, 1);
+      umma_commit(bar_hid);
+    };
+    bool ok = n_local > 0 && ln2(0);
+    if (ok) {
       gs.sync();
-      if (gs.leader) {
-        tc_fence_after();
-        umma_f16(tmem + L::C_HID, d64(L::A2), d64(L::W_0), ID_HID, 0);
-        umma_f16(tmem + L::C_HID, d64(L::A2 + 32), d64(L::W_0 + 32), ID_HID, 1);
-        umma_f16(tmem + L::C_HID, d64(L::ONES), d64(L::B_0), ID_HID, 1);
-        umma_commit(bar_hid);
+      if (gs.leader) issue_mlp0();
+    }
+    for (int li = 0; ok && li < n_local; ++li, cur.advance(g.win, win_step)) {
+      if (li + 1 < n_local) {
+        // A2 of pair li is read by its mlp0
+        if (!gs.wait(bar_hid, li & 1, SCB_ERR_WAIT_ATTN) || !ln2(li + 1)) break;
       }
+      // mlp2 of pair li has completed: z is final and the hidden columns are free
+      if (!gs.wait(bar_out, li & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (li + 1 < n_local && gs.leader) issue_mlp0();
+      tc_fence_after();
+      const int b = li & 1;
+      float z[32];
+      tmem_ld16x2(trow + L::C_ACC + b * T, z, trow + L::C_ACC + b * T + 16, z + 16);
+      tc_fence_before();
+      mbar_arrive(acc_free + b);
+      bool lr, lc, st;
+      const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
+      if (pix >= 0 && st) {
+        const float4* b24 = reinterpret_cast<const float4*>(sm + L::B2F);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 bb = b24[q];
+          z[4 * q] += bb.x;
+          z[4 * q + 1] += bb.y;
+          z[4 * q + 2] += bb.z;
+          z[4 * q + 3] += bb.w;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) dst[c] = pack8(z + 8 * c);
+      }
+    }
+    if (gs.leader) {
+      umma_commit(drain + 2);
+      mbar_wait(drain + 2, 0, SCB_ERR_WAIT_ATTN);
+    }
+  } else {
+    // ====== G4 (two threads per row, one per 64 hidden columns): GELU -> H -> [z] ======
+    GroupSync gs{4, 32 * L::G4_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + L::G3_WARPS + 3), status + 6,
+                 abort_flag, 0u};
+    const int hf = (warp - L::G1_WARPS - L::G2_WARPS - L::G3_WARPS) >> 2;
+    for (int li = 0; li < n_local; ++li) {
       if (!gs.wait(bar_hid, li & 1, SCB_ERR_WAIT_ATTN)) break;
       tc_fence_after();
+      // GELU of this thread's 64 hidden columns [64 hf, 64 hf + 64), 32 at a time; the
+      // packed result (A of mlp2) goes to the first 32 of those columns, each half
+      // after its own values have been read
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         float hv[32];
@@ -507,46 +594,27 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           __half2 a = __floats2half2_rn(hv[2 * j], hv[2 * j + 1]);
-          a = gelu_tanh_h2(a);
+          a = gelu2_tanh_h2(a);
           pk[j] = *reinterpret_cast<uint32_t*>(&a);
         }
-        uint8_t* hb = sm + L::H + hf * 16384;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(hb + swz_off(row, h2 * 4 + c, 128)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        tmem_st16u(trow + L::C_HID + hf * 64 + h2 * 16, pk);
       }
+      tmem_wait_st();
       tc_fence_before();
-      fence_proxy_async_smem();
       gs.sync();
       if (gs.leader) {
         tc_fence_after();
-        const uint32_t d = tmem + acc;
+        const uint32_t d = tmem + L::C_ACC + (li & 1) * T;
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(d, d128(L::H + kb * 16384 + 32 * k), d128(L::W_2 + kb * 4096 + 32 * k), ID_T, 1);
-        umma_f16(d, d64(L::ONES), d64(L::B_2), ID_T, 1);
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(d, tmem + L::C_HID + (k >> 2) * 64 + (k & 3) * 8,
+                      d128(L::W_2 + (k >> 2) * 4096 + 32 * (k & 3)), ID_T, 1);
         umma_commit(bar_out);
-      }
-      if (!gs.wait(bar_out, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      tc_fence_after();
-      float z[16];
-      tmem_ld16(trow + acc + hf * 16, z);
-      tc_fence_before();
-      mbar_arrive(acc_free + b);
-      bool lr, lc, st;
-      const long pix = locate(li, lr, lc, st);
-      if (pix >= 0 && st) {
-        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T + hf * 16);
-        dst[0] = pack8(z);
-        dst[1] = pack8(z + 8);
       }
     }
     if (gs.leader) {
-      umma_commit(drain + 2);
-      mbar_wait(drain + 2, 0, SCB_ERR_WAIT_ATTN);
+      umma_commit(drain + 3);
+      mbar_wait(drain + 3, 0, SCB_ERR_WAIT_ATTN);
     }
   }
   tc_fence_before();
