@@ -465,8 +465,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           float v[32];
           tmem_ld16x2(tbase + c, v, tbase + c + 16, v + 16);
           if (e.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(e.bias + n0 + c);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += __ldg(e.bias + n0 + c + j);
+            for (int j = 0; j < 8; ++j) {
+              const float4 bb = __ldg(b4 + j);
+              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+            }
           }
           if (e.res16 && p < g.M) {
             const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + n0 + c);
@@ -503,9 +507,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         float v[32];
         tmem_ld16x2(tbase + c, v, tbase + c + 16, v + 16);
         const int n = n0 + c;
-        if (e.bias) {
+        if (e.bias) {  // 32 columns of bias as eight 16-byte loads (n is a multiple of 32)
+          const float4* b4 = reinterpret_cast<const float4*>(e.bias + n);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += __ldg(e.bias + n + j);
+          for (int j = 0; j < 8; ++j) {
+            const float4 bb = __ldg(b4 + j);
+            v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+          }
         }
         if (e.act == ACT_RELU) {
 #pragma unroll
@@ -634,9 +642,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tmem_ld16(tbase + c, v);
         const int n = n0 + c;       // global GEMM column
         const int oc = col0 + c;    // output column
-        if (e.bias) {
+        if (e.bias) {  // n is a multiple of 16
+          const float4* b4 = reinterpret_cast<const float4*>(e.bias + n);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] += __ldg(e.bias + n + j);
+          for (int j = 0; j < 4; ++j) {
+            const float4 bb = __ldg(b4 + j);
+            v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+          }
         }
         if (e.act == ACT_RELU) {
 #pragma unroll
@@ -736,8 +748,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int n = n0 + c;
           const int oc = col0 + c;
           if (e.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(e.bias + n);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += __ldg(e.bias + n + j);
+            for (int j = 0; j < 4; ++j) {
+              const float4 bb = __ldg(b4 + j);
+              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+            }
           }
           if (p >= 0) {
             if (e.res16) {

@@ -1400,9 +1400,11 @@ int build_plan(scb_ctx* ctx, Arena& A) {
     }
     const int nb = ctx->config[s];
     for (int i = 0; i < nb; ++i) {
-      // the residual stream: fp16 in xs (default), or fp32 in xw with xs its copy
-      // (SCB_OPT_RESIDUAL32); a down stage starts from the fp32 skip plane either way
-      const float* xin = (!up && i == 0) ? A.skip[lvl] : ctx->residual32 ? A.xw : nullptr;
+      // the residual stream: fp16 in xs (default; a down stage's first block reads the
+      // skip plane's fp16 shadow, which the head / down conv wrote into xs), or fp32
+      // in xw with xs its copy (SCB_OPT_RESIDUAL32; a down stage then starts from the
+      // fp32 skip plane itself)
+      const float* xin = !ctx->residual32 ? nullptr : (!up && i == 0) ? A.skip[lvl] : A.xw;
       const bool last = i == nb - 1;
       const float* skip = nullptr;
       float* xout = ctx->residual32 ? A.xw : nullptr;
@@ -2095,6 +2097,8 @@ int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16,
   GemmOp g{};
   if (!mk.flat(g, static_cast<const __half*>(a16), M, K, K, static_cast<const __half*>(b16), N))
     return fail(ctx, SCB_EINVAL, err);
+  if (reinterpret_cast<uintptr_t>(bias) % 16)
+    return fail(ctx, SCB_EINVAL, "bias must be 16-byte aligned (the epilogue reads it as float4)");
   g.e.bias = bias;
   g.e.act = act;
   g.e.res16 = static_cast<const __half*>(res16);
