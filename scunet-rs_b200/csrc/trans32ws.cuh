@@ -10,9 +10,10 @@
 //      (exchanged through shared memory), P' = 2^(s - max) -> [O' | rowsum =
 //      P'.[V0 | V1 | 1]] -> O = O' / rowsum -> [x1 = O.Wproj^T + y_t.I + b_proj]
 //   G3 (4 warps, one thread per row): LN2(x1) -> A2 -> [hid = A2.W0'^T + b0'] for
-//      the next pair while G4 works on this one; z = acc + b2 -> Z
-//   G4 (8 warps, two threads per row, 64 hidden columns each): 2 GELU(hid) -> H
-//      -> [acc = x1 + H.(W2/2)^T]
+//      the next pair while G4 works on this one, in two 64-column chunks with their
+//      own TMEM buffers; z = acc + b2 -> Z
+//   G4 (8 warps, two threads per row, 32 columns of a chunk each): per chunk,
+//      2 GELU(hid) -> H -> [acc += H.(W2/2)^T]
 //
 //   x  = y_t;  x1 = x + proj(WMSA(LN1(x)));  z = x1 + mlp2(GELU(mlp0(LN2(x1))))
 //   (tools/network_scunet.py:128-136; WMSA as tools/network_scunet.py:69-102)
@@ -172,14 +173,15 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   uint64_t* bar_qkv = bars + 0;
   uint64_t* bar_s = bars + 1;
   uint64_t* bar_o = bars + 2;
-  uint64_t* bar_hid = bars + 3;
-  uint64_t* bar_out = bars + 4;
-  uint64_t* x1_done = bars + 5;   // [2] per x1 accumulator buffer: proj committed
-  uint64_t* acc_free = bars + 7;  // [2] G3 has read z (128 arrivals)
-  uint64_t* so_free = bars + 9;   // [2] per score buffer: G2 has read O' and the row sums (256 arrivals)
-  uint64_t* drain = bars + 11;    // [4] one per issuing group
-  constexpr int NBAR = 15;
+  uint64_t* x1_done = bars + 3;   // [2] per x1 accumulator buffer: proj committed
+  uint64_t* acc_free = bars + 5;  // [2] G3 has read z (128 arrivals)
+  uint64_t* so_free = bars + 7;   // [2] per score buffer: G2 has read O' and the row sums (256 arrivals)
+  uint64_t* bar_hid = bars + 9;   // [2] per hidden chunk: mlp0 committed
+  uint64_t* bar_out = bars + 11;  // [2] per hidden chunk: its mlp2 K steps committed
+  uint64_t* drain = bars + 13;    // [4] one per issuing group
+  constexpr int NBAR = 17;
   uint32_t* misc = reinterpret_cast<uint32_t*>(bars + NBAR);
+  static_assert(17 * 8 + 10 * 4 <= 256, "barrier region");
   uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
   volatile uint32_t* status = misc + 2;  // [4][2]
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
     }
   }
   if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(bars + i, (i == 7 || i == 8) ? 128u : ((i == 9 || i == 10) ? 256u : 1u));
+    for (int i = 0; i < NBAR; ++i) mbar_init(bars + i, (i == 5 || i == 6) ? 128u : ((i == 7 || i == 8) ? 256u : 1u));
     mbar_fence_init();
     *abort_flag = 0u;
   }
@@ -497,8 +499,10 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   } else if (warp < L::G1_WARPS + L::G2_WARPS + L::G3_WARPS) {
     // ====== G3 (one thread per row): LN2(x1) -> A2 -> [hidden]; z out ======
     // It runs a pair ahead of G4: LN2 of pair li + 1 while G4 applies GELU to pair
-    // li, and issues mlp0 of pair li + 1 as soon as mlp2 of pair li (the last reader
-    // of the hidden columns) has completed.
+    // li; the hidden layer is two 64-column chunks with their own buffers, and mlp0
+    // of chunk c of pair li + 1 is issued as soon as mlp2's K steps of chunk c of
+    // pair li (the last reader of that buffer) have completed, so the GELU warps
+    // find the next chunk computed while they work on the current one.
     GroupSync gs{3, 32 * L::G3_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + 2), status + 4, abort_flag, 0u};
     WinCursor cur;
     cur.init(g.win, 2 * first + slot);
@@ -527,26 +531,35 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       tc_fence_before();
       return true;
     };
-    auto issue_mlp0 = [&]() {
+    constexpr uint32_t ID_H64 = make_idesc_f16(128, 64);
+    auto issue_mlp0 = [&](int c) {  // hidden columns [64 c, 64 c + 64) -> buffer c
       tc_fence_after();
-      umma_f16_ts(tmem + L::C_HID, tmem + L::C_A2, d64(L::W_0), ID_HID, 0);
-      umma_f16_ts(tmem + L::C_HID, tmem + L::C_A2 + 8, d64(L::W_0 + 32), ID_HID, 1);
-      umma_f16(tmem + L::C_HID, d64(L::ONES), d64(L::B_0), ID_HID, 1);
-      umma_commit(bar_hid);
+      const uint32_t d = tmem + L::C_HID + c * 64;
+      umma_f16_ts(d, tmem + L::C_A2, d64(L::W_0 + c * 64 * 64), ID_H64, 0);
+      umma_f16_ts(d, tmem + L::C_A2 + 8, d64(L::W_0 + c * 64 * 64 + 32), ID_H64, 1);
+      umma_f16(d, d64(L::ONES), d64(L::B_0 + c * 64 * 64), ID_H64, 1);
+      umma_commit(bar_hid + c);
     };
     bool ok = n_local > 0 && ln2(0);
     if (ok) {
       gs.sync();
-      if (gs.leader) issue_mlp0();
+      if (gs.leader) {
+        issue_mlp0(0);
+        issue_mlp0(1);
+      }
     }
     for (int li = 0; ok && li < n_local; ++li, cur.advance(g.win, win_step)) {
-      if (li + 1 < n_local) {
-        // A2 of pair li is read by its mlp0
-        if (!gs.wait(bar_hid, li & 1, SCB_ERR_WAIT_ATTN) || !ln2(li + 1)) break;
+      const bool more = li + 1 < n_local;
+      if (more) {
+        // A2 of pair li is read by both of its mlp0 chunks (one issuer: chunk 1's
+        // commit covers chunk 0)
+        if (!gs.wait(bar_hid + 1, li & 1, SCB_ERR_WAIT_ATTN) || !ln2(li + 1)) break;
       }
-      // mlp2 of pair li has completed: z is final and the hidden columns are free
-      if (!gs.wait(bar_out, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      if (li + 1 < n_local && gs.leader) issue_mlp0();
+      if (!gs.wait(bar_out + 0, li & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (more && gs.leader) issue_mlp0(0);
+      // chunk 1's mlp2 has completed: z is final
+      if (!gs.wait(bar_out + 1, li & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (more && gs.leader) issue_mlp0(1);
       tc_fence_after();
       const int b = li & 1;
       float z[32];
@@ -575,21 +588,24 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       mbar_wait(drain + 2, 0, SCB_ERR_WAIT_ATTN);
     }
   } else {
-    // ====== G4 (two threads per row, one per 64 hidden columns): GELU -> H -> [z] ======
+    // ====== G4 (two threads per row): per hidden chunk, 2 GELU -> H -> [acc += H.(W2/2)^T] ======
     GroupSync gs{4, 32 * L::G4_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + L::G3_WARPS + 3), status + 6,
                  abort_flag, 0u};
     const int hf = (warp - L::G1_WARPS - L::G2_WARPS - L::G3_WARPS) >> 2;
     for (int li = 0; li < n_local; ++li) {
-      if (!gs.wait(bar_hid, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      tc_fence_after();
-      // GELU of this thread's 64 hidden columns [64 hf, 64 hf + 64), 32 at a time; the
-      // packed result (A of mlp2) goes to the first 32 of those columns, each half
-      // after its own values have been read
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
+      bool ok = true;
+#pragma unroll 1
+      for (int c = 0; c < 2 && ok; ++c) {
+        if (!gs.wait(bar_hid + c, li & 1, SCB_ERR_WAIT_ATTN)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // this thread's 32 hidden columns [32 hf, 32 hf + 32) of chunk c; the packed
+        // result (A of mlp2) goes to the first 16 of them, after they have been read
+        const uint32_t col = L::C_HID + c * 64 + hf * 32;
         float hv[32];
-        const uint32_t col = trow + L::C_HID + hf * 64 + h2 * 32;
-        tmem_ld16x2(col, hv, col + 16, hv + 16);
+        tmem_ld16x2(trow + col, hv, trow + col + 16, hv + 16);
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -597,20 +613,23 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
           a = gelu2_tanh_h2(a);
           pk[j] = *reinterpret_cast<uint32_t*>(&a);
         }
-        tmem_st16u(trow + L::C_HID + hf * 64 + h2 * 16, pk);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      gs.sync();
-      if (gs.leader) {
-        tc_fence_after();
-        const uint32_t d = tmem + L::C_ACC + (li & 1) * T;
+        tmem_st16u(trow + col, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        gs.sync();
+        if (gs.leader) {
+          tc_fence_after();
+          const uint32_t d = tmem + L::C_ACC + (li & 1) * T;
+          // K steps of chunk c: hidden [64 c + 16 k, + 16) sits at H columns
+          // C_HID + 64 c + 32 (k / 2) + 8 (k % 2)
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_f16_ts(d, tmem + L::C_HID + (k >> 2) * 64 + (k & 3) * 8,
-                      d128(L::W_2 + (k >> 2) * 4096 + 32 * (k & 3)), ID_T, 1);
-        umma_commit(bar_out);
+          for (int k = 0; k < 4; ++k)
+            umma_f16_ts(d, tmem + L::C_HID + c * 64 + (k >> 1) * 32 + (k & 1) * 8,
+                        d128(L::W_2 + c * 4096 + 32 * k), ID_T, 1);
+          umma_commit(bar_out + c);
+        }
       }
+      if (!ok) break;
     }
     if (gs.leader) {
       umma_commit(drain + 3);
