@@ -7,11 +7,12 @@
 //      -> LN1 -> A1 -> [qkv = A1.Wqkv'^T + b] -> Q (TMEM), K rows and V rows
 //      (shared memory) -> [S = Q.K^T]
 //   G2 (8 warps, two threads per row, 32 keys each): + rel-pos bias, mask, max
-//      (exchanged through shared memory), P' = 2^(s - max) -> [O' | rowsum =
-//      P'.[V0 | V1 | 1]] -> O = O' / rowsum -> [x1 = O.Wproj^T + y_t.I + b_proj]
-//   G3 (4 warps, one thread per row): LN2(x1) -> A2 -> [hid = A2.W0'^T + b0'] for
-//      the next pair while G4 works on this one, in two 64-column chunks with their
-//      own TMEM buffers; z = acc + b2 -> Z
+//      (exchanged through shared memory), P' = 2^(s - max)
+//      -> [O' | rowsum = P'.[V0 | V1 | 1]]
+//   G3 (4 warps, one thread per row): O = O' / rowsum -> [x1 = O.Wproj^T + y_t.I +
+//      b_proj] -> LN2(x1) -> A2 -> [hid = A2.W0'^T + b0'] for the next pair while G4
+//      works on this one, in two 64-column chunks with their own TMEM buffers;
+//      z = acc + b2 -> Z
 //   G4 (8 warps, two threads per row, 32 columns of a chunk each): per chunk,
 //      2 GELU(hid) -> H -> [acc += H.(W2/2)^T]
 //
@@ -170,12 +171,13 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  // Barriers that complete once per pair come in pairs indexed by the pair's parity
+  // wherever a waiter could otherwise see the barrier two phases ahead of it.
   uint64_t* bar_qkv = bars + 0;
-  uint64_t* bar_s = bars + 1;
-  uint64_t* bar_o = bars + 2;
-  uint64_t* x1_done = bars + 3;   // [2] per x1 accumulator buffer: proj committed
-  uint64_t* acc_free = bars + 5;  // [2] G3 has read z (128 arrivals)
-  uint64_t* so_free = bars + 7;   // [2] per score buffer: G2 has read O' and the row sums (256 arrivals)
+  uint64_t* bar_s = bars + 1;     // [2] per score buffer: S committed
+  uint64_t* bar_o = bars + 3;     // [2] per score buffer: P.V committed
+  uint64_t* x1_done = bars + 5;   // [2] per x1 accumulator buffer: proj committed
+  uint64_t* so_free = bars + 7;   // [2] per score buffer: G3 has read O' and the row sums (128 arrivals)
   uint64_t* bar_hid = bars + 9;   // [2] per hidden chunk: mlp0 committed
   uint64_t* bar_out = bars + 11;  // [2] per hidden chunk: its mlp2 K steps committed
   uint64_t* drain = bars + 13;    // [4] one per issuing group
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
     }
   }
   if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(bars + i, (i == 5 || i == 6) ? 128u : ((i == 7 || i == 8) ? 256u : 1u));
+    for (int i = 0; i < NBAR; ++i) mbar_init(bars + i, (i == 7 || i == 8) ? 128u : 1u);
     mbar_fence_init();
     *abort_flag = 0u;
   }
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       if (!gs.wait(bar_qkv, li & 1, SCB_ERR_WAIT_ATTN)) break;
       // Q of pair li - 1 is an operand of its S UMMA (K and V^T buffers li & 1 were
       // freed with score buffer li & 1)
-      if (li >= 1 && !gs.wait(bar_s, (li - 1) & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (li >= 1 && !gs.wait(bar_s + ((li - 1) & 1), ((li - 1) >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
       tc_fence_after();
       {
         float q[32];
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         const int kb = L::K + (li & 1) * 8192;
         umma_f16_ts(tmem + sbuf, tmem + L::C_Q, d64(kb), ID_S, 0);
         umma_f16_ts(tmem + sbuf, tmem + L::C_Q + 8, d64(kb + 32), ID_S, 1);
-        umma_commit(bar_s);
+        umma_commit(bar_s + (li & 1));
       }
     }
     cp_async_wait_all();
@@ -389,15 +391,14 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       mbar_wait(drain + 0, 0, SCB_ERR_WAIT_ATTN);
     }
   } else if (warp < L::G1_WARPS + L::G2_WARPS) {
-    // ====== G2 (two threads per row, 32 keys each): softmax -> P' -> [O', rowsum]
-    //        -> O -> [x1] ======
+    // ====== G2 (two threads per row, 32 keys each): softmax -> P' -> [O', rowsum] ======
     GroupSync gs{2, 32 * L::G2_WARPS, tid == 160, status + 2, abort_flag, 0u};  // leaders sit on different SMSPs
     const int hf = (warp - L::G1_WARPS) >> 2;
     WinCursor cur;
     cur.init(g.win, 2 * first + slot);
     for (int li = 0; li < n_local; ++li, cur.advance(g.win, win_step)) {
       const uint32_t sbuf = L::C_SB + (li & 1) * 128;
-      if (!gs.wait(bar_s, li & 1, SCB_ERR_WAIT_ATTN)) break;
+      if (!gs.wait(bar_s + (li & 1), (li >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
       tc_fence_after();
       bool last_row, last_col, st;
       (void)cur.pixel(g.win, qi, qj, last_row, last_col, st);
@@ -456,40 +457,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         for (int k = 0; k < 4; ++k)  // K step k = keys 16k .. 16k + 15 = two 8-row groups
           umma_f16_ts(tmem + sbuf + 32, tmem + sbuf + 8 * k, make_sdesc_lbo_sbo(vb + 2048 * k, 8192, 1024, SW_128B),
                       ID_PV, k);
-        umma_commit(bar_o);
-      }
-      if (!gs.wait(bar_o, li & 1, SCB_ERR_WAIT_ATTN)) break;
-      // O of pair li - 1 is an operand of its proj UMMA
-      if (li >= 1 && !gs.wait(x1_done + ((li - 1) & 1), ((li - 1) >> 1) & 1, SCB_ERR_WAIT_ATTN)) break;
-      tc_fence_after();
-      {
-        float o[16];
-        tmem_ld16(trow + sbuf + 32 + slot * 32 + hf * 16, o);  // own window's half of O', this thread's 16 d
-        const float inv = __fdividef(1.f, tmem_ld1(trow + sbuf + 32 + 64));
-        uint32_t po[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) po[j] = pack_half2(o[2 * j] * inv, o[2 * j + 1] * inv);
-        tmem_st8u(trow + L::C_O + hf * 8, po);
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      mbar_arrive(so_free + (li & 1));
-      gs.sync();
-      if (gs.leader) {
-        const int b = li & 1;
-        // accumulator b last held pair li - 2's z: G3 must have read it
-        const bool ok = li < 2 || mbar_wait_abortable(acc_free + b, ((li - 2) >> 1) & 1, abort_flag, SCB_ERR_WAIT_ATTN);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t d = tmem + L::C_ACC + b * T;
-          const int yb = L::Y + (li % 3) * 8192;
-          umma_f16_ts(d, tmem + L::C_O, d64(L::W_PROJ), ID_T, 0);
-          umma_f16_ts(d, tmem + L::C_O + 8, d64(L::W_PROJ + 32), ID_T, 1);
-          umma_f16(d, d64(yb), d64(L::IDENT), ID_T, 1);
-          umma_f16(d, d64(yb + 32), d64(L::IDENT + 32), ID_T, 1);
-          umma_f16(d, d64(L::ONES), d64(L::B_PROJ), ID_T, 1);
-          umma_commit(x1_done + b);
-        }
+        umma_commit(bar_o + (li & 1));
       }
     }
     if (gs.leader) {
@@ -497,8 +465,9 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       mbar_wait(drain + 1, 0, SCB_ERR_WAIT_ATTN);
     }
   } else if (warp < L::G1_WARPS + L::G2_WARPS + L::G3_WARPS) {
-    // ====== G3 (one thread per row): LN2(x1) -> A2 -> [hidden]; z out ======
-    // It runs a pair ahead of G4: LN2 of pair li + 1 while G4 applies GELU to pair
+    // ====== G3 (one thread per row): O = O'/rowsum -> [x1]; LN2(x1) -> A2 -> [hidden];
+    //        z out ======
+    // It runs a pair ahead of G4: proj and LN2 of pair li + 1 while G4 applies GELU to pair
     // li; the hidden layer is two 64-column chunks with their own buffers, and mlp0
     // of chunk c of pair li + 1 is issued as soon as mlp2's K steps of chunk c of
     // pair li (the last reader of that buffer) have completed, so the GELU warps
@@ -540,7 +509,40 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       umma_f16(d, d64(L::ONES), d64(L::B_0 + c * 64 * 64), ID_H64, 1);
       umma_commit(bar_hid + c);
     };
-    bool ok = n_local > 0 && ln2(0);
+    // O' / rowsum of pair li -> O (TMEM) -> [x1 = O.Wproj^T + y_t.I + b_proj]. The O
+    // columns were last read by pair li - 1's proj, which ln2(li - 1) waited for; the
+    // accumulator li & 1 last held pair li - 2's z, which this group has read.
+    auto normproj = [&](int li) -> bool {
+      const int b = li & 1;
+      const uint32_t sbuf = L::C_SB + b * 128;
+      if (!gs.wait(bar_o + b, (li >> 1) & 1, SCB_ERR_WAIT_ATTN)) return false;
+      tc_fence_after();
+      float o[32];
+      tmem_ld16x2(trow + sbuf + 32 + slot * 32, o, trow + sbuf + 48 + slot * 32, o + 16);  // own window's half
+      const float inv = __fdividef(1.f, tmem_ld1(trow + sbuf + 32 + 64));
+      tc_fence_before();
+      mbar_arrive(so_free + b);  // score buffer b may take pair li + 2's qkv
+      uint32_t po[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) po[j] = pack_half2(o[2 * j] * inv, o[2 * j + 1] * inv);
+      tmem_st16u(trow + L::C_O, po);
+      tmem_wait_st();
+      tc_fence_before();
+      gs.sync();
+      if (gs.leader) {
+        tc_fence_after();
+        const uint32_t d = tmem + L::C_ACC + b * T;
+        const int yb = L::Y + (li % 3) * 8192;
+        umma_f16_ts(d, tmem + L::C_O, d64(L::W_PROJ), ID_T, 0);
+        umma_f16_ts(d, tmem + L::C_O + 8, d64(L::W_PROJ + 32), ID_T, 1);
+        umma_f16(d, d64(yb), d64(L::IDENT), ID_T, 1);
+        umma_f16(d, d64(yb + 32), d64(L::IDENT + 32), ID_T, 1);
+        umma_f16(d, d64(L::ONES), d64(L::B_PROJ), ID_T, 1);
+        umma_commit(x1_done + b);
+      }
+      return true;
+    };
+    bool ok = n_local > 0 && normproj(0) && ln2(0);
     if (ok) {
       gs.sync();
       if (gs.leader) {
@@ -553,7 +555,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       if (more) {
         // A2 of pair li is read by both of its mlp0 chunks (one issuer: chunk 1's
         // commit covers chunk 0)
-        if (!gs.wait(bar_hid + 1, li & 1, SCB_ERR_WAIT_ATTN) || !ln2(li + 1)) break;
+        if (!normproj(li + 1) || !gs.wait(bar_hid + 1, li & 1, SCB_ERR_WAIT_ATTN) || !ln2(li + 1)) break;
       }
       if (!gs.wait(bar_out + 0, li & 1, SCB_ERR_WAIT_ATTN)) break;
       if (more && gs.leader) issue_mlp0(0);
@@ -565,7 +567,6 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       float z[32];
       tmem_ld16x2(trow + L::C_ACC + b * T, z, trow + L::C_ACC + b * T + 16, z + 16);
       tc_fence_before();
-      mbar_arrive(acc_free + b);
       bool lr, lc, st;
       const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
       if (pix >= 0 && st) {
