@@ -174,7 +174,7 @@ def reference_arm(a, rank, world):
     }), flush=True)
 
 
-KERNEL_OF_CLASS = {"attention": "window_attn_kernel", "trans_fused": "trans32_ws_kernel + trans64_kernel",
+KERNEL_OF_CLASS = {"attention": "window_attn_kernel", "trans_fused": "trans32_ws_kernel + trans64_ws_kernel",
                    "head": "head_tc_kernel"}
 
 
@@ -277,8 +277,8 @@ def ncu_traffic(path):
     torch.cuda.synchronize()
     prof = be.profile()
     be.close()
-    mine = ("gemm_tc_kernel", "head_tc_kernel", "io_kernel", "mlp_fused_kernel", "trans32_ws_kernel",
-            "trans64_kernel", "window_attn_kernel")
+    mine = ("gemm_tc_kernel", "head_tc_kernel", "io_kernel", "mlp_fused_kernel", "trans32_ws_kernel", "trans64_ws_kernel",
+            "window_attn_kernel")
     ls = [l for l in ls if any(k in l[0] for k in mine)]
     if len(ls) < len(prof):
         raise SystemExit(f"{len(ls)} captured launches of this library, {len(prof)} ops in a forward")

@@ -34,7 +34,7 @@
 #include "io_kernels.cuh"
 #include "trans.cuh"
 #include "trans32ws.cuh"
-#include "trans64.cuh"
+#include "trans64ws.cuh"
 #include "mlp.cuh"
 
 using namespace scb;
@@ -802,18 +802,18 @@ cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
 }
 
 cudaError_t launch_trans64(const Op& op, int sms, cudaStream_t st) {
-  using L = Trans64Layout;
+  using L = T64;
   static bool attr_set[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 16 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(trans64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(trans64_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const long pairs = (op.trans.win.n_windows + 1) / 2;
-  const int grid = (int)std::max(1L, std::min((pairs + 1) / 2, (long)sms));  // two pair pipelines per CTA
-  trans64_kernel<<<grid, 512, L::SMEM, st>>>(op.trans);
+  const int grid = (int)std::max(1L, std::min(pairs, (long)sms));  // one CTA per SM, persistent over pairs
+  trans64_ws_kernel<<<grid, L::THREADS, L::SMEM, st>>>(op.trans);
   return cudaGetLastError();
 }
 
