@@ -289,6 +289,16 @@ __device__ __forceinline__ void u32_to_f32_16(const uint32_t* r, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One 32x32b column: thread t of the warp gets row (lane base + t), column `taddr`.
+// Waits for the load itself (one value: nothing to overlap it with).
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  tmem_wait_ld();
+  asm volatile("" : "+r"(r));
+  return __uint_as_float(r);
+}
+
 // One 16-column load, waited for immediately.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];

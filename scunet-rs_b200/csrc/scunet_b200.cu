@@ -777,9 +777,11 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
   }
   int dev_sms = 148;
   cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, dev);
+  // CTA c takes head c % heads: the grid is a multiple of the head count
   const long pairs = (op.attn.win.n_windows + 1) / 2;
-  const unsigned grid = (unsigned)std::max(1L, std::min(pairs, (long)dev_sms * ATT_CTAS));
-  window_attn_kernel<<<grid, 256, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
+  const long per_head = std::max(1L, std::min(pairs, (long)dev_sms * ATT_CTAS / op.attn.heads));
+  const unsigned grid = (unsigned)(per_head * op.attn.heads);
+  window_attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(op.attn_in, op.attn_out, op.attn_rp, op.attn);
   return cudaGetLastError();
 }
 

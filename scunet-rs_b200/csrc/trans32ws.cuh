@@ -99,16 +99,6 @@ __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// One 32x32b column: thread t of the warp gets row (lane base + t), column `taddr`.
-// Waits for the load itself (one value: nothing to overlap it with).
-__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
-  uint32_t r;
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
-  tmem_wait_ld();
-  asm volatile("" : "+r"(r));
-  return __uint_as_float(r);
-}
-
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Bounded mbarrier wait that also gives up when another group raised `abort_flag`;
