@@ -11,7 +11,7 @@
 //   (tools/network_scunet.py:49-67, cuda/scunet.cu:137-147);
 //   softmax over the 64 keys, O = P.v.
 //
-// Persistent CTAs of 128 threads (four per SM, 128 TMEM columns each) walk pairs of
+// Persistent CTAs of 128 threads (three per SM, 128 TMEM columns each) walk pairs of
 // windows (128 tokens, one UMMA M tile), one thread per token row; a CTA keeps one
 // head. Per pair:
 //   q, k  -> smem [128 x 32] fp16 K-major (64B swizzle)            (UMMA A and B)
@@ -26,8 +26,8 @@
 //                     token of window s reads columns 32 + 32 s .. + 31 and the row
 //                     sum of the fp16 P' it was multiplied with at column 96
 //   out = O / rowsum: fp16 to the output plane at the token's pixel.
-// The next pair's q, k, v are loaded into registers while the current pair computes,
-// so no pair waits a DRAM round trip.
+// The next pair's q, k, v are copied (cp.async) into a second operand buffer while
+// the current pair computes, so no pair waits a DRAM round trip.
 #pragma once
 #include "ptx.cuh"
 
@@ -41,15 +41,18 @@ struct AttnGeom {
   long out_ld;     // elements per pixel row of out
 };
 
-// Layout per CTA (4 CTAs per SM, 128 TMEM columns each). A CTA keeps one head h for
-// its whole life, so its relative-position bias table is built once.
-constexpr int ATT_Q = 0;                  // [128 x 64 B] SW64
-constexpr int ATT_K = 8192;               // [128 x 64 B] SW64
-constexpr int ATT_V = 16384;              // V, MN-major: [64 keys x 128 B] = [V_0 | V_1], then the ones atom
-constexpr int ATT_BIAS = ATT_V + 16384;   // fp16 [64 query positions][64 keys], log2 units, chunk-swizzled
+// Layout per CTA (3 CTAs per SM, 128 TMEM columns each). A CTA keeps one head h for
+// its whole life, so its relative-position bias table is built once. The q, k, v rows
+// of the next pair are copied by cp.async straight into the other of two operand
+// buffers while the current pair computes.
+constexpr int ATT_Q = 0;                  // 2 x [128 x 64 B] SW64
+constexpr int ATT_K = 16384;              // 2 x [128 x 64 B] SW64
+constexpr int ATT_V = 32768;              // 2 x V, MN-major: [64 keys x 128 B] = [V_0 | V_1]
+constexpr int ATT_ONES = 49152;           // [64 keys x 128 B]: N element 64 = 1 (the row sums)
+constexpr int ATT_BIAS = ATT_ONES + 8192; // fp16 [64 query positions][64 keys], log2 units, chunk-swizzled
 constexpr int ATT_BAR = ATT_BIAS + 8192;
 constexpr int ATT_SMEM = ATT_BAR + 64 + 1024;
-constexpr int ATT_CTAS = 4;               // per SM
+constexpr int ATT_CTAS = 3;               // per SM
 constexpr int ATT_THREADS = 128;          // one per token row of a window pair
 
 __global__ void __launch_bounds__(ATT_THREADS, ATT_CTAS)
@@ -78,7 +81,7 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     }
     // the ones atom of the V operand: N element 64 = 1 for every key (the row sums)
     for (int i = tid; i < 64 * 8; i += blockDim.x)
-      *reinterpret_cast<uint4*>(sm + ATT_V + 8192 + swz_off(i >> 3, i & 7, 128)) =
+      *reinterpret_cast<uint4*>(sm + ATT_ONES + swz_off(i >> 3, i & 7, 128)) =
           make_uint4((i & 7) == 0 ? 0x3C00u : 0u, 0u, 0u, 0u);
   }
   if (tid == 0) {
@@ -103,14 +106,17 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     if (pr >= n_pairs || win >= g.win.n_windows) return -1;
     return win_token_pixel(g.win, win, qi, qj, lr, lc, st);
   };
-  // this token's q, k, v of head h: 3 x 64 bytes
-  auto load_qkv = [&](long pix, uint4* d) {
+  // this token's q, k, v of head h (3 x 64 bytes) -> Q, K rows and V row tok, N
+  // elements [32 slot, +32), of operand buffer b; zeros past the last window
+  auto fetch_qkv = [&](long pix, int b) {
+    const __half* src = pix >= 0 ? qkv + pix * g.qkv_ld + h * 32 : qkv;
 #pragma unroll
-    for (int m = 0; m < 3; ++m)
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        d[4 * m + c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(qkv + pix * g.qkv_ld + m * g.t + h * 32) + c)
-                                : make_uint4(0u, 0u, 0u, 0u);
+    for (int c = 0; c < 4; ++c) {
+      cp_async16(sm + ATT_Q + b * 8192 + swz_off(row, c, 64), src + 8 * c, pix >= 0);
+      cp_async16(sm + ATT_K + b * 8192 + swz_off(row, c, 64), src + g.t + 8 * c, pix >= 0);
+      cp_async16(sm + ATT_V + b * 8192 + swz_off(tok, 4 * slot + c, 128), src + 2 * g.t + 8 * c, pix >= 0);
+    }
+    cp_async_commit();
   };
   auto sync_mma = [&]() {
     fence_proxy_async_smem();
@@ -127,30 +133,23 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
   long pair = p0;
   bool lr, lc, st;
   long pix = locate(pair, lr, lc, st);
-  uint4 nx[12];
-  load_qkv(pix, nx);
-  for (; pair < n_pairs; pair += pstride) {
+  fetch_qkv(pix, 0);
+  for (int u = 0; pair < n_pairs; pair += pstride, ++u) {
+    const int b = u & 1;
     const bool last_row = lr, last_col = lc, store = st;
     const long pix_c = pix;
-    uint4 cur[12];
-#pragma unroll
-    for (int m = 0; m < 12; ++m) cur[m] = nx[m];
-    pix = locate(pair + pstride, lr, lc, st);  // the next pair's q, k, v load while this one computes
-    load_qkv(pix, nx);
-    // ---- Q, K rows (64-byte swizzled); V row tok, N elements [32 slot, +32) (MN-major) ----
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      *reinterpret_cast<uint4*>(sm + ATT_Q + swz_off(row, c, 64)) = cur[c];
-      *reinterpret_cast<uint4*>(sm + ATT_K + swz_off(row, c, 64)) = cur[4 + c];
-      *reinterpret_cast<uint4*>(sm + ATT_V + swz_off(tok, 4 * slot + c, 128)) = cur[8 + c];
-    }
+    // the next pair's q, k, v stream into buffer b ^ 1 (its last readers, the S and
+    // P.V UMMAs of pair u - 1, have completed) while this pair computes
+    pix = locate(pair + pstride, lr, lc, st);
+    fetch_qkv(pix, b ^ 1);
+    cp_async_wait_1();  // this thread's rows of pair u have landed
     sync_mma();
     if (tid == 0) {  // S = Q K^T -> TMEM [0, 128)
       constexpr uint32_t id = make_idesc_f16(128, 128);
 #pragma unroll
       for (int k = 0; k < 2; ++k)
-        umma_f16(tmem, make_sdesc(sb + ATT_Q + k * 32, 64, SW_64B), make_sdesc(sb + ATT_K + k * 32, 64, SW_64B), id,
-                 k);
+        umma_f16(tmem, make_sdesc(sb + ATT_Q + b * 8192 + k * 32, 64, SW_64B),
+                 make_sdesc(sb + ATT_K + b * 8192 + k * 32, 64, SW_64B), id, k);
       umma_commit(bar);
     }
     wait_mma();
@@ -204,7 +203,9 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
       constexpr uint32_t id = make_idesc_f16_bmn(128, 80);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        umma_f16_ts(tmem + 32, tmem + 8 * k, make_sdesc_lbo_sbo(sb + ATT_V + 2048 * k, 8192, 1024, SW_128B), id, k);
+        umma_f16_ts(tmem + 32, tmem + 8 * k,
+                    make_sdesc_lbo_sbo(sb + ATT_V + b * 8192 + 2048 * k, ATT_ONES - ATT_V - b * 8192, 1024, SW_128B),
+                    id, k);
       umma_commit(bar);
     }
     wait_mma();
@@ -226,6 +227,7 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     __syncthreads();  // Q, K, V, P' and the TMEM accumulators are reused by the next pair
     tc_fence_after();
   }
+  cp_async_wait_all();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 128);
 }

@@ -99,7 +99,6 @@ __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Bounded mbarrier wait that also gives up when another group raised `abort_flag`;
 // a timeout records `code` and raises the flag.
