@@ -90,3 +90,50 @@ def test_config5_bands_at_4096(scb, be3):
     _, scratch = be3.footprint()
     assert scratch == 0, f"{scratch} bytes of scratch still held after release_scratch"
     assert d <= 1e-4
+
+
+def test_speed_vs_torch_fp32_cuda(scb, be3, weights3):
+    """The speed proxy for the reference's own CUDA path: the same network in torch
+    CUDA FP32 (TF32 off) on the same B200, one 1920x1080 frame (padded to 1088 rows),
+    inputs resident on the device, CUDA-event timed after warm-up. The reference
+    reports its CUDA path 1.1-1.25x slower than upstream torch CUDA
+    (`docs/TECH_NOTES.md:65-69`), so this ratio understates the speed-up over it."""
+    torch = _torch()
+    import scunet_torch
+    import torch.nn.functional as F
+    x = scb.synth.frames(4001, 1, 1080, 1920)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.empty((1, 3, 1080, 1920), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+
+    def ours():
+        be3.forward_dev(xd.data_ptr(), scb.SCB_U8, 1, 3, 1080, 1920, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
+
+    scunet_torch.strict_fp32()
+    wt = {k: torch.as_tensor(v, dtype=torch.float32).cuda().contiguous() for k, v in weights3.tensors.items()}
+    xp = F.pad(xd.float().div_(255), (0, 0, 0, 8), mode="replicate")
+
+    def proxy():
+        with torch.no_grad():
+            scunet_torch.forward_padded(xp, wt)
+
+    def time_ms(fn, stream, warm, reps):
+        with torch.cuda.stream(stream):
+            for _ in range(warm):
+                fn()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(reps):
+                fn()
+            t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / reps
+
+    ms_ours = time_ms(ours, s, 3, 10)
+    ms_proxy = time_ms(proxy, torch.cuda.current_stream(), 1, 3)
+    ratio = ms_proxy / ms_ours
+    print(f"1920x1080 frame: this library {ms_ours:.2f} ms, torch CUDA FP32 {ms_proxy:.1f} ms, "
+          f"ratio {ratio:.1f}x (x1.1-1.25 against the reference CUDA path: "
+          f"{1.1 * ratio:.1f}-{1.25 * ratio:.1f}x)")
+    assert ratio > 1.0
