@@ -144,6 +144,7 @@ constexpr int kMaxResidentB = 40 * 1024;
 
 // Residual slab buffers of the TMA epilogue. Four (three slabs of lookahead) were
 // measured slower than two: the extra staging costs the 1x1 convs pipeline stages.
+// The 3x3 convs measured the same with two to six.
 constexpr int kResBufs = 2;
 
 template <int BN, int BK, int GEO, bool TMAEPI>
@@ -531,6 +532,9 @@ struct Op {
   CUtensorMap mlp_a, mlp_w0, mlp_w2;
   // HEAD: the x1 (f32) and shadow (fp16) planes as TMA store maps
   CUtensorMap head_m32, head_m16;
+  // TAIL: the (y + x1) shadow as a TMA load map (one 128-pixel row segment per box)
+  CUtensorMap tail_map;
+  TailGeom tail{};
 };
 
 // A row band of one image (config 5): full-resolution rows [R0, R0 + rows) of the
@@ -666,7 +670,7 @@ struct scb_ctx {
   __half* wdown[3] = {};
   __half* wup[3] = {};
   __half* whead16 = nullptr;  // [64][32]: K = (ci, ky, kx) zero-padded to 32
-  __half* wtail16 = nullptr;  // [16][9*64]: rows >= in_nc zero, K = (ky, kx, ci)
+  __half* wtail16 = nullptr;  // [32][64]: row 3 * tap + co, K = ci (unused rows zero)
   Arena arena;
   int last_launches = 0;
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
@@ -786,6 +790,7 @@ cudaError_t launch_attn(const Op& op, cudaStream_t st) {
 }
 
 cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, const Op& op, cudaStream_t st);
+cudaError_t launch_tail(scb_ctx* ctx, void* y, const TailGeom& g, const Op& op, cudaStream_t st);
 
 cudaError_t launch_trans32(const Op& op, int sms, cudaStream_t st) {
   using L = T32;
@@ -859,6 +864,21 @@ cudaError_t launch_head(scb_ctx* ctx, const void* x, const HeadGeom& g, const Op
   const long tiles = ((long)g.n * g.rows * g.wp + 127) / 128;
   const int grid = (int)std::max(1L, std::min(tiles, (long)ctx->sms * 3));
   head_tc_kernel<<<grid, 128, HEAD_SMEM, st>>>(x, ctx->whead16, op.head_m32, op.head_m16, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tail(scb_ctx* ctx, void* y, const TailGeom& g, const Op& op, cudaStream_t st) {
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tail_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TAIL_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long units = (long)g.n * g.strips * g.chunks;
+  const int grid = (int)std::max(1L, std::min(units, (long)ctx->sms * 2));
+  tail_tc_kernel<<<grid, TAIL_THREADS, TAIL_SMEM, st>>>(op.tail_map, ctx->wtail16, y, g);
   return cudaGetLastError();
 }
 
@@ -945,13 +965,12 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
       return launch_head(ctx, io.x, g, op, st);
     }
     case Op::TAIL: {
-      GemmOp t = op.gemm;  // the 3x3 implicit GEMM over the (y + x1) shadow, N = 16
-      t.e.nchw_out = io.y;
-      t.e.nchw_c = io.c;
-      t.e.nchw_h = io.h;
-      t.e.nchw_w = io.w;
-      t.e.nchw_u8 = io.y_u8;
-      return launch_gemm(t, ctx->sms, st);
+      TailGeom g = op.tail;
+      g.c = io.c;
+      g.h = io.h;
+      g.w = io.w;
+      g.u8 = io.y_u8;
+      return launch_tail(ctx, io.y, g, op, st);
     }
     case Op::GEMM:
       return launch_gemm(op.gemm, ctx->sms, st);
@@ -973,8 +992,11 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
 // written once, weights included: the numerator of its memory roofline.
 double op_bytes(const Arena& A, const Op& op, const Io& io) {
   switch (op.kind) {
-    case Op::GEMM:
-    case Op::TAIL: {
+    case Op::TAIL: {  // the shadow in, the crop out, the weights
+      const TailGeom& g = op.tail;
+      return (double)g.n * g.rows_out * g.W * 64 * 2 + 32.0 * 64 * 2 + (double)A.n * io.h * io.w * io.c * (io.y_u8 ? 1 : 4);
+    }
+    case Op::GEMM: {
       const GemmOp& o = op.gemm;
       const GemmGeom& g = o.g;
       const GemmEpi& e = o.e;
@@ -996,7 +1018,6 @@ double op_bytes(const Arena& A, const Op& op, const Io& io) {
       if (e.skip32) per_elem += 4;
       double b = px_in * cin * 2 + n_cols * cin * taps * 2 + px * n_cols * per_elem;
       if (e.ln_out) b += px * e.ln_n * 2;
-      if (op.kind == Op::TAIL) b += (double)A.n * io.h * io.w * io.c * (io.y_u8 ? 1 : 4);
       return b;
     }
     case Op::TRANS: {
@@ -1441,10 +1462,19 @@ int build_plan(scb_ctx* ctx, Arena& A) {
   Op tail{};
   tail.kind = Op::TAIL;
   {
-    Maker mk{&err};
-    if (!mk.conv3(tail.gemm, A.xs[0], R0.n, R0.H, R0.W, 64, 64, ctx->wtail16, 16, false, R0.row0, R0.rows))
-      return fail(ctx, SCB_EINVAL, err);
-    tail.gemm.e.nchw_row_off = R0.grow0 - R0.row0;
+    const uint64_t dims[4] = {64, (uint64_t)R0.W, (uint64_t)R0.H, (uint64_t)R0.n};
+    const uint64_t str[3] = {64 * 2, (uint64_t)R0.W * 64 * 2, (uint64_t)R0.H * R0.W * 64 * 2};
+    const uint32_t box[4] = {64, 128, 1, 1};
+    if (!encode_map(&tail.tail_map, A.xs[0], 4, dims, str, box, 2, 128, err)) return fail(ctx, SCB_EINVAL, err);
+    TailGeom& tg = tail.tail;
+    tg.n = R0.n;
+    tg.H = R0.H;
+    tg.W = R0.W;
+    tg.row0 = R0.row0;
+    tg.rows_out = R0.rows;
+    tg.row_off = R0.grow0 - R0.row0;
+    tg.strips = (R0.W + TAIL_COLS - 1) / TAIL_COLS;
+    tg.chunks = (R0.rows + TAIL_ROWS - 1) / TAIL_ROWS;
   }
   tail.tag = TAG_TAIL;
   tail.flops = 2.0 * P0 * 9 * 64 * ctx->in_nc;
@@ -1635,10 +1665,12 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
   p = need("m_tail.0.weight", {in_nc, dim, 3, 3});
   if (!p) return fail(nullptr, SCB_ENOWEIGHT, tab.err);
   {
-    std::vector<float> t16((size_t)16 * 9 * dim, 0.f);
+    // m_tail as the tail kernel's B operand: row 3 * tap + co, K = ci (rows 27..31
+    // and those of absent output channels zero)
+    std::vector<float> t16((size_t)32 * dim, 0.f);
     for (int co = 0; co < in_nc; ++co)
       for (int ci = 0; ci < dim; ++ci)
-        for (int k = 0; k < 9; ++k) t16[((size_t)co * 9 + k) * dim + ci] = p[((size_t)co * dim + ci) * 9 + k];
+        for (int k = 0; k < 9; ++k) t16[((size_t)3 * k + co) * dim + ci] = p[((size_t)co * dim + ci) * 9 + k];
     o_tail16 = blob.half(t16);
     const float* hw = tab.get("m_head.0.weight", {dim, in_nc, 3, 3});
     std::vector<float> h16((size_t)dim * 32, 0.f);
