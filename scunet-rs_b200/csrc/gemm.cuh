@@ -78,6 +78,13 @@ struct GemmGeom {
   // 1: all of B (every k block of the op's single N tile) is loaded into shared
   // memory once per CTA and stays there; the pipeline stages then carry A only
   int b_res;
+  // flat GEMMs and 3x3 convs with an fp16 residual (TMA epilogue, BN <= 128):
+  // > 0 = the residual enters the accumulator on the tensor cores as res_kb =
+  // BN / BK more k blocks per tile: k block j is A = the tile's residual columns
+  // [n0 + j BK, + BK) (EpiMaps::resA), added into accumulator columns
+  // [j BK, + BK) by UMMAs of N = 32 against slices of a 32 x 32 identity B (built
+  // in shared memory). Exact: fp16 x 1 summed in fp32.
+  int res_kb;
 };
 
 struct GemmEpi {
@@ -116,6 +123,7 @@ struct GemmEpi {
   // (GEO_FLAT, no activation, fp16 residual at most).
   int st_res16, st_res32, st_skip, st_out16, st_out32, st_ln;
   int st_res_bytes, st_out_bytes;  // bytes of one buffer of all residual / output slabs
+  int st_ident_bytes;              // the residual k blocks' 32 x 32 identity B (fp16), first in staging
   int res_bufs;                    // residual buffers (2..4): slabs are requested res_bufs - 1 ahead
 };
 
@@ -123,6 +131,7 @@ struct GemmEpi {
 // M tile's pixel block.
 struct EpiMaps {
   CUtensorMap res16, res32, skip, out16, out32, lnout, out16b;
+  CUtensorMap resA;  // the residual as an A operand: box = BK channels x the tile's pixels
 };
 
 
@@ -307,6 +316,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  constexpr bool RES_MMA = TMAEPI && (GEO == GEO_FLAT || is_conv3(GEO)) && BN <= 128;
+  if (RES_MMA && g.res_kb > 0) {
+    // the 32 x 32 identity B of the residual k blocks: K-major 64-byte rows,
+    // 64B-swizzled like a TMA-loaded tile
+    for (int idx = threadIdx.x; idx < 32 * 4; idx += blockDim.x) {
+      const int n = idx >> 2, c = idx & 3;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      const int k = n - c * 8;  // position of the one inside this chunk, if any
+      if (k >= 0 && k < 8) w[k >> 1] = (k & 1) ? 0x3C000000u : 0x00003C00u;
+      *reinterpret_cast<uint4*>(staging + swz_off(n, c, 64)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -366,6 +388,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           if (!b_res) load_b(sa + L::A_BYTES, &full[s], kb, n0);
         }
+        if (RES_MMA) {
+          for (int j = 0; j < g.res_kb && ok; ++j, ++it) {
+            const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[s], 128 * BK * 2);
+            if (GEO == GEO_FLAT)
+              tma_load_2d(smem + s * SBYTES, &em.resA, &full[s], n0 + j * BK, mt * 128);
+            else
+              tma_load_4d(smem + s * SBYTES, &em.resA, &full[s], n0 + j * BK, x0, y0, img);
+          }
+        }
       }
     }
   } else if (warp == 1) {
@@ -413,6 +446,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           umma_commit(&empty[s]);
         }
+        if (RES_MMA) {
+          // accumulator columns j BK + 32 h + n += A channels 32 h + 16 q + k' (k' < 16)
+          // against identity rows n, columns 16 q + k': a one where n = 16 q + k'
+          constexpr uint32_t IDESC_R = make_idesc_f16(128, 32);
+          const uint32_t si = smem_u32(staging);
+          for (int j = 0; j < g.res_kb && ok; ++j, ++it) {
+            const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            if (!mbar_wait(&full[s], ph, SCB_ERR_WAIT_FULL)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * SBYTES);
+#pragma unroll
+            for (int h = 0; h < BK / 32; ++h)
+#pragma unroll
+              for (int q = 0; q < 2; ++q)
+                umma_f16(d_tmem + j * BK + h * 32, make_sdesc(sa + (2 * h + q) * 32, ROWB, SWZ),
+                         make_sdesc(si + q * 32, 64, SW_64B), IDESC_R, 1);
+            umma_commit(&empty[s]);
+          }
+        }
         umma_commit(&acc_full[a]);
       }
     }
@@ -424,10 +476,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool has_res = e.st_res16 >= 0 || e.st_res32 >= 0 || e.st_skip >= 0;
     uint32_t t = 0, rs = 0, os = 0;  // tiles, residual slabs consumed, output slabs stored
     const uint32_t NRES = (uint32_t)e.res_bufs;
-    uint8_t* out_stage = staging + NRES * e.st_res_bytes;
+    uint8_t* res_stage = staging + e.st_ident_bytes;
+    uint8_t* out_stage = res_stage + NRES * e.st_res_bytes;
     auto issue_res = [&](int mt, int col, uint32_t idx) {
       const uint32_t b = idx % NRES;
-      uint8_t* base = staging + b * e.st_res_bytes;
+      uint8_t* base = res_stage + b * e.st_res_bytes;
       mbar_arrive_expect_tx(&res_full[b], e.st_res_bytes);
       if (e.st_res16 >= 0) epi_slab_load<GEO>(base + e.st_res16, &em.res16, &res_full[b], col, mt, g);
       if (e.st_res32 >= 0) epi_slab_load<GEO>(base + e.st_res32, &em.res32, &res_full[b], col, mt, g);
@@ -532,7 +585,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (has_res) {
           const uint32_t b = rs % NRES;
           mbar_wait(&res_full[b], (rs / NRES) & 1, SCB_ERR_WAIT_ACC);
-          const uint8_t* base = staging + b * e.st_res_bytes;
+          const uint8_t* base = res_stage + b * e.st_res_bytes;
           if (e.st_res16 >= 0) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {

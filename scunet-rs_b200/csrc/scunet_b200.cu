@@ -147,6 +147,13 @@ constexpr int kMaxResidentB = 40 * 1024;
 // The 3x3 convs measured the same with two to six.
 constexpr int kResBufs = 2;
 
+// An fp16 residual of a flat GEMM or 3x3 conv (BN <= 128, TMA epilogue) is added on
+// the tensor cores as extra k blocks against an identity B, not in the epilogue.
+#ifndef SCB_RESIDUAL_MMA
+#define SCB_RESIDUAL_MMA 1
+#endif
+constexpr bool kResidualMma = SCB_RESIDUAL_MMA != 0;
+
 template <int BN, int BK, int GEO, bool TMAEPI>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   using L = GemmSmem<BN, BK, GEO>;
@@ -161,7 +168,7 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   }
   GemmEpi e = op.e;
   e.res_bufs = e.st_res_bytes ? kResBufs : 2;
-  const int staging = TMAEPI ? e.res_bufs * e.st_res_bytes + 2 * e.st_out_bytes : 0;
+  const int staging = TMAEPI ? e.st_ident_bytes + e.res_bufs * e.st_res_bytes + 2 * e.st_out_bytes : 0;
   GemmGeom g = op.g;
   const int bres_bytes = g.num_kb * L::B_BYTES;
   g.b_res = g.n_tiles == 1 && bres_bytes <= kMaxResidentB;
@@ -423,7 +430,8 @@ struct Maker {
   bool finish_epi(GemmOp& op) {
     GemmEpi& e = op.e;
     e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = e.st_ln = -1;
-    e.st_res_bytes = e.st_out_bytes = 0;
+    e.st_res_bytes = e.st_out_bytes = e.st_ident_bytes = 0;
+    op.g.res_kb = 0;
     op.tma_epi = false;
     if (e.out16b && (e.out16_split % 32 || e.out16_split <= 0 || e.out16_split >= op.g.n_total)) {
       *err = "a split fp16 output must split at a multiple of 32 columns";
@@ -439,7 +447,28 @@ struct Maker {
     if (!ln_tma || e.nchw_out || op.geo == GEO_UP2 || !tma_epi_supported(op.geo, op.bn, op.bk)) return true;
     const int N = op.g.n_total;
     int off = 0;
-    if (e.res16) {
+    if (e.res16 && kResidualMma && (is_conv3(op.geo) || op.geo == GEO_FLAT) && op.bn <= 128 && !e.res32 &&
+        !e.skip32 && !e.ln_out && e.act == ACT_NONE) {
+      // the residual as extra k blocks on the tensor cores (A = its pixels, B = I);
+      // not under an activation, which the epilogue applies before the residual
+      const GemmGeom& g = op.g;
+      const uint32_t sw = op.bk * 2;
+      if (op.geo == GEO_FLAT) {
+        const uint64_t dims[2] = {(uint64_t)N, (uint64_t)g.M};
+        const uint64_t str[1] = {(uint64_t)e.res16_ld * 2};
+        const uint32_t box[2] = {(uint32_t)op.bk, 128};
+        if (!encode_map(&op.em.resA, e.res16, 2, dims, str, box, 2, sw, *err)) return false;
+      } else {
+        const uint64_t n = (uint64_t)g.M / ((uint64_t)g.H * g.W);
+        const uint64_t dims[4] = {(uint64_t)N, (uint64_t)g.W, (uint64_t)(g.row0 + g.rows_out), n};
+        const uint64_t str[3] = {(uint64_t)e.res16_ld * 2, (uint64_t)g.W * e.res16_ld * 2,
+                                 (uint64_t)g.H * g.W * e.res16_ld * 2};
+        const uint32_t box[4] = {(uint32_t)op.bk, (uint32_t)g.TW, (uint32_t)g.TH, 1};
+        if (!encode_map(&op.em.resA, e.res16, 4, dims, str, box, 2, sw, *err)) return false;
+      }
+      op.g.res_kb = op.bn / op.bk;
+      e.st_ident_bytes = 2048;
+    } else if (e.res16) {
       if (!stream_map(op, &op.em.res16, e.res16, e.res16_ld, N, 2)) return false;
       e.st_res16 = off;
       off += 128 * 64;
