@@ -15,8 +15,12 @@
 //   GEO_DOWN2 2x2 / stride 2 conv: the input viewed as 5-D (C, dx, W/2, dy, rows/2);
 //             tap (dy, dx) of a TH x TW output block is one TMA box.
 //   GEO_UP2   2x2 / stride 2 transposed conv: a plain GEMM over input pixels with
-//             N ordered (dy, dx, c_out); the epilogue scatters each N tile to the
-//             output pixel (2y+dy, 2x+dx) (pixel shuffle).
+//             N ordered (dy, dx, c_out); each N tile lies in one output quadrant
+//             (dy, dx) and goes to output pixels (2y+dy, 2x+dx) (pixel shuffle).
+//             With the TMA epilogue the M tiles are TW x TH input pixels (A: a
+//             3-D box) and an output slab is one box of a 5-D view of the output
+//             (channel, dx, x, dy, row); the direct epilogue takes 128
+//             consecutive input pixels and scatters per thread.
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
 // UMMA issuer (one elected lane), warps 2..5 = epilogue (thread = accumulator row).
@@ -209,11 +213,20 @@ __device__ __forceinline__ long row_pixel(const GemmGeom& g, int mt, int r, int 
     const int y = ty * g.TH + r / g.TW, x = tx * g.TW + r % g.TW;
     if (x >= g.W || y >= g.H) return -1;
     return (long)y * g.W + x;
-  } else {  // GEO_UP2
-    const long p = (long)mt * 128 + r;
-    if (p >= g.M) return -1;
-    const long R = p / g.up_w;
-    const int x = (int)(p - R * g.up_w);
+  } else {  // GEO_UP2: flat tiles of 128 input pixels, or TW x TH tiles when g.TW > 0
+    long R;
+    int x;
+    if (g.TW > 0) {
+      const int ty = mt / g.tiles_x;
+      R = (long)ty * g.TH + r / g.TW;
+      x = (mt - ty * g.tiles_x) * g.TW + r % g.TW;
+      if (x >= g.up_w || R >= g.H) return -1;
+    } else {
+      const long p = (long)mt * 128 + r;
+      if (p >= g.M) return -1;
+      R = p / g.up_w;
+      x = (int)(p - R * g.up_w);
+    }
     const int d = n0 / g.up_cout;
     col0 = n0 - d * g.up_cout;
     return (2 * R + (d >> 1)) * (2L * g.up_w) + 2 * x + (d & 1);
@@ -233,7 +246,7 @@ __device__ __forceinline__ void tile_origin(const GemmGeom& g, int mt, int& img,
     const int ty = rem / g.tiles_x;
     y0 = g.row0 + ty * g.TH;
     x0 = (rem - ty * g.tiles_x) * g.TW;
-  } else if (GEO == GEO_DOWN2) {
+  } else if (GEO == GEO_DOWN2 || (GEO == GEO_UP2 && g.TW > 0)) {
     const int ty = mt / g.tiles_x;
     y0 = ty * g.TH;
     x0 = (mt - ty * g.tiles_x) * g.TW;
@@ -246,12 +259,16 @@ __device__ __forceinline__ void epi_slab_load(void* dst, const CUtensorMap* m, u
                                               const GemmGeom& g) {
   int img, y0, x0;
   tile_origin<GEO>(g, mt, img, y0, x0);
-  if (is_conv3(GEO))
+  if (is_conv3(GEO)) {
     tma_load_4d(dst, m, bar, col, x0, y0, img);
-  else if (GEO == GEO_DOWN2)
+  } else if (GEO == GEO_DOWN2) {
     tma_load_3d(dst, m, bar, col, x0, y0);
-  else
+  } else if (GEO == GEO_UP2) {  // the output quadrant (dy, dx) of GEMM column col
+    const int d = col / g.up_cout;
+    tma_load_5d(dst, m, bar, col - d * g.up_cout, d & 1, x0, d >> 1, y0);
+  } else {
     tma_load_2d(dst, m, bar, col, mt * 128);
+  }
 }
 
 template <int GEO>
@@ -259,12 +276,16 @@ __device__ __forceinline__ void epi_slab_store(const CUtensorMap* m, const void*
                                                const GemmGeom& g) {
   int img, y0, x0;
   tile_origin<GEO>(g, mt, img, y0, x0);
-  if (is_conv3(GEO))
+  if (is_conv3(GEO)) {
     tma_store_4d(m, src, col, x0, y0, img);
-  else if (GEO == GEO_DOWN2)
+  } else if (GEO == GEO_DOWN2) {
     tma_store_3d(m, src, col, x0, y0);
-  else
+  } else if (GEO == GEO_UP2) {  // the output quadrant (dy, dx) of GEMM column col
+    const int d = col / g.up_cout;
+    tma_store_5d(m, src, col - d * g.up_cout, d & 1, x0, d >> 1, y0);
+  } else {
     tma_store_2d(m, src, col, mt * 128);
+  }
 }
 
 // Named barrier over the four epilogue warps only.
@@ -369,7 +390,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
           uint8_t* sa = smem + s * SBYTES;
           mbar_arrive_expect_tx(&full[s], b_res ? L::A_TX : L::A_TX + L::B_BYTES);
-          if (GEO == GEO_FLAT || GEO == GEO_UP2) {
+          if (GEO == GEO_UP2 && g.TW > 0) {
+            tma_load_3d(sa, &tmA, &full[s], kb * BK, x0, y0);
+          } else if (GEO == GEO_FLAT || GEO == GEO_UP2) {
             tma_load_2d(sa, &tmA, &full[s], kb * BK, mt * 128);
           } else if (GEO == GEO_CONV3) {
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;

@@ -201,6 +201,9 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_TCASE(256, 64, GEO_CONV3)
   SCB_GEMM_TCASE(128, 64, GEO_DOWN2)
   SCB_GEMM_TCASE(256, 64, GEO_DOWN2)
+  SCB_GEMM_TCASE(64, 64, GEO_UP2)
+  SCB_GEMM_TCASE(128, 64, GEO_UP2)
+  SCB_GEMM_TCASE(256, 64, GEO_UP2)
   SCB_GEMM_CASE(32, 32, GEO_FLAT)
   SCB_GEMM_CASE(32, 64, GEO_FLAT)
   SCB_GEMM_CASE(64, 64, GEO_FLAT)
@@ -225,7 +228,8 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
 bool tma_epi_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{64, 64, GEO_FLAT},   {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
                                {128, 32, GEO_FLAT},  {32, 32, GEO_CONV3X}, {32, 32, GEO_CONV3W}, {64, 64, GEO_CONV3X}, {128, 64, GEO_CONV3X}, {256, 64, GEO_CONV3},
-                               {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}};
+                               {128, 64, GEO_DOWN2}, {256, 64, GEO_DOWN2}, {64, 64, GEO_UP2},    {128, 64, GEO_UP2},
+                               {256, 64, GEO_UP2}};
   for (auto& r : tab)
     if (r[0] == bn && r[1] == bk && r[2] == geo) return true;
   return false;
@@ -416,6 +420,14 @@ struct Maker {
       const uint64_t str[3] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es, (uint64_t)g.H * g.W * ld * es};
       const uint32_t box[4] = {32, (uint32_t)g.TW, (uint32_t)g.TH, 1};
       return encode_map(m, base, 4, dims, str, box, es, sw, *err);
+    } else if (op.geo == GEO_UP2) {
+      // output pixel (2R + dy, 2x + dx) of input pixel (R, x) as (channel, dx, x, dy, R)
+      const uint64_t cw = (uint64_t)ld * es;
+      const uint64_t dims[5] = {(uint64_t)g.up_cout, 2, (uint64_t)g.W, 2, (uint64_t)g.H};
+      const uint64_t str[4] = {cw, 2 * cw, 2 * (uint64_t)g.W * cw, 4 * (uint64_t)g.W * cw};
+      const uint32_t box[5] = {32, 1, (uint32_t)g.TW, 1, (uint32_t)g.TH};
+      (void)cols;
+      return encode_map(m, base, 5, dims, str, box, es, sw, *err);
     } else {  // GEO_DOWN2
       const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)g.W, (uint64_t)g.H};
       const uint64_t str[2] = {(uint64_t)ld * es, (uint64_t)g.W * ld * es};
@@ -444,7 +456,8 @@ struct Maker {
     }
     // the TMA epilogue's LayerNorm: flat GEMMs without activation, fp16 residual at most
     const bool ln_tma = !e.ln_out || (op.geo == GEO_FLAT && e.act == ACT_NONE && !e.res32 && !e.skip32);
-    if (!ln_tma || e.nchw_out || op.geo == GEO_UP2 || !tma_epi_supported(op.geo, op.bn, op.bk)) return true;
+    if (!ln_tma || e.nchw_out || (op.geo == GEO_UP2 && op.g.TW == 0) || !tma_epi_supported(op.geo, op.bn, op.bk))
+      return true;
     const int N = op.g.n_total;
     int off = 0;
     if (e.res16 && kResidualMma && (is_conv3(op.geo) || op.geo == GEO_FLAT) && op.bn <= 128 && !e.res32 &&
@@ -509,7 +522,25 @@ struct Maker {
   bool up2(GemmOp& op, const __half* x, int n, int h, int w, int cin, const __half* wt, int cout) {
     op.g.up_w = w;
     op.g.up_cout = cout;
-    return flat(op, x, (long)n * h * w, cin, cin, wt, 4 * cout, GEO_UP2);
+    if (!flat(op, x, (long)n * h * w, cin, cin, wt, 4 * cout, GEO_UP2)) return false;
+    if (tma_epi_supported(GEO_UP2, op.bn, op.bk)) {
+      // TW x TH tiles of input pixels over the stacked rows, for the TMA epilogue
+      int TW, TH;
+      pick_tile(w, TW, TH);
+      const int rows = n * h;
+      const uint64_t dims[3] = {(uint64_t)cin, (uint64_t)w, (uint64_t)rows};
+      const uint64_t str[2] = {(uint64_t)cin * 2, (uint64_t)w * cin * 2};
+      const uint32_t box[3] = {(uint32_t)op.bk, (uint32_t)TW, (uint32_t)TH};
+      if (!encode_map(&op.ta, x, 3, dims, str, box, 2, op.bk * 2, *err)) return false;
+      op.g.W = w;
+      op.g.H = rows;
+      op.g.TW = TW;
+      op.g.TH = TH;
+      op.g.tiles_x = (w + TW - 1) / TW;
+      op.g.tiles_y = (rows + TH - 1) / TH;
+      op.g.m_tiles = op.g.tiles_x * op.g.tiles_y;
+    }
+    return true;
   }
 };
 
