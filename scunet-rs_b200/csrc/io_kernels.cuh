@@ -61,34 +61,46 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
   uint32_t phase = 0;
   const long npx = (long)g.n * g.rows * g.wp;
   const long tiles = (npx + 127) / 128;
-  for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+  // The 27 input taps of this thread's pixel of `tile`, as the raw bits loaded (a
+  // uint8 value or an f32 bit pattern; 0 outside the image = the conv's zero pad):
+  // the next tile's loads are issued before this tile's MMA wait and epilogue and
+  // converted only when they are written to shared memory, so their latency is
+  // hidden behind that work.
+  auto gather = [&](long tile, uint32_t* raw) {
     const long p = tile * 128 + tid;
-    float in[32];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) in[k] = 0.f;
-    if (p < npx) {
-      const int img = (int)(p / ((long)g.rows * g.wp));
-      const int rem = (int)(p - (long)img * g.rows * g.wp);
-      const int y = g.row0 + rem / g.wp, xx = rem % g.wp;
+    for (int k = 0; k < 27; ++k) raw[k] = 0u;
+    if (tile >= tiles || p >= npx) return;
+    const int img = (int)(p / ((long)g.rows * g.wp));
+    const int rem = (int)(p - (long)img * g.rows * g.wp);
+    const int y = g.row0 + rem / g.wp, xx = rem % g.wp;
 #pragma unroll
-      for (int ci = 0; ci < 3; ++ci) {
-        if (ci < g.c) {
+    for (int ci = 0; ci < 3; ++ci) {
+      if (ci < g.c) {
 #pragma unroll
-          for (int ky = 0; ky < 3; ++ky) {
+        for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
-              const int yy = y + ky - 1, xq = xx + kx - 1;
-              if (yy >= 0 && yy < g.hp && xq >= 0 && xq < g.wp) {
-                const int sy = min(yy, g.h - 1), sx = min(xq, g.w - 1);
-                const long off = (((long)img * g.c + ci) * g.h + sy) * g.w + sx;
-                in[(ci * 3 + ky) * 3 + kx] = g.in_u8 ? (float)reinterpret_cast<const uint8_t*>(x)[off] * (1.0f / 255.0f)
-                                                     : reinterpret_cast<const float*>(x)[off];
-              }
+          for (int kx = 0; kx < 3; ++kx) {
+            const int yy = y + ky - 1, xq = xx + kx - 1;
+            if (yy >= 0 && yy < g.hp && xq >= 0 && xq < g.wp) {
+              const int sy = min(yy, g.h - 1), sx = min(xq, g.w - 1);
+              const long off = (((long)img * g.c + ci) * g.h + sy) * g.w + sx;
+              raw[(ci * 3 + ky) * 3 + kx] = g.in_u8 ? (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(x) + off)
+                                                    : __ldg(reinterpret_cast<const uint32_t*>(x) + off);
             }
           }
         }
       }
     }
+  };
+  uint32_t raw[27];
+  gather(blockIdx.x, raw);
+  for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    float in[32];
+#pragma unroll
+    for (int k = 0; k < 27; ++k) in[k] = g.in_u8 ? (float)raw[k] * (1.0f / 255.0f) : __uint_as_float(raw[k]);
+#pragma unroll
+    for (int k = 27; k < 32; ++k) in[k] = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       *reinterpret_cast<uint4*>(sm + swz_off(tid, c, 64)) =
@@ -105,6 +117,7 @@ head_tc_kernel(const void* __restrict__ x, const __half* __restrict__ wk /*[64][
         umma_f16(tmem, make_sdesc(sb + k * 32, 64, SW_64B), make_sdesc(sb + 8192 + k * 32, 64, SW_64B), id, k);
       umma_commit(bar);
     }
+    gather(tile + gridDim.x, raw);
     mbar_wait(bar, phase, SCB_ERR_WAIT_ATTN);
     phase ^= 1;
     tc_fence_after();
