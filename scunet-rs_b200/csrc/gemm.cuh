@@ -82,7 +82,7 @@ struct GemmGeom {
   // 1: all of B (every k block of the op's single N tile) is loaded into shared
   // memory once per CTA and stays there; the pipeline stages then carry A only
   int b_res;
-  // flat GEMMs and 3x3 convs with an fp16 residual (TMA epilogue, BN <= 128):
+  // flat GEMMs and 3x3 convs with an fp16 residual (TMA epilogue, no activation):
   // > 0 = the residual enters the accumulator on the tensor cores as res_kb =
   // BN / BK more k blocks per tile: k block j is A = the tile's residual columns
   // [n0 + j BK, + BK) (EpiMaps::resA), added into accumulator columns
@@ -337,7 +337,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
-  constexpr bool RES_MMA = TMAEPI && (GEO == GEO_FLAT || is_conv3(GEO)) && BN <= 128;
+  constexpr bool RES_MMA = TMAEPI && (GEO == GEO_FLAT || is_conv3(GEO));
   if (RES_MMA && g.res_kb > 0) {
     // the 32 x 32 identity B of the residual k blocks: K-major 64-byte rows,
     // 64B-swizzled like a TMA-loaded tile
@@ -548,7 +548,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
             }
           }
-          if (e.res16 && p < g.M) {
+          if (e.res16 && g.res_kb == 0 && p < g.M) {  // (else already in the accumulator)
             const uint4* src = reinterpret_cast<const uint4*>(e.res16 + p * e.res16_ld + n0 + c);
 #pragma unroll
             for (int h = 0; h < 4; ++h) {

@@ -147,7 +147,7 @@ constexpr int kMaxResidentB = 40 * 1024;
 // The 3x3 convs measured the same with two to six.
 constexpr int kResBufs = 2;
 
-// An fp16 residual of a flat GEMM or 3x3 conv (BN <= 128, TMA epilogue) is added on
+// An fp16 residual of a flat GEMM or 3x3 conv (TMA epilogue, no activation) is added on
 // the tensor cores as extra k blocks against an identity B, not in the epilogue.
 #ifndef SCB_RESIDUAL_MMA
 #define SCB_RESIDUAL_MMA 1
@@ -460,8 +460,8 @@ struct Maker {
       return true;
     const int N = op.g.n_total;
     int off = 0;
-    if (e.res16 && kResidualMma && (is_conv3(op.geo) || op.geo == GEO_FLAT) && op.bn <= 128 && !e.res32 &&
-        !e.skip32 && !e.ln_out && e.act == ACT_NONE) {
+    if (e.res16 && kResidualMma && (is_conv3(op.geo) || op.geo == GEO_FLAT) && !e.res32 && !e.skip32 &&
+        e.act == ACT_NONE) {
       // the residual as extra k blocks on the tensor cores (A = its pixels, B = I);
       // not under an activation, which the epilogue applies before the residual
       const GemmGeom& g = op.g;
