@@ -30,14 +30,16 @@
 // epilogue staging space.
 //
 // Two epilogues:
-//   TMAEPI = true : asynchronous. The epilogue works in 32-column slabs. Residual
-//                   slabs (fp16/fp32/skip) are TMA-loaded into swizzled smem one
-//                   slab ahead (the first before the accumulator wait); outputs are
-//                   written to swizzled smem staging and leave through TMA bulk
-//                   tensor stores, double-buffered. Every global byte moves in full
-//                   lines through the TMA unit.
-//   TMAEPI = false: per-thread vector loads/stores; needed for the LayerNorm
-//                   second pass, the pixel-shuffle (UP2) and crop-to-NCHW stores.
+//   TMAEPI = true : asynchronous. The epilogue works in 32-column slabs. An fp16
+//                   residual without an activation enters the accumulator as
+//                   extra UMMA k blocks (GemmGeom::res_kb); other residual slabs
+//                   (fp32/skip) are TMA-loaded into swizzled smem one slab ahead
+//                   (the first before the accumulator wait); outputs are written to
+//                   swizzled smem staging and leave through TMA bulk tensor stores,
+//                   double-buffered. Every global byte moves in full lines through
+//                   the TMA unit.
+//   TMAEPI = false: per-thread vector loads/stores, for the variants without a TMA
+//                   one (and the LayerNorm of non-flat GEMMs).
 #pragma once
 #include <cuda.h>
 #include "ptx.cuh"
@@ -116,12 +118,6 @@ struct GemmEpi {
   __half* ln_out;
   long ln_ld;
   int ln_lo, ln_n;
-  // Crop-to-NCHW output (the tail conv): columns [0, nchw_c) of pixels inside the
-  // h x w crop of each image go to nchw_out[img][c][y][x], as f32 or as uint8
-  // quantised clamp(v,0,1)*255+0.5 truncated (src/image.rs:60-63).
-  void* nchw_out;
-  int nchw_c, nchw_h, nchw_w, nchw_u8;
-  int nchw_row_off;  // image row of stored row y is y + nchw_row_off
   // TMA epilogue: staging offsets (bytes within one buffer) of each stream's
   // [128 x 32-column] slab; -1 = stream absent. st_ln: the LayerNorm output slab
   // (GEO_FLAT, no activation, fp16 residual at most).
@@ -736,22 +732,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const float2 f = __half22float2(gelu_tanh_h2(__floats2half2_rn(v[j], v[j + 1])));
             v[j] = f.x;
             v[j + 1] = f.y;
-          }
-        }
-        if (p >= 0 && e.nchw_out != nullptr && c == 0) {
-          const long hw = (long)g.H * g.W;
-          const int img = (int)(p / hw);
-          const int rem = (int)(p - img * hw);
-          const int x = rem % g.W;
-          const int y = rem / g.W + e.nchw_row_off;
-          if (y >= 0 && y < e.nchw_h && x < e.nchw_w) {
-            for (int co = 0; co < e.nchw_c; ++co) {
-              const long o = (((long)img * e.nchw_c + co) * e.nchw_h + y) * e.nchw_w + x;
-              if (e.nchw_u8)
-                reinterpret_cast<uint8_t*>(e.nchw_out)[o] = (uint8_t)(int)(fminf(fmaxf(v[co], 0.f), 1.f) * 255.f + 0.5f);
-              else
-                reinterpret_cast<float*>(e.nchw_out)[o] = v[co];
-            }
           }
         }
         if (p >= 0) {

@@ -179,7 +179,7 @@ struct TailGeom {
   int c;               // output channels (1 or 3)
   int h, w;            // crop
   int row_off;         // image row of stored row y is y + row_off
-  int u8;              // 1: uint8 output (clamped, rounded), 0: f32
+  int u8;              // 1: uint8 output, clamp(v, 0, 1) * 255 + 0.5 truncated (src/image.rs:60-63); 0: f32
   int strips, chunks;  // work units per image
 };
 constexpr int TAIL_COLS = 126, TAIL_ROWS = 32, TAIL_STAGES = 4, TAIL_NB = 4;

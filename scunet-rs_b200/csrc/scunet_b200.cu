@@ -215,7 +215,6 @@ cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
   SCB_GEMM_CASE(64, 64, GEO_UP2)
   SCB_GEMM_CASE(128, 64, GEO_UP2)
   SCB_GEMM_CASE(256, 64, GEO_UP2)
-  SCB_GEMM_CASE(16, 64, GEO_CONV3)
   SCB_GEMM_CASE(32, 32, GEO_CONV3)
   SCB_GEMM_CASE(64, 64, GEO_CONV3)
   SCB_GEMM_CASE(128, 64, GEO_CONV3)
@@ -238,7 +237,7 @@ bool tma_epi_supported(int geo, int bn, int bk) {
 bool gemm_supported(int geo, int bn, int bk) {
   static const int tab[][3] = {{32, 32, GEO_FLAT},   {32, 64, GEO_FLAT},   {64, 64, GEO_FLAT},   {96, 32, GEO_FLAT},
                                {128, 32, GEO_FLAT},  {128, 64, GEO_FLAT},  {192, 64, GEO_FLAT},  {256, 64, GEO_FLAT},
-                               {64, 64, GEO_UP2},    {128, 64, GEO_UP2},   {256, 64, GEO_UP2},   {32, 32, GEO_CONV3},   {16, 64, GEO_CONV3},
+                               {64, 64, GEO_UP2},    {128, 64, GEO_UP2},   {256, 64, GEO_UP2},   {32, 32, GEO_CONV3},
                                {64, 64, GEO_CONV3},  {128, 64, GEO_CONV3}, {256, 64, GEO_CONV3}, {128, 64, GEO_DOWN2},
                                {256, 64, GEO_DOWN2}};
   for (auto& r : tab)
@@ -437,8 +436,8 @@ struct Maker {
   }
 
   // After the epilogue pointers are set: pick the TMA epilogue when this op can use
-  // it (no LayerNorm pass, no pixel shuffle, no NCHW crop, a compiled variant) and
-  // build its stream maps and staging layout.
+  // it (a LayerNorm only on a flat GEMM, an up conv only with its 2-D tiles, a
+  // compiled variant) and build its stream maps and staging layout.
   bool finish_epi(GemmOp& op) {
     GemmEpi& e = op.e;
     e.st_res16 = e.st_res32 = e.st_skip = e.st_out16 = e.st_out32 = e.st_ln = -1;
@@ -456,7 +455,7 @@ struct Maker {
     }
     // the TMA epilogue's LayerNorm: flat GEMMs without activation, fp16 residual at most
     const bool ln_tma = !e.ln_out || (op.geo == GEO_FLAT && e.act == ACT_NONE && !e.res32 && !e.skip32);
-    if (!ln_tma || e.nchw_out || (op.geo == GEO_UP2 && op.g.TW == 0) || !tma_epi_supported(op.geo, op.bn, op.bk))
+    if (!ln_tma || (op.geo == GEO_UP2 && op.g.TW == 0) || !tma_epi_supported(op.geo, op.bn, op.bk))
       return true;
     const int N = op.g.n_total;
     int off = 0;
