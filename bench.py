@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Throughput of the SCUNet forward pass on B200, in megapixels per second.
 
-Workload: seeded 1920x1080 RGB uint8 frames (smooth field
+Workload (configuration 4 of the benchmark set): seeded 1920x1080 RGB uint8 frames (smooth field
 plus luma-dependent and 2x2-correlated noise), replicate-padded to 1920x1088 on the
 device, colour SCUNet with seeded weights. A step is one pass over `--frames`
 frames per GPU (batch sharding, no collective: weak scaling); frames go through
@@ -11,15 +11,16 @@ the library in micro-batches of `--micro` frames per `scb_forward_dev` call.
 
 One JSON line on rank 0. `value` is device-timed (CUDA events on the launch
 stream, max over ranks) with inputs resident in HBM; `e2e` is the same metric
-through the host-pointer C-ABI call `scb_forward_host` (pinned host uint8 in,
-float32 out, copies inside the timed region). `roofline` is the dominant op class
+through the host-pointer C-ABI call `scb_forward_host`, one call per step over the
+step's frames (pinned host uint8 in, float32 out, copies inside the timed region;
+the library overlaps them with the compute of the neighbouring micro-batches). `roofline` is the dominant op class
 from a live per-launch event profile (`scb_set_profiling` / `scb_profile_bytes`),
 against HBM or the tensor pipe by its arithmetic intensity, with the DRAM traffic
 ncu measured for it (`profiles/traffic.json`, written by `--ncu-traffic`). `cpu_baseline` times
 the CPU oracle port (`oracle/scunet_torch.py`, the reference's algorithm restated in
 torch float32, all host threads) on a bounded 512x512 crop.
 
-`--workload band` measures BASELINE.json config 5 instead: one seeded 8192x8192
+`--workload band` measures configuration 5 instead: one seeded 8192x8192
 RGB uint8 image split into 64-row-aligned row bands, one band per rank
 (`scb_band_init` + `scb_forward_band`; halo rows cross NVLink with NCCL send/recv
 inside the forward). A step is one forward of the whole image; the total work is
@@ -64,6 +65,8 @@ def args_():
     ap.add_argument("--frames", type=int, default=16, help="frames per GPU per step")
     ap.add_argument("--micro", type=int, default=4, help="frames per library call")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--residual32", action="store_true",
+                    help="keep the in-stage residual stream in fp32 (SCB_OPT_RESIDUAL32, the reference's precision)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-traffic", metavar="CSV",
                     help="write profiles/traffic.json from an ncu capture of one 1-frame forward and exit")
@@ -172,6 +175,14 @@ def reference_arm(a, rank, world):
         "cpu_baseline": {"value": value, "unit": "MP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "MP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def arith_label(be):
+    """The arithmetic the context's options give, for the bench line."""
+    scb = importlib.import_module("scunet-rs_b200")
+    r32 = be.options.get(scb.backend.SCB_OPT_RESIDUAL32, 0)
+    stream = "fp32 in-stage residual stream" if r32 else "fp16 in-stage residual stream"
+    return f"fp16 tensor-core operands, {stream}, fp32 accumulate and U-Net skips"
 
 
 KERNEL_OF_CLASS = {"attention": "window_attn_kernel", "trans_fused": "trans32_ws_kernel + trans64_ws_kernel",
@@ -329,6 +340,15 @@ class Job:
         if self.world > 1:
             self.dist.barrier()
 
+    def gather(self, v):
+        """[v of rank 0, v of rank 1, ...] on every rank."""
+        if self.world == 1:
+            return [v]
+        t = self.torch.zeros(self.world, dtype=self.torch.float64, device="cuda")
+        t[self.rank] = v
+        self.dist.all_reduce(t)
+        return [float(u) for u in t.cpu()]
+
     def max_over_ranks(self, v):
         if self.world == 1:
             return v
@@ -351,7 +371,9 @@ class Job:
         t1.record(stream)
         torch.cuda.synchronize()
         clocks = clk.stop()
-        ms = self.max_over_ranks(t0.elapsed_time(t1) / steps)
+        mine = t0.elapsed_time(t1) / steps
+        self.per_rank = self.gather(mine)
+        ms = max(self.per_rank)
         self.barrier()
         return ms, clocks
 
@@ -367,6 +389,8 @@ def frames_workload(a, job, scb):
     assert F % micro == 0, "--frames must be a multiple of --micro"
     wt = scb.Weights.seeded(3, 0)
     be = scb.B200(wt, device=local)
+    if a.residual32:
+        be.set_option(scb.backend.SCB_OPT_RESIDUAL32, 1)
     frames = scb.synth.frames(4000 + rank, F, H, W, distinct=min(F, 4))
     x_dev = torch.from_numpy(frames).cuda()
     y_dev = torch.empty((F, C, H, W), dtype=torch.float32, device="cuda")
@@ -387,6 +411,7 @@ def frames_workload(a, job, scb):
     torch.cuda.synchronize()
     launches_per_call = be.last_launch_count()
     ms, clocks = job.timed(step, a.steps, stream)
+    per_rank = [round(v, 3) for v in job.per_rank]
     mp_step = F * H * W * world / 1e6
     value = mp_step / (ms / 1e3)
 
@@ -403,12 +428,12 @@ def frames_workload(a, job, scb):
         hx = torch.from_numpy(frames).pin_memory()
         hy = torch.empty((F, C, H, W), dtype=torch.float32).pin_memory()
 
+        be.set_option(scb.backend.SCB_OPT_HOST_CHUNK, micro)
+
         def e2e_step():
-            for i in range(0, F, micro):
-                rc = be.lib.scb_forward_host(be.ctx, hx[i].data_ptr(), scb.SCB_U8, micro, C, H, W, hy[i].data_ptr(),
-                                             scb.SCB_F32)
-                if rc:
-                    raise RuntimeError(be.lib.scb_last_error(be.ctx).decode())
+            rc = be.lib.scb_forward_host(be.ctx, hx.data_ptr(), scb.SCB_U8, F, C, H, W, hy.data_ptr(), scb.SCB_F32)
+            if rc:
+                raise RuntimeError(be.lib.scb_last_error(be.ctx).decode())
 
         e2e_step()
         job.barrier()
@@ -418,7 +443,10 @@ def frames_workload(a, job, scb):
         dt = (time.perf_counter() - t) / a.steps
         dt = job.max_over_ranks(dt)
         e2e = {"value": mp_step / dt, "unit": "MP/s", "h2d_bytes_per_step": int(hx.numel()) * world,
-               "d2h_bytes_per_step": int(hy.numel() * 4) * world, "api": "scb_forward_host (pinned host buffers)"}
+               "d2h_bytes_per_step": int(hy.numel() * 4) * world,
+               "api": f"scb_forward_host, one call of {F} frames per step (pinned host buffers; {micro}-frame "
+                      f"compute chunks, copies of the neighbouring chunks overlapped)",
+               "timing": "host wall clock around the synchronous calls, max over ranks"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -438,8 +466,9 @@ def frames_workload(a, job, scb):
                        "parallelism": f"dp{world} (batch sharding, no collective)",
                        "l2": "inputs larger than L2 (each step streams %.1f GB of activations)" % (
                            scb.need_bytes(micro, 3, 1088, 1920) / 1e9),
-                       "arith": "fp16 tensor-core operands, fp32 accumulate and residual stream"},
-            "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_call * (F // micro) * a.steps,
+                       "arith": arith_label(be)},
+            "clocks": clocks, "per_rank_ms": per_rank, "slowest_rank": int(np.argmax(per_rank)),
+            "e2e": e2e, "gpu_launches": launches_per_call * (F // micro) * a.steps,
             "roofline": roofline, "cpu_baseline": cpu,
         }), flush=True)
     be.close()
@@ -479,6 +508,7 @@ def band_workload(a, job, scb):
     torch.cuda.synchronize()
     launches_per_call = be.last_launch_count()
     ms, clocks = job.timed(step, a.steps, stream)
+    per_rank = [round(v, 3) for v in job.per_rank]
     mp_step = S * S / 1e6
     value = mp_step / (ms / 1e3)
 
@@ -526,8 +556,9 @@ def band_workload(a, job, scb):
                        "parallelism": f"row bands over {world} GPU(s), halo rows by NCCL send/recv",
                        "l2": "inputs larger than L2 (one forward streams %.0f GB of activations)" % (
                            scb.need_bytes(1, 3, hp, hp) / 1e9),
-                       "arith": "fp16 tensor-core operands, fp32 accumulate and residual stream"},
-            "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_call * a.steps,
+                       "arith": arith_label(be)},
+            "clocks": clocks, "per_rank_ms": per_rank, "slowest_rank": int(np.argmax(per_rank)),
+            "e2e": e2e, "gpu_launches": launches_per_call * a.steps,
             "roofline": roofline, "cpu_baseline": None,
         }), flush=True)
     be.close()

@@ -16,9 +16,11 @@
  *    is used by one host thread at a time (the reference serialises on a mutex,
  *    tests/device_lock.rs:7-14). Independent contexts on different devices run
  *    concurrently (batch sharding: one context per GPU).
- *  - Images are NCHW float32 in [0,1] (or uint8 where stated); the network's
- *    arithmetic is fp16 tensor-core operands with fp32 accumulation and an fp32
- *    residual stream.
+ *  - Images are NCHW float32 in [0,1] (or uint8 where stated). The network's
+ *    arithmetic is fp16 tensor-core operands with fp32 accumulation; the four
+ *    U-Net skips are stored in fp32 and every other intermediate, including by
+ *    default the residual stream inside a stage, in fp16 (SCB_OPT_RESIDUAL32 keeps
+ *    that stream in fp32, the reference's precision).
  */
 #ifndef SCUNET_B200_H
 #define SCUNET_B200_H
@@ -79,13 +81,14 @@ int scb_forward_dev(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int 
  * request fail or stall on cudaMalloc (which can fail under fragmentation and
  * synchronises the device), or a host whose own allocator owns the GPU's memory.
  * This entry point has no counterpart in the reference. It allocates nothing:
- * its scratch is a 14 MiB array inside the library's device image, which every
- * GPU that loads the library holds until the process exits. Limit: the padded
- * batch (n * ceil(h/64)*64 * ceil(w/64)*64) may hold at most 8192 pixels, e.g.
- * one 64x128 or two 64x64 images; larger requests fail with SCB_EINVAL and a
- * message. The first call on a context's device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream
- * capture. Every call, from every context on a device, shares the one array and
+ * its scratch is a 14 MiB array inside the library's device image. scb_create
+ * reserves it: it looks the array's device address up (cudaGetSymbolAddress),
+ * which loads the library's device code on that GPU together with the array, so
+ * a later call here loads and allocates nothing; the GPU then holds the 14 MiB
+ * until the process exits (scb_mem_report's `fixed`). Limit: the padded batch
+ * (n * ceil(h/64)*64 * ceil(w/64)*64) may hold at most 8192 pixels, e.g. one
+ * 64x128 or two 64x64 images; larger requests fail with SCB_EINVAL and a
+ * message. Every call, from every context on a device, shares the one array and
  * overwrites it (nothing in it needs to start at zero), so calls whose GPU work
  * overlaps race: run them on one stream or order them with events. Same inputs,
  * outputs and asynchrony as scb_forward_dev; the context's weights must already
@@ -94,10 +97,14 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
                             int y_dtype, void* stream);
 
 /* Same as scb_forward_dev with host pointers: copies in, runs, copies out,
- * synchronises (the end-to-end call a host application makes). */
+ * synchronises (the end-to-end call a host application makes). The batch runs as
+ * a pipeline of chunks of images (SCB_OPT_HOST_CHUNK images each; by default as
+ * many as make up four 1920x1088 frames): while chunk k computes, chunk k + 1 is
+ * copied in and chunk k - 1 out on two copy streams, so with pinned host buffers
+ * the copies hide behind the compute. */
 int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype);
 
-/* ---- one large image split into row bands ----
+/* ---- one large image split into row bands (an image too large to run whole) ----
  * The padded image's 64-row blocks are divided into contiguous row bands. Each band
  * runs the whole network on its rows, stored with 4 halo rows above and below at
  * every level; after every block's conv1_1 (and before the tail conv) the bands
@@ -124,12 +131,32 @@ int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks);
 int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int w, void* y, int y_dtype,
                      void* stream);
 
+/* Wait for a banded forward on `stream` (NULL = the context's own) with a deadline.
+ * NCCL's send/recv kernels wait for the peer without a bound, so a rank whose peer
+ * died would otherwise hang in cudaStreamSynchronize. This polls the stream and the
+ * band group's asynchronous NCCL error every 0.2 ms; when a peer fails or
+ * `timeout_ms` passes it aborts the group (ncclCommAbort, which stops this GPU's
+ * NCCL kernels) and returns SCB_ECUDA; the next banded forward then needs a new
+ * scb_band_init. No counterpart in the reference (single GPU). */
+int scb_band_sync(scb_ctx* ctx, void* stream, int timeout_ms);
+
 /* Device bytes a forward of n images of hp x wp needs beyond the weights
- * (`memguard::device_need`, src/memguard.rs:66-74). Pure arithmetic. */
+ * (`memguard::device_need`, src/memguard.rs:66-74). Pure arithmetic, for the
+ * default options (SCB_OPT_FUSE_TRANS on, SCB_OPT_RESIDUAL32 off); a context whose
+ * options differ allocates what its own options need. */
 int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes);
 
-/* `Backend::footprint` (src/backend.rs:27-31): device bytes held now. */
+/* `Backend::footprint` (src/backend.rs:27-31): device bytes held now - the weights,
+ * and the scratch arenas scb_release_scratch frees. The fixed no-allocation array
+ * is not scratch in that sense (nothing frees it); scb_mem_report gives it. */
 void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_bytes);
+
+/* `Backend::mem_report` (src/backend.rs:33-44; `Cuda::mem_report`,
+ * src/cuda.rs:395-424) as numbers: the most device memory the context has held at
+ * once (weights + scratch arenas; the number that decides whether a size fits),
+ * what it holds now, and the fixed 14 MiB no-allocation array its GPU holds since
+ * scb_create. Any pointer may be NULL. */
+int scb_mem_report(const scb_ctx* ctx, size_t* high_water, size_t* live, size_t* fixed);
 
 /* `Backend::release_scratch` (src/backend.rs:46-55): drop the arena. */
 void scb_release_scratch(scb_ctx* ctx);
@@ -182,6 +209,21 @@ int scb_probe_mlp(scb_ctx* ctx, int stage, int index, const void* a16, void* z16
  * (odd = SW), as the reference walker does (src/cuda.rs:1702, 1775, 1811-1817). */
 int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n, int H, int W, float* y32);
 
+/* m_head alone: x [n][c][h][w] (x_dtype SCB_U8 or SCB_F32, device) -> the replicate-
+ * padded 3x3 conv c -> 64 as x1_32 float32 and x1_16 fp16, both [n][hp][wp][64]
+ * (NHWC, hp and wp the multiples of 64 above h and w). */
+int scb_probe_head(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, float* x1_32, void* x1_16);
+
+/* m_tail alone: s16 fp16 [n][hp][wp][64] -> the 3x3 conv 64 -> c cropped to h x w,
+ * y [n][c][h][w] as float32 or uint8 (quantised as scb_forward_dev does). */
+int scb_probe_tail(scb_ctx* ctx, const void* s16, int n, int c, int h, int w, void* y, int y_dtype);
+
+/* The failure path of every kernel's bounded waits, on purpose and without a fault:
+ * one warp waits up to `limit_us` (1 .. 1e6) on an mbarrier nothing completes, gives
+ * up, records the failure in the device error word and returns; this returns
+ * SCB_EDEVICE with the message the forwards give, and the context stays usable. */
+int scb_probe_wait_timeout(scb_ctx* ctx, int limit_us);
+
 /* Number of kernel launches the last forward issued (for launch accounting). */
 int scb_last_launch_count(const scb_ctx* ctx);
 
@@ -195,7 +237,9 @@ int scb_last_launch_count(const scb_ctx* ctx);
  * either way). Measured cost of fp16: max |diff| vs the FP32 reference 1.0e-3 ->
  * 1.2e-3 at 256x256, inside the 2e-3 acceptance bar; it saves 6 of the 16 bytes per
  * channel a block moves through its 1x1 convs. */
-enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2 };
+/* SCB_OPT_HOST_CHUNK (default 0 = automatic): images per compute call of
+ * scb_forward_host's pipeline. */
+enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3 };
 int scb_set_option(scb_ctx* ctx, int option, int value);
 
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,
@@ -214,6 +258,13 @@ int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max)
  * result written once, weights included), the numerator of a memory roofline. No
  * counterpart in the reference, whose profile reports times only. */
 int scb_profile_bytes(const scb_ctx* ctx, double* bytes, int max);
+
+/* `Backend::profile_report` (src/backend.rs:33-38; `Cuda::profile_report`,
+ * src/cuda.rs:1875-1886): the last profiled forward's device time per op class,
+ * most expensive first, as text (one line per class: ms, share, launches, achieved
+ * TFLOP/s, class). Writes at most cap - 1 bytes and a NUL into buf (buf may be NULL
+ * to size it); returns the full length. Empty when profiling is off. */
+int scb_profile_report(scb_ctx* ctx, char* buf, size_t cap);
 
 #ifdef __cplusplus
 }

@@ -30,9 +30,12 @@ SYMBOLS = [
     "scb_probe_down2", "scb_probe_up2", "scb_probe_attention", "scb_probe_block", "scb_last_launch_count",
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
     "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes", "scb_probe_mlp",
+    "scb_band_sync", "scb_probe_head", "scb_probe_tail", "scb_probe_wait_timeout", "scb_mem_report",
+    "scb_profile_report",
 ]
 SCB_OPT_FUSE_TRANS = 1
 SCB_OPT_RESIDUAL32 = 2
+SCB_OPT_HOST_CHUNK = 3
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
               "trans_fused", "halo", "mlp"]
 
@@ -71,6 +74,12 @@ def load_library(path=None):
     lib.scb_band_init.argtypes = [vp, vp, i, i]
     lib.scb_forward_band.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
     lib.scb_profile_bytes.argtypes = [vp, ctypes.POINTER(ctypes.c_double), i]
+    lib.scb_band_sync.argtypes = [vp, vp, i]
+    lib.scb_probe_head.argtypes = [vp, vp, i, i, i, i, i, vp, vp]
+    lib.scb_probe_tail.argtypes = [vp, vp, i, i, i, i, vp, i]
+    lib.scb_probe_wait_timeout.argtypes = [vp, i]
+    lib.scb_mem_report.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(sz)]
+    lib.scb_profile_report.argtypes = [vp, ctypes.c_char_p, sz]
     lib.scb_probe_mlp.argtypes = [vp, i, i, vp, vp, i]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
@@ -144,6 +153,7 @@ class B200:
             raise BackendError(f"scb_create: {self.lib.scb_last_error(None).decode()}")
         self.ctx = ctx
         self._keep = None  # weights are on the device now
+        self.options = {}  # the SCB_OPT_* values set on this context
 
     # -- the trait ------------------------------------------------------------
     def name(self):
@@ -169,6 +179,24 @@ class B200:
 
     def release_scratch(self):
         self.lib.scb_release_scratch(self.ctx)
+
+    def mem_report(self):
+        """`Backend::mem_report` (`src/backend.rs:33-44`) as numbers: {high_water, live,
+        fixed} device bytes (fixed = the no-allocation array, held since creation)."""
+        hw, live, fixed = ctypes.c_size_t(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
+        self._check(self.lib.scb_mem_report(self.ctx, ctypes.byref(hw), ctypes.byref(live), ctypes.byref(fixed)),
+                    "scb_mem_report")
+        return {"high_water": hw.value, "live": live.value, "fixed": fixed.value}
+
+    def profile_report(self):
+        """`Backend::profile_report` (`src/backend.rs:33-38`): the last profiled
+        forward's device time per op class as text ("" when profiling is off)."""
+        n = self.lib.scb_profile_report(self.ctx, None, 0)
+        if n <= 0:
+            return ""
+        buf = ctypes.create_string_buffer(n + 1)
+        self.lib.scb_profile_report(self.ctx, buf, n + 1)
+        return buf.value.decode()
 
     # -- batched paths ----------------------------------------------------------
     def forward_host(self, x, out_u8=False):
@@ -212,8 +240,14 @@ class B200:
         self._check(self.lib.scb_forward_band(self.ctx, x_ptr, x_dtype, c, h, w, y_ptr, y_dtype, stream or None),
                     "scb_forward_band")
 
+    def band_sync(self, timeout_ms, stream=0):
+        """Wait for the banded forward on `stream` with a deadline; a failed peer or
+        the deadline aborts the band group and raises."""
+        self._check(self.lib.scb_band_sync(self.ctx, stream or None, int(timeout_ms)), "scb_band_sync")
+
     def set_option(self, option, value):
         self._check(self.lib.scb_set_option(self.ctx, option, int(value)), "scb_set_option")
+        self.options[option] = int(value)
 
     def set_profiling(self, on):
         self._check(self.lib.scb_set_profiling(self.ctx, int(bool(on))), "scb_set_profiling")

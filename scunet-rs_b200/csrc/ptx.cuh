@@ -23,6 +23,7 @@ enum : unsigned {
   SCB_ERR_WAIT_ACC = 3,    // epilogue waited for an accumulator never committed
   SCB_ERR_WAIT_ACC_FREE = 4,
   SCB_ERR_WAIT_ATTN = 5,
+  SCB_ERR_WAIT_PROBE = 6,  // scb_probe_wait_timeout: a wait nothing completes, by design
 };
 
 __device__ __forceinline__ void record_error(unsigned code) {
@@ -86,20 +87,25 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for phase `parity` of `bar` to complete; false (and the error word set to
-// `code`) after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+// `code`) after `limit_ns` of %globaltimer.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, unsigned code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 255u) {
-      if (globaltimer() - t0 > 1000000000ull) {
+      if (globaltimer() - t0 > limit_ns) {
         record_error(code);
         return false;
       }
       __nanosleep(64);
     }
   }
+}
+
+// The kernels' waits: ~1 s, far beyond any legitimate stall.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  return mbar_wait_limit(bar, parity, code, 1000000000ull);
 }
 
 // ---------------------------------------------------------------------------

@@ -24,12 +24,14 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <ctime>
 #include <map>
 #include <string>
 #include <vector>
 
 #include "../../include/scunet_b200.h"
 #include "attn.cuh"
+#include "host_logic.h"
 #include "gemm.cuh"
 #include "io_kernels.cuh"
 #include "trans.cuh"
@@ -40,13 +42,17 @@
 using namespace scb;
 
 // Scratch for scb_forward_dev_noalloc, for callers that cannot allocate device
-// memory at call time. It is a fixed array in the library's device image: every
-// GPU that loads the library holds these 14 MiB until the process exits. Its size
-// covers the scratch plan of any batch whose padded pixels (n * hp * wp) total at
-// most kNoAllocMaxPixels (1704 bytes per padded pixel plus 1 KiB alignment per
-// buffer). Host code only ever takes its address with cudaGetSymbolAddress.
+// memory at call time. It is a fixed array in the library's device image: the
+// device code is loaded (and these 14 MiB reserved) on a GPU when scb_create looks
+// the array up, and the GPU holds it until the process exits. Its size covers the
+// scratch plan of any batch whose padded pixels (n * hp * wp) total at most
+// kNoAllocMaxPixels (1704 bytes per padded pixel plus 1 KiB alignment per buffer).
+// Host code only ever takes its address with cudaGetSymbolAddress.
 static constexpr long kNoAllocMaxPixels = 8192;
 static constexpr size_t kNoAllocBytes = 14u << 20;
+// scb_forward_host: padded pixels per compute call when SCB_OPT_HOST_CHUNK is 0
+// (four 1920x1088 frames).
+static constexpr long kHostChunkPixels = 4L * 1088 * 1920;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 namespace {
@@ -188,39 +194,19 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   if (op.bn == BN && op.bk == BK && op.geo == GEO && op.tma_epi)                       \
     return launch_t<BN, BK, GEO, true>(op, sms, st);
 
+// Every compiled GEMM variant: T = with the TMA epilogue, D = direct epilogue.
+#define SCB_GEMM_VARIANTS(T, D)                                                                              \
+  T(64, 64, GEO_FLAT) T(128, 64, GEO_FLAT) T(192, 64, GEO_FLAT) T(256, 64, GEO_FLAT) T(128, 32, GEO_FLAT)   \
+  T(32, 32, GEO_CONV3X) T(32, 32, GEO_CONV3W) T(64, 64, GEO_CONV3X) T(128, 64, GEO_CONV3X)                  \
+  T(256, 64, GEO_CONV3) T(128, 64, GEO_DOWN2) T(256, 64, GEO_DOWN2) T(64, 64, GEO_UP2) T(128, 64, GEO_UP2)  \
+  T(256, 64, GEO_UP2)                                                                                       \
+  D(32, 32, GEO_FLAT) D(32, 64, GEO_FLAT) D(64, 64, GEO_FLAT) D(96, 32, GEO_FLAT) D(128, 32, GEO_FLAT)      \
+  D(128, 64, GEO_FLAT) D(192, 64, GEO_FLAT) D(256, 64, GEO_FLAT) D(64, 64, GEO_UP2) D(128, 64, GEO_UP2)     \
+  D(256, 64, GEO_UP2) D(32, 32, GEO_CONV3) D(64, 64, GEO_CONV3) D(128, 64, GEO_CONV3) D(256, 64, GEO_CONV3) \
+  D(128, 64, GEO_DOWN2) D(256, 64, GEO_DOWN2)
+
 cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
-  SCB_GEMM_TCASE(64, 64, GEO_FLAT)
-  SCB_GEMM_TCASE(128, 64, GEO_FLAT)
-  SCB_GEMM_TCASE(192, 64, GEO_FLAT)
-  SCB_GEMM_TCASE(256, 64, GEO_FLAT)
-  SCB_GEMM_TCASE(128, 32, GEO_FLAT)
-  SCB_GEMM_TCASE(32, 32, GEO_CONV3X)
-  SCB_GEMM_TCASE(32, 32, GEO_CONV3W)
-  SCB_GEMM_TCASE(64, 64, GEO_CONV3X)
-  SCB_GEMM_TCASE(128, 64, GEO_CONV3X)
-  SCB_GEMM_TCASE(256, 64, GEO_CONV3)
-  SCB_GEMM_TCASE(128, 64, GEO_DOWN2)
-  SCB_GEMM_TCASE(256, 64, GEO_DOWN2)
-  SCB_GEMM_TCASE(64, 64, GEO_UP2)
-  SCB_GEMM_TCASE(128, 64, GEO_UP2)
-  SCB_GEMM_TCASE(256, 64, GEO_UP2)
-  SCB_GEMM_CASE(32, 32, GEO_FLAT)
-  SCB_GEMM_CASE(32, 64, GEO_FLAT)
-  SCB_GEMM_CASE(64, 64, GEO_FLAT)
-  SCB_GEMM_CASE(96, 32, GEO_FLAT)
-  SCB_GEMM_CASE(128, 32, GEO_FLAT)
-  SCB_GEMM_CASE(128, 64, GEO_FLAT)
-  SCB_GEMM_CASE(192, 64, GEO_FLAT)
-  SCB_GEMM_CASE(256, 64, GEO_FLAT)
-  SCB_GEMM_CASE(64, 64, GEO_UP2)
-  SCB_GEMM_CASE(128, 64, GEO_UP2)
-  SCB_GEMM_CASE(256, 64, GEO_UP2)
-  SCB_GEMM_CASE(32, 32, GEO_CONV3)
-  SCB_GEMM_CASE(64, 64, GEO_CONV3)
-  SCB_GEMM_CASE(128, 64, GEO_CONV3)
-  SCB_GEMM_CASE(256, 64, GEO_CONV3)
-  SCB_GEMM_CASE(128, 64, GEO_DOWN2)
-  SCB_GEMM_CASE(256, 64, GEO_DOWN2)
+  SCB_GEMM_VARIANTS(SCB_GEMM_TCASE, SCB_GEMM_CASE)
   return cudaErrorInvalidConfiguration;
 }
 
@@ -617,8 +603,6 @@ struct Arena {
   float* xw = nullptr;
   __half *y = nullptr, *yt = nullptr;  // conv1_1 output: conv half, trans half (two planes)
   __half *hc = nullptr, *z = nullptr, *a = nullptr, *o = nullptr, *qh = nullptr;
-  float* io_in = nullptr;  // staging for host-pointer forwards
-  float* io_out = nullptr;
   std::vector<Op> ops;     // head .. tail
 };
 
@@ -658,7 +642,6 @@ size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band
   size_t o_xw = take(opt.residual32 ? wmax * 256 : 0), o_y = take(wmax * 64), o_yt = take(wmax * 64),
          o_hc = take(wmax * 64),
          o_z = take(wmax * 128), o_a = take(umax * 64), o_o = take(umax * 64), o_qh = take(umax * 256);
-  size_t o_in = take(px[0] * in_nc * 4), o_out = take(px[0] * in_nc * 4);
   if (A) {
     char* b = A->base;
     for (int s = 0; s < 4; ++s) {
@@ -673,8 +656,6 @@ size_t arena_layout(int n, int in_nc, int hp, int wp, Arena* A, const Band* band
     A->a = reinterpret_cast<__half*>(b + o_a);
     A->o = reinterpret_cast<__half*>(b + o_o);
     A->qh = reinterpret_cast<__half*>(b + o_qh);
-    A->io_in = reinterpret_cast<float*>(b + o_in);
-    A->io_out = reinterpret_cast<float*>(b + o_out);
   }
   return off;
 }
@@ -735,9 +716,22 @@ struct scb_ctx {
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
   bool residual32 = false; // SCB_OPT_RESIDUAL32
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
-  // context's device (looked up on the first call) and the plan laid out in it.
+  // context's device (looked up by scb_create, which loads the device code and
+  // with it the array) and the plan laid out in it.
   void* noalloc_base = nullptr;
   Arena noalloc;
+  // device bytes this context has held: weights + scratch arenas now, and the
+  // most it held at once (`Cuda::mem_report`'s high-water, src/cuda.rs:395-424)
+  size_t high_water = 0;
+  // scb_forward_host: a copy stream each way, two staging slots each way
+  // ([in0 | in1 | out0 | out1], `io_slot` bytes each) and the events that order
+  // them against the compute stream; images per compute call (SCB_OPT_HOST_CHUNK,
+  // 0 = as many as fit kHostChunkPixels)
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  char* io = nullptr;
+  size_t io_bytes = 0, io_slot = 0;
+  cudaEvent_t ev_in[2] = {}, ev_comp[2] = {}, ev_out[2] = {};
+  int host_chunk = 0;
   // row bands (config 5): one band per rank over NCCL, or all bands of one image
   // on this GPU (virtual bands, in lockstep)
   ncclComm_t nccl = nullptr;
@@ -779,6 +773,17 @@ int cuda_fail(scb_ctx* ctx, cudaError_t e, const char* what) {
     cudaError_t _e = (x);                           \
     if (_e != cudaSuccess) return cuda_fail(ctx, _e, what); \
   } while (0)
+
+// Device bytes the context holds now (weights and every scratch arena it owns;
+// the fixed no-allocation array is reported on its own).
+size_t live_bytes(const scb_ctx* ctx) {
+  size_t s = ctx->wbytes + ctx->arena.bytes + ctx->band_arena.bytes + ctx->io_bytes;
+  for (const Arena& A : ctx->vbands) s += A.bytes;
+  return s;
+}
+
+// Record the high-water after an allocation.
+void note_mem(scb_ctx* ctx) { ctx->high_water = std::max(ctx->high_water, live_bytes(ctx)); }
 
 // Host-side weight table lookup with shape check.
 struct Table {
@@ -987,6 +992,9 @@ struct NcclApi {
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  // the band watchdog (scb_band_sync): a peer's failure, and tearing the group down
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
 };
 
 const NcclApi* nccl_api(std::string& err) {
@@ -1004,8 +1012,11 @@ const NcclApi* nccl_api(std::string& err) {
       api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
       api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
       api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+      api.CommGetAsyncError =
+          reinterpret_cast<decltype(api.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+      api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
       loaded = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.Send && api.Recv && api.GroupStart &&
-               api.GroupEnd && api.GetErrorString;
+               api.GroupEnd && api.GetErrorString && api.CommGetAsyncError && api.CommAbort;
     }
   }
   if (!loaded) {
@@ -1552,20 +1563,21 @@ int ensure_arena(scb_ctx* ctx, int n, int hp, int wp) {
     A.bytes = 0;
   }
   if (!A.base) {
+    // admission before allocating (`memguard::check_cuda`, src/memguard.rs:262-285):
+    // refuse what cannot fit; if free memory cannot be read, let cudaMalloc decide
     size_t free_b = 0, total_b = 0;
-    cudaMemGetInfo(&free_b, &total_b);
-    if (need > free_b) {
-      char buf[256];
-      snprintf(buf, sizeof buf, "%d x %dx%d needs %.2f GiB of device scratch, %.2f GiB free", n, hp, wp,
-               need / 1073741824.0, free_b / 1073741824.0);
-      return fail(ctx, SCB_ENOMEM, buf);
-    }
+    const bool query_ok = cudaMemGetInfo(&free_b, &total_b) == cudaSuccess;
+    if (!query_ok) cudaGetLastError();  // not sticky: clear it
+    if (admit_arena(need, query_ok, free_b) == Admit::refuse)
+      return fail(ctx, SCB_ENOMEM, admit_message(n, hp, wp, need, free_b));
     cudaError_t e = cudaMalloc(&A.base, need);
     if (e != cudaSuccess) {
       A.base = nullptr;
+      cudaGetLastError();
       return fail(ctx, SCB_ENOMEM, std::string("arena allocation refused: ") + cudaGetErrorString(e));
     }
     A.bytes = need;
+    note_mem(ctx);
   }
   A.n = n;
   A.hp = hp;
@@ -1637,9 +1649,11 @@ int ensure_band_arena(scb_ctx* ctx, Arena& A, const Band& band, int hp, int wp) 
     cudaError_t e = cudaMalloc(&A.base, need);
     if (e != cudaSuccess) {
       A.base = nullptr;
+      cudaGetLastError();
       return fail(ctx, SCB_ENOMEM, std::string("band arena allocation refused: ") + cudaGetErrorString(e));
     }
     A.bytes = need;
+    note_mem(ctx);
   }
   CKC(ctx, cudaMemset(A.base, 0, A.bytes), "band arena clear");
   CKC(ctx, cudaDeviceSynchronize(), "band arena clear");
@@ -1655,6 +1669,45 @@ int ensure_band_arena(scb_ctx* ctx, Arena& A, const Band& band, int hp, int wp) 
 void free_arena(Arena& A) {
   if (A.base) cudaFree(A.base);
   A = Arena{};
+}
+
+// One warp waits, with a limit of `limit_ns`, on an mbarrier that nothing ever
+// arrives on: the bounded wait runs out, records SCB_ERR_WAIT_PROBE in the device
+// error word and returns. It exercises the path every kernel takes when a
+// handshake is lost, without a fault: the kernel holds no TMEM and issues no copies.
+__global__ void wait_probe_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) mbar_wait_limit(&bar, 0, SCB_ERR_WAIT_PROBE, limit_ns);
+  __syncwarp();
+}
+
+// Load every kernel of the library on the current device now. With lazy module
+// loading (the CUDA 12 default) a kernel's code is otherwise uploaded, into newly
+// allocated device memory, at its first launch; scb_create calls this so that no
+// later call - scb_forward_dev_noalloc's first one included - loads or allocates
+// anything for code. Querying a kernel's attributes loads it.
+cudaError_t preload_kernels() {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaSuccess;
+#define SCB_PRELOAD_T(BN, BK, GEO) \
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, BK, GEO, true>);
+#define SCB_PRELOAD_D(BN, BK, GEO) \
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, BK, GEO, false>);
+  SCB_GEMM_VARIANTS(SCB_PRELOAD_T, SCB_PRELOAD_D)
+#undef SCB_PRELOAD_T
+#undef SCB_PRELOAD_D
+  const void* others[] = {(const void*)window_attn_kernel,     (const void*)trans32_ws_kernel,
+                          (const void*)trans64_ws_kernel,      (const void*)mlp_fused_kernel<128>,
+                          (const void*)mlp_fused_kernel<256>,  (const void*)head_tc_kernel,
+                          (const void*)tail_tc_kernel,         (const void*)wait_probe_kernel};
+  for (const void* f : others)
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
+  return e;
 }
 
 int check_device_error(scb_ctx* ctx) {
@@ -1859,6 +1912,13 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
   }
   cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device);
   e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking);
+  for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+    e = cudaEventCreateWithFlags(&ctx->ev_in[b], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_comp[b], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_out[b], cudaEventDisableTiming);
+  }
   if (e == cudaSuccess) e = cudaMalloc(&ctx->wblob, blob.host.size());
   if (e == cudaSuccess) e = cudaMemcpy(ctx->wblob, blob.host.data(), blob.host.size(), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
@@ -1867,6 +1927,17 @@ int scb_create(const scb_tensor* tensors, int n_tensors, int in_nc, int dim, int
     return fail(nullptr, SCB_ECUDA, m);
   }
   ctx->wbytes = blob.host.size();
+  note_mem(ctx);
+  // Load the device code on this GPU now, and with it the no-allocation scratch
+  // array, so that scb_forward_dev_noalloc never loads a module (or allocates) when
+  // it is called: looking up a __device__ symbol loads the module that holds it.
+  e = cudaGetSymbolAddress(&ctx->noalloc_base, g_noalloc_scratch);
+  if (e == cudaSuccess && ctx->noalloc_base) e = preload_kernels();
+  if (e != cudaSuccess || !ctx->noalloc_base) {
+    std::string m = std::string("loading the device code: ") + cudaGetErrorString(e);
+    scb_destroy(ctx);
+    return fail(nullptr, SCB_ECUDA, m);
+  }
   char* b = ctx->wblob;
   auto H16 = [&](size_t o) { return reinterpret_cast<__half*>(b + o); };
   auto F = [&](size_t o) { return reinterpret_cast<float*>(b + o); };
@@ -1924,12 +1995,7 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
     return fail(ctx, SCB_EINVAL, buf);
   }
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-  if (!ctx->noalloc_base) {
-    void* base = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
-    if (e != cudaSuccess || !base) return cuda_fail(ctx, e, "cudaGetSymbolAddress(no-allocation scratch)");
-    ctx->noalloc_base = base;
-  }
+  if (!ctx->noalloc_base) return fail(ctx, SCB_EINVAL, "the no-allocation scratch was not reserved by scb_create");
   Arena& A = ctx->noalloc;
   if (!(A.n == n && A.hp == hp && A.wp == wp && !A.ops.empty())) {
     const size_t need = arena_layout(n, ctx->in_nc, hp, wp, nullptr, nullptr, arena_opts(ctx));
@@ -1954,22 +2020,66 @@ int scb_forward_dev_noalloc(scb_ctx* ctx, const void* x, int x_dtype, int n, int
   return SCB_OK;
 }
 
+// The host-pointer forward runs the batch as a pipeline of chunks of images: the
+// copy in of chunk k + 1 and the copy out of chunk k - 1 (each on its own stream,
+// so both copy engines work) overlap the compute of chunk k. Two staging slots each
+// way; events keep a slot from being overwritten while a copy or the forward still
+// reads it.
+int forward_host_pipelined(scb_ctx* ctx, const char* x, int x_u8, int n, int c, int h, int w, char* y, int y_u8) {
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  const int chunk = std::min(n, ctx->host_chunk > 0 ? ctx->host_chunk
+                                                    : (int)std::max(1L, kHostChunkPixels / ((long)hp * wp)));
+  const size_t img_in = (size_t)c * h * w * (x_u8 ? 1 : 4), img_out = (size_t)c * h * w * (y_u8 ? 1 : 4);
+  const size_t slot = ((size_t)chunk * c * h * w * 4 + 1023) & ~size_t(1023);
+  if (ctx->io_bytes < 4 * slot) {
+    if (ctx->io) cudaFree(ctx->io);
+    ctx->io = nullptr;
+    ctx->io_bytes = 0;
+    if (cudaMalloc(&ctx->io, 4 * slot) != cudaSuccess) {
+      cudaGetLastError();
+      ctx->io = nullptr;
+      return fail(ctx, SCB_ENOMEM, "host staging allocation refused");
+    }
+    ctx->io_bytes = 4 * slot;
+    note_mem(ctx);
+  }
+  ctx->io_slot = slot;
+  cudaStream_t cs = ctx->stream;
+  for (int i0 = 0, k = 0; i0 < n; i0 += chunk, ++k) {
+    const int b = k & 1, m = std::min(chunk, n - i0);
+    int r = ensure_arena(ctx, m, hp, wp);
+    if (r) return r;
+    char* in = ctx->io + b * slot;
+    char* out = ctx->io + (2 + b) * slot;
+    if (k >= 2) CKC(ctx, cudaStreamWaitEvent(ctx->h2d, ctx->ev_comp[b], 0), "wait");  // chunk k-2 read `in`
+    CKC(ctx, cudaMemcpyAsync(in, x + i0 * img_in, m * img_in, cudaMemcpyHostToDevice, ctx->h2d), "H2D");
+    CKC(ctx, cudaEventRecord(ctx->ev_in[b], ctx->h2d), "event");
+    CKC(ctx, cudaStreamWaitEvent(cs, ctx->ev_in[b], 0), "wait");
+    if (k >= 2) CKC(ctx, cudaStreamWaitEvent(cs, ctx->ev_out[b], 0), "wait");  // chunk k-2's `out` copied
+    r = run_ops(ctx, ctx->arena, in, x_u8, out, y_u8, c, h, w, cs);
+    if (r) return r;
+    CKC(ctx, cudaEventRecord(ctx->ev_comp[b], cs), "event");
+    CKC(ctx, cudaStreamWaitEvent(ctx->d2h, ctx->ev_comp[b], 0), "wait");
+    CKC(ctx, cudaMemcpyAsync(y + i0 * img_out, out, m * img_out, cudaMemcpyDeviceToHost, ctx->d2h), "D2H");
+    CKC(ctx, cudaEventRecord(ctx->ev_out[b], ctx->d2h), "event");
+  }
+  return SCB_OK;
+}
+
 int scb_forward_host(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, void* y, int y_dtype) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
   if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
-  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-  int r = ensure_arena(ctx, n, hp, wp);
+  int r = forward_host_pipelined(ctx, static_cast<const char*>(x), x_dtype == SCB_U8, n, c, h, w,
+                                 static_cast<char*>(y), y_dtype == SCB_U8);
+  // whatever happened, nothing of this call may still be running when it returns
+  const cudaError_t e1 = cudaStreamSynchronize(ctx->h2d), e2 = cudaStreamSynchronize(ctx->stream),
+                    e3 = cudaStreamSynchronize(ctx->d2h);
   if (r) return r;
-  Arena& A = ctx->arena;
-  const size_t in_b = (size_t)n * c * h * w * (x_dtype == SCB_U8 ? 1 : 4);
-  const size_t out_b = (size_t)n * c * h * w * (y_dtype == SCB_U8 ? 1 : 4);
-  CKC(ctx, cudaMemcpyAsync(A.io_in, x, in_b, cudaMemcpyHostToDevice, ctx->stream), "H2D");
-  r = run_ops(ctx, A, A.io_in, x_dtype == SCB_U8, A.io_out, y_dtype == SCB_U8, c, h, w, ctx->stream);
-  if (r) return r;
-  CKC(ctx, cudaMemcpyAsync(y, A.io_out, out_b, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
-  CKC(ctx, cudaStreamSynchronize(ctx->stream), "forward");
+  CKC(ctx, e1, "copy in");
+  CKC(ctx, e2, "forward");
+  CKC(ctx, e3, "copy out");
   r = check_device_error(ctx);
   if (r) return r;
   ctx->err.clear();
@@ -2080,6 +2190,60 @@ int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int
   return SCB_OK;
 }
 
+int scb_band_sync(scb_ctx* ctx, void* stream, int timeout_ms) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (timeout_ms < 0) return fail(ctx, SCB_EINVAL, "timeout_ms must be >= 0");
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  std::string err;
+  const NcclApi* nc = ctx->nccl ? nccl_api(err) : nullptr;
+  cudaError_t serr = cudaSuccess;
+  ncclResult_t aerr = ncclSuccess;
+  auto query = [&]() {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return 0;
+    if (q == cudaErrorNotReady) return 1;
+    serr = q;
+    return -1;
+  };
+  auto async_err = [&]() {
+    if (!nc) return 0;
+    ncclResult_t a = ncclSuccess;
+    if (nc->CommGetAsyncError(ctx->nccl, &a) != ncclSuccess) a = ncclSystemError;
+    if (a == ncclInProgress) return 0;
+    aerr = a;
+    return a == ncclSuccess ? 0 : 1;
+  };
+  auto now = []() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + 1e-9 * ts.tv_nsec;
+  };
+  auto nap = []() {
+    timespec ts{0, 200000};  // 0.2 ms
+    nanosleep(&ts, nullptr);
+  };
+  const Watch w = watch_until(query, async_err, now, nap, timeout_ms / 1000.0);
+  if (w == Watch::done) {
+    const int r = check_device_error(ctx);
+    if (r) return r;
+    ctx->err.clear();
+    return SCB_OK;
+  }
+  if (w == Watch::stream_error) return cuda_fail(ctx, serr, "banded forward");
+  // a peer failed or the exchange did not finish in time: abort the group so that
+  // NCCL's kernels on this GPU stop waiting for the peer; the context needs a new
+  // scb_band_init before the next banded forward
+  std::string why = w == Watch::peer_error
+                        ? std::string("a band peer failed: ") + (nc ? nc->GetErrorString(aerr) : "?")
+                        : "the banded forward did not finish within " + std::to_string(timeout_ms) + " ms";
+  if (nc && ctx->nccl) {
+    nc->CommAbort(ctx->nccl);
+    ctx->nccl = nullptr;
+  }
+  return fail(ctx, SCB_ECUDA, why + "; the band group was aborted (call scb_band_init again)");
+}
+
 int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes) {
   if (!bytes || n <= 0 || hp <= 0 || wp <= 0 || hp % 64 || wp % 64 || (in_nc != 1 && in_nc != 3)) return SCB_EINVAL;
   *bytes = arena_layout(n, in_nc, hp, wp, nullptr);
@@ -2091,7 +2255,7 @@ void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_by
   if (scratch_bytes) {
     size_t s = 0;
     if (ctx) {
-      s = ctx->arena.bytes + ctx->band_arena.bytes;
+      s = ctx->arena.bytes + ctx->band_arena.bytes + ctx->io_bytes;
       for (const Arena& A : ctx->vbands) s += A.bytes;
     }
     *scratch_bytes = s;
@@ -2102,10 +2266,15 @@ void scb_release_scratch(scb_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->h2d) cudaStreamSynchronize(ctx->h2d);
+  if (ctx->d2h) cudaStreamSynchronize(ctx->d2h);
   free_arena(ctx->arena);
   free_arena(ctx->band_arena);
   for (Arena& A : ctx->vbands) free_arena(A);
   ctx->vbands.clear();
+  if (ctx->io) cudaFree(ctx->io);
+  ctx->io = nullptr;
+  ctx->io_bytes = 0;
 }
 
 int scb_set_option(scb_ctx* ctx, int option, int value) {
@@ -2118,6 +2287,11 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     ctx->noalloc.n = 0;
     ctx->band_arena.ops.clear();
     for (Arena& A : ctx->vbands) A.ops.clear();
+    return SCB_OK;
+  }
+  if (option == SCB_OPT_HOST_CHUNK) {
+    if (value < 0) return fail(ctx, SCB_EINVAL, "SCB_OPT_HOST_CHUNK must be >= 0");
+    ctx->host_chunk = value;
     return SCB_OK;
   }
   return fail(ctx, SCB_EINVAL, "unknown option " + std::to_string(option));
@@ -2167,8 +2341,13 @@ void scb_destroy(scb_ctx* ctx) {
     if (const NcclApi* nc = nccl_api(err)) nc->CommDestroy(ctx->nccl);
   }
   for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
+  for (int b = 0; b < 2; ++b)
+    for (cudaEvent_t ev : {ctx->ev_in[b], ctx->ev_comp[b], ctx->ev_out[b]})
+      if (ev) cudaEventDestroy(ev);
   if (ctx->wblob) cudaFree(ctx->wblob);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
+  if (ctx->d2h) cudaStreamDestroy(ctx->d2h);
   delete ctx;
 }
 
@@ -2344,6 +2523,112 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
   r = probe_finish(ctx, e);
   cudaFree(base);
   return r;
+}
+
+int scb_probe_head(scb_ctx* ctx, const void* x, int x_dtype, int n, int c, int h, int w, float* x1_32, void* x1_16) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!x || !x1_32 || !x1_16) return fail(ctx, SCB_EINVAL, "NULL pointer");
+  if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  const double P = (double)n * hp * wp;
+  Op head{};
+  std::string err;
+  const uint64_t d[2] = {64, (uint64_t)P}, s32[1] = {256}, s16[1] = {128};
+  const uint32_t b32[2] = {32, 128}, b16[2] = {64, 128};
+  if (!encode_map(&head.head_m32, x1_32, 2, d, s32, b32, 4, 128, err) ||
+      !encode_map(&head.head_m16, x1_16, 2, d, s16, b16, 2, 128, err))
+    return fail(ctx, SCB_EINVAL, err);
+  const HeadGeom g{n, c, h, w, hp, wp, x_dtype == SCB_U8, 0, hp};
+  return probe_finish(ctx, launch_head(ctx, x, g, head, ctx->stream));
+}
+
+int scb_probe_tail(scb_ctx* ctx, const void* s16, int n, int c, int h, int w, void* y, int y_dtype) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (!s16 || !y) return fail(ctx, SCB_EINVAL, "NULL pointer");
+  if (!geom_ok(ctx, n, c, h, w)) return SCB_EINVAL;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
+  Op tail{};
+  std::string err;
+  const uint64_t dims[4] = {64, (uint64_t)wp, (uint64_t)hp, (uint64_t)n};
+  const uint64_t str[3] = {64 * 2, (uint64_t)wp * 64 * 2, (uint64_t)hp * wp * 64 * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  if (!encode_map(&tail.tail_map, s16, 4, dims, str, box, 2, 128, err)) return fail(ctx, SCB_EINVAL, err);
+  TailGeom g{};
+  g.n = n;
+  g.H = hp;
+  g.W = wp;
+  g.row0 = 0;
+  g.rows_out = hp;
+  g.row_off = 0;
+  g.strips = (wp + TAIL_COLS - 1) / TAIL_COLS;
+  g.chunks = (hp + TAIL_ROWS - 1) / TAIL_ROWS;
+  g.c = c;
+  g.h = h;
+  g.w = w;
+  g.u8 = y_dtype == SCB_U8;
+  return probe_finish(ctx, launch_tail(ctx, y, g, tail, ctx->stream));
+}
+
+int scb_probe_wait_timeout(scb_ctx* ctx, int limit_us) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (limit_us < 1 || limit_us > 1000000) return fail(ctx, SCB_EINVAL, "limit_us must be 1 .. 1000000");
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  wait_probe_kernel<<<1, 32, 0, ctx->stream>>>(1000ull * (unsigned long long)limit_us);
+  return probe_finish(ctx, cudaGetLastError());
+}
+
+int scb_mem_report(const scb_ctx* ctx, size_t* high_water, size_t* live, size_t* fixed) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (high_water) *high_water = ctx->high_water;
+  if (live) *live = live_bytes(ctx);
+  if (fixed) *fixed = ctx->noalloc_base ? kNoAllocBytes : 0;
+  return SCB_OK;
+}
+
+int scb_profile_report(scb_ctx* ctx, char* buf, size_t cap) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  static const char* kClass[] = {"head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0",
+                                 "mlp2", "down", "up", "trans_fused", "halo", "mlp_fused"};
+  const int n = (int)ctx->prof_tags.size();
+  std::vector<int> tags(n);
+  std::vector<double> fl(n);
+  std::vector<float> ms(n);
+  const int got = ctx->profiling ? scb_profile_read(ctx, tags.data(), fl.data(), ms.data(), n) : 0;
+  // per class: launches, device ms, algorithmic FLOPs; most expensive first
+  struct Row { int launches = 0; double ms = 0, flops = 0; };
+  std::vector<Row> rows(14);
+  double total = 0;
+  for (int i = 0; i < got; ++i) {
+    if (tags[i] < 0 || tags[i] >= 14 || ms[i] < 0) continue;
+    rows[tags[i]].launches++;
+    rows[tags[i]].ms += ms[i];
+    rows[tags[i]].flops += fl[i];
+    total += ms[i];
+  }
+  std::vector<int> order;
+  for (int k = 0; k < 14; ++k)
+    if (rows[k].launches) order.push_back(k);
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return rows[a].ms > rows[b].ms; });
+  std::string out;
+  if (got > 0) {
+    char line[160];
+    snprintf(line, sizeof line, "  ---- device time per op class (total %.2f ms, %d launches) ----\n", total, got);
+    out += line;
+    for (int k : order) {
+      snprintf(line, sizeof line, "  %9.3f ms  %5.1f %%  %6d launches  %8.1f TFLOP/s  %s\n", rows[k].ms,
+               total > 0 ? 100.0 * rows[k].ms / total : 0.0, rows[k].launches,
+               rows[k].ms > 0 ? rows[k].flops / (rows[k].ms * 1e-3) / 1e12 : 0.0, kClass[k]);
+      out += line;
+    }
+  }
+  if (buf && cap) {
+    const size_t m = std::min(cap - 1, out.size());
+    memcpy(buf, out.data(), m);
+    buf[m] = 0;
+  }
+  return (int)out.size();
 }
 
 }  // extern "C"

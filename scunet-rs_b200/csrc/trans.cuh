@@ -1,5 +1,5 @@
 // Shared pieces of the fused transformer-half kernels (trans32ws.cuh for trans width
-// T = 32 at full resolution, trans64.cuh for T = 64 at half resolution). Each runs
+// T = 32 at full resolution, trans64ws.cuh for T = 64 at half resolution). Each runs
 // the whole transformer half of a ConvTransBlock on pairs of 8x8 windows (128
 // tokens, one UMMA M tile):
 //

@@ -113,6 +113,13 @@ def frames(seed, n, h=1080, w=1920, distinct=None):
     return np.stack([base[i % k] for i in range(n)])
 
 
+def frame_at(seed, k, h=1080, w=1920):
+    """Frame k of the config-4 batch with seed `seed`, generated on its own (its
+    random stream is seeded with (seed, k)), so a test can take any subset of the
+    256 frames without generating the ones before it."""
+    return frame(np.random.default_rng([seed, k]), h, w)
+
+
 CONFIGS = {
     1: dict(name="color 64x64", c=3, h=64, w=64, n=1, sigma=25.0 / 255.0),
     2: dict(name="color 512x512", c=3, h=512, w=512, n=1, sigma=15.0 / 255.0),

@@ -1,4 +1,5 @@
-"""One image in row bands against the whole-image forward.
+"""One image in row bands (the 8192x8192 configuration's split) against the
+whole-image forward.
 
 The banded schedule (halo rows, per-block boundary exchange, shifted windows that
 straddle band edges, the image-edge wrap handled by the global window mask) must
@@ -122,3 +123,61 @@ def test_two_gpu_bands_over_nccl(scb, be3):
     d = np.abs(got - want)
     print(f"2-GPU bands: max |bands - whole| {np.nanmax(d):.3e}")
     assert np.isfinite(got).all() and d.max() <= TOL
+
+
+def _full_size_worker(rank, nranks, uid, S, q):
+    """One rank of the 8192^2 check: the whole-image forward of the image on this
+    rank's own GPU, then this rank's band over NCCL, compared on the device."""
+    import importlib
+    import sys
+    import torch
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    scb = importlib.import_module("scunet-rs_b200")
+    torch.cuda.set_device(rank)
+    be = None
+    try:
+        be = scb.B200(scb.Weights.seeded(3, 0), device=rank)
+        x = scb.synth.noisy_image_device(1005, 3, S, S, 25 / 255, device="cuda")
+        whole = torch.empty((1, 3, S, S), dtype=torch.float32, device="cuda")
+        s = torch.cuda.Stream()
+        torch.cuda.synchronize()
+        be.forward_dev(x.data_ptr(), scb.SCB_U8, 1, 3, S, S, whole.data_ptr(), scb.SCB_F32, s.cuda_stream)
+        s.synchronize()
+        be.release_scratch()
+        be.band_init(uid, rank, nranks)
+        y = torch.full_like(whole, float("nan"))
+        be.forward_band(x.data_ptr(), scb.SCB_U8, 3, S, S, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
+        be.band_sync(600000, s.cuda_stream)
+        r0, rows = scb.shard.band_rows(S, rank, nranks)
+        band, ref = y[:, :, r0:r0 + rows], whole[:, :, r0:r0 + rows]
+        q.put((rank, bool(torch.isfinite(band).all()), float((band - ref).abs().max())))
+    except Exception as e:  # reported, not raised: the parent reads the queue
+        q.put((rank, False, repr(e)))
+    finally:
+        if be is not None:
+            be.close()
+
+
+def test_two_gpu_bands_at_8192(scb):
+    """Config 5 at its own size over two GPUs and NCCL: each rank's band of the
+    8192x8192 image equals the whole-image forward's rows (both ranks also run the
+    whole image on their own GPU, 78 GB of scratch, released before the bands)."""
+    torch = _torch()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    uid = scb.band_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_full_size_worker, args=(r, 2, uid, 8192, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=600) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for rank, finite, d in res:
+        print(f"8192^2, 2 GPUs, rank {rank}: max |band - whole| {d}")
+        assert finite and isinstance(d, float) and d <= TOL, (rank, finite, d)

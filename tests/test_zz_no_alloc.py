@@ -9,6 +9,11 @@ through the C ABI, on two different images and geometries inside that limit, and
 checks each output against the allocating entry point's output for the same
 input; then it checks that a request over the limit is refused with a message.
 
+A second test creates a fresh context and makes the no-allocation forward its
+first GPU work: the device's free memory must not change across that call (the
+context reserved the array and loaded the device code when it was created), and
+its output must match a later allocating forward.
+
 This file is named to be collected last, so a run that stops at the first
 failure has already run every other test.
 """
@@ -51,5 +56,38 @@ def test_noalloc_forward_matches_forward_dev(scb, weights3):
         rc = be.lib.scb_forward_dev_noalloc(be.ctx, xd.data_ptr(), scb.SCB_U8, 1, 3, 72, 100, yd.data_ptr(),
                                             scb.SCB_F32, sp)
         assert rc == -1 and "8192" in be.lib.scb_last_error(be.ctx).decode()
+    finally:
+        be.close()
+
+
+def test_noalloc_first_call_on_fresh_context_allocates_nothing(scb, weights3):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    be = scb.B200(weights3)
+    try:
+        n, h, w = 1, 64, 128
+        x = scb.synth.noisy_image(77, 3, h, w, 25 / 255)[None]
+        xd = torch.from_numpy(x).cuda()
+        y_na = torch.full((n, 3, h, w), float("nan"), dtype=torch.float32, device="cuda")
+        y_ref = torch.empty((n, 3, h, w), dtype=torch.float32, device="cuda")
+        stream = torch.cuda.Stream()
+        sp = stream.cuda_stream
+        torch.cuda.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        rc = be.lib.scb_forward_dev_noalloc(be.ctx, xd.data_ptr(), scb.SCB_U8, n, 3, h, w, y_na.data_ptr(),
+                                            scb.SCB_F32, sp)
+        assert rc == 0, be.lib.scb_last_error(be.ctx).decode()
+        stream.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        assert free1 == free0, f"the first no-allocation call changed free device memory by {free0 - free1} bytes"
+        assert be.footprint()[1] == 0 and be.mem_report()["fixed"] == 14 << 20
+        be.forward_dev(xd.data_ptr(), scb.SCB_U8, n, 3, h, w, y_ref.data_ptr(), scb.SCB_F32, sp)
+        stream.synchronize()
+        got, want = y_na.cpu().numpy(), y_ref.cpu().numpy()
+        assert np.isfinite(got).all()
+        d = float(np.abs(want - got).max())
+        print(f"fresh context: max |noalloc - forward_dev| = {d:.3e}")
+        assert d <= MAX_ABS
     finally:
         be.close()
