@@ -146,6 +146,14 @@ int scb_band_sync(scb_ctx* ctx, void* stream, int timeout_ms);
  * options differ allocates what its own options need. */
 int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes);
 
+/* `memguard::check_cuda` (src/memguard.rs:262-285) for this context: would a forward
+ * of n images of hp x wp (multiples of 64) fit now? *need = the scratch arena this
+ * context's options need; *avail = free device memory plus the arena the context
+ * holds (the next forward frees or reuses it). SCB_OK when it fits, SCB_ENOMEM with
+ * the message when it does not; fails open (SCB_OK, *avail = 0) when free memory
+ * cannot be read. The forwards apply the same test before they allocate. */
+int scb_check_admission(scb_ctx* ctx, int n, int hp, int wp, size_t* need, size_t* avail);
+
 /* `Backend::footprint` (src/backend.rs:27-31): device bytes held now - the weights,
  * and the scratch arenas scb_release_scratch frees. The fixed no-allocation array
  * is not scratch in that sense (nothing frees it); scb_mem_report gives it. */

@@ -31,7 +31,7 @@ SYMBOLS = [
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
     "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes", "scb_probe_mlp",
     "scb_band_sync", "scb_probe_head", "scb_probe_tail", "scb_probe_wait_timeout", "scb_mem_report",
-    "scb_profile_report",
+    "scb_profile_report", "scb_check_admission",
 ]
 SCB_OPT_FUSE_TRANS = 1
 SCB_OPT_RESIDUAL32 = 2
@@ -80,6 +80,7 @@ def load_library(path=None):
     lib.scb_probe_wait_timeout.argtypes = [vp, i]
     lib.scb_mem_report.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_profile_report.argtypes = [vp, ctypes.c_char_p, sz]
+    lib.scb_check_admission.argtypes = [vp, i, i, i, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_probe_mlp.argtypes = [vp, i, i, vp, vp, i]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
     lib.scb_footprint.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
@@ -294,16 +295,10 @@ def run(be, x, c, h, w, wt):
 
 
 def check_b200(be, p, n=1):
-    """`memguard::check_cuda` (`src/memguard.rs:262-285`): refuse before allocating
-    when the arena would not fit in free device memory; fail open when the free
-    figure cannot be read."""
-    need = need_bytes(n, be.in_nc, p.hp, p.wp)
-    try:
-        import torch
-        free, _ = torch.cuda.mem_get_info(be.device)
-    except Exception:
-        return
-    have_arena = be.footprint()[1]
-    if need > free + have_arena:
-        raise BackendError(f"{p.h}x{p.w} needs {need / 2**30:.2f} GiB of device scratch, "
-                           f"{(free + have_arena) / 2**30:.2f} GiB available")
+    """`memguard::check_cuda` (`src/memguard.rs:262-285`) through the library's own
+    admission (`scb_check_admission`): refuse before allocating when the arena would
+    not fit in free device memory; fail open when the free figure cannot be read."""
+    need, avail = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    rc = be.lib.scb_check_admission(be.ctx, n, p.hp, p.wp, ctypes.byref(need), ctypes.byref(avail))
+    if rc != 0:
+        raise BackendError(f"{p.h}x{p.w}: {be.lib.scb_last_error(be.ctx).decode()}")

@@ -2250,6 +2250,24 @@ int scb_need_bytes(int n, int in_nc, int hp, int wp, size_t* bytes) {
   return SCB_OK;
 }
 
+int scb_check_admission(scb_ctx* ctx, int n, int hp, int wp, size_t* need, size_t* avail) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  if (n <= 0 || hp <= 0 || wp <= 0 || hp % 64 || wp % 64) return fail(ctx, SCB_EINVAL, "geometry must be padded to 64");
+  const size_t nb = arena_layout(n, ctx->in_nc, hp, wp, nullptr, nullptr, arena_opts(ctx));
+  if (need) *need = nb;
+  if (avail) *avail = 0;
+  CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  size_t free_b = 0, total_b = 0;
+  const bool query_ok = cudaMemGetInfo(&free_b, &total_b) == cudaSuccess;
+  if (!query_ok) cudaGetLastError();
+  // the arena this context holds now is freed or reused by the next forward
+  const size_t have = free_b + ctx->arena.bytes;
+  if (avail) *avail = query_ok ? have : 0;
+  if (admit_arena(nb, query_ok, have) == Admit::refuse) return fail(ctx, SCB_ENOMEM, admit_message(n, hp, wp, nb, have));
+  ctx->err.clear();
+  return SCB_OK;
+}
+
 void scb_footprint(const scb_ctx* ctx, size_t* weights_bytes, size_t* scratch_bytes) {
   if (weights_bytes) *weights_bytes = ctx ? ctx->wbytes : 0;
   if (scratch_bytes) {

@@ -140,6 +140,12 @@ def test_admission_refuses_before_allocating(scb, be3):
     xd = torch.zeros((n, 3, h, w), dtype=torch.uint8, device="cuda")      # real buffers of the
     yd = torch.zeros((n, 3, h, w), dtype=torch.uint8, device="cuda")      # requested size
     be3.release_scratch()
+    import ctypes
+    need, avail = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert be3.lib.scb_check_admission(be3.ctx, 1, 64, 64, ctypes.byref(need), ctypes.byref(avail)) == 0
+    assert 0 < need.value < avail.value
+    rc = be3.lib.scb_check_admission(be3.ctx, n, h, w, ctypes.byref(need), ctypes.byref(avail))
+    assert rc == -4 and need.value == scb.need_bytes(n, 3, h, w) and need.value > avail.value
     rc = be3.lib.scb_forward_dev(be3.ctx, xd.data_ptr(), scb.SCB_U8, n, 3, h, w, yd.data_ptr(), scb.SCB_U8, None)
     msg = be3.lib.scb_last_error(be3.ctx).decode()
     assert rc == -4 and "needs" in msg and "GiB free" in msg, (rc, msg)
