@@ -16,7 +16,7 @@ step's frames (pinned host uint8 in, float32 out, copies inside the timed region
 the library overlaps them with the compute of the neighbouring micro-batches). `roofline` is the dominant op class
 from a live per-launch event profile (`scb_set_profiling` / `scb_profile_bytes`),
 against HBM or the tensor pipe by its arithmetic intensity, with the DRAM traffic
-ncu measured for it (`profiles/traffic.json`, written by `--ncu-traffic`). `cpu_baseline` times
+ncu measured for it (`profiles/traffic.json`, written by `--ncu-traffic-kernels`). `cpu_baseline` times
 the CPU oracle port (`oracle/scunet_torch.py`, the reference's algorithm restated in
 torch float32, all host threads) on a bounded 512x512 crop.
 
@@ -68,8 +68,8 @@ def args_():
     ap.add_argument("--residual32", action="store_true",
                     help="keep the in-stage residual stream in fp32 (SCB_OPT_RESIDUAL32, the reference's precision)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ncu-traffic", metavar="CSV",
-                    help="write profiles/traffic.json from an ncu capture of one 1-frame forward and exit")
+    ap.add_argument("--ncu-traffic-kernels", metavar="RAW_CSV:KERNEL:SKIP", nargs="+",
+                    help="write profiles/traffic.json from per-kernel ncu captures of a 1-frame forward and exit")
     ap.add_argument("--ncu-launches", metavar="CSV", help="print a per-kernel launch table of an ncu capture and exit")
     return ap.parse_args()
 
@@ -185,9 +185,6 @@ def arith_label(be):
     return f"fp16 tensor-core operands, {stream}, fp32 accumulate and U-Net skips"
 
 
-KERNEL_OF_CLASS = {"attention": "window_attn_kernel", "trans_fused": "trans32_ws_kernel + trans64_ws_kernel",
-                   "head": "head_tc_kernel"}
-
 
 def class_totals(prof):
     """{class: [flops, bytes, ms, launches]} over one profiled forward."""
@@ -201,17 +198,36 @@ def class_totals(prof):
     return cls
 
 
-def roofline_from_profile(prof, frames_per_call):
-    """The dominant op class of one profiled forward against its roofline: HBM when
-    its arithmetic intensity is below the ridge point of the measured peaks, the
-    tensor pipe otherwise. `achieved` = the class's algorithmic bytes (or FLOPs) per
-    launch / its average launch time; `traffic` = measured DRAM bytes per launch
-    (profiles/traffic.json, an ncu capture of a one-frame forward scaled to
-    `frames_per_call` frames)."""
+def kernel_totals(prof, kernels):
+    """{kernel: {flops, bytes, ms, launches, classes}} over one profiled forward."""
+    out = {}
+    for (cls, fl, nb, t), k in zip(prof, kernels):
+        if k.startswith("("):  # halo exchanges and memsets are not kernels of this library
+            continue
+        e = out.setdefault(k, {"flops": 0.0, "bytes": 0.0, "ms": 0.0, "launches": 0, "classes": set()})
+        e["flops"] += fl
+        e["bytes"] += nb
+        e["ms"] += t
+        e["launches"] += 1
+        e["classes"].add(cls)
+    return out
+
+
+def roofline_from_profile(prof, kernels):
+    """The dominant kernel (most device time) of one profiled forward against its
+    roofline: HBM when its arithmetic intensity is below the ridge point of the
+    measured peaks, the tensor pipe otherwise. `achieved` = the kernel's algorithmic
+    bytes (or FLOPs) per launch / its average launch time (CUDA events on the launch
+    stream). `traffic` = DRAM bytes per launch: the DRAM / algorithmic byte ratio ncu
+    measured on a few launches of the same kernel (profiles/traffic.json, per-kernel
+    captures of a one-frame forward) times this workload's algorithmic bytes per
+    launch."""
     cls = class_totals(prof)
     tot_ms = sum(v[2] for v in cls.values())
-    dom = max((k for k in cls if k != "halo"), key=lambda k: cls[k][2])
-    fl, nb, ms, n = cls[dom]
+    ks = kernel_totals(prof, kernels)
+    dom = max(ks, key=lambda k: ks[k]["ms"])
+    d = ks[dom]
+    fl, nb, ms, n = d["flops"], d["bytes"], d["ms"], d["launches"]
     pk, pk_kind = peaks()
     tflops = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
     hbm = float(pk["hbm_gbs"])
@@ -224,18 +240,20 @@ def roofline_from_profile(prof, frames_per_call):
     else:
         achieved, peak, unit, bound = fl / n / t_launch / 1e12, tflops, "TFLOP/s", "tensor"
         src = f"{pk_kind} bf16/fp16 dense sustained"
-    traffic = None
+    traffic, ratio = None, None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
-        d = json.loads(tf.read_text())
-        c = d.get("classes", {}).get(dom)
+        c = json.loads(tf.read_text()).get("kernels", {}).get(dom)
         if c:
-            traffic = c["dram_bytes"] / c["launches"] * frames_per_call / d.get("frames_per_call", 1)
+            ratio = c["dram_bytes"] / c["algorithmic_bytes"]
+            traffic = ratio * nb / n
     return {
-        "kernel": KERNEL_OF_CLASS.get(dom, f"gemm_tc_kernel [{dom}]"), "class": dom,
+        "kernel": dom, "classes": sorted(d["classes"]),
         "bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-        "peak_source": src, "traffic": traffic, "algorithmic_bytes_per_launch": nb / n,
-        "flops_per_launch": fl / n, "launches": n, "share_of_forward": ms / tot_ms,
+        "peak_source": src, "traffic": traffic, "traffic_over_algorithmic": ratio,
+        "algorithmic_bytes_per_launch": nb / n, "flops_per_launch": fl / n, "launches": n,
+        "share_of_forward": ms / tot_ms,
+        "kernels_ms_share": {k: round(v["ms"] / tot_ms, 4) for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
         "classes_ms_share": {k: round(v[2] / tot_ms, 4) for k, v in sorted(cls.items(), key=lambda kv: -kv[1][2])},
         "whole_forward_tflops": sum(v[0] for v in cls.values()) / (tot_ms / 1e3) / 1e12,
     }
@@ -272,13 +290,33 @@ def ncu_launch_summary(path):
     return "\n".join(out)
 
 
-def ncu_traffic(path):
-    """Align an ncu capture of one 1-frame forward (gpu__time_duration.sum,
-    dram__bytes_read.sum, dram__bytes_write.sum per launch) with a profiled forward of
-    the same configuration; write profiles/traffic.json; print the per-class table."""
+def read_ncu_raw(path):
+    """`ncu -i <rep> --page raw --csv` output -> [(kernel name, {metric: value})]."""
+    import csv
+    rows = list(csv.reader(l for l in Path(path).read_text().splitlines() if l.startswith('"')))
+    h = rows[0]
+    out = []
+    for r in rows[2:]:  # row 1 holds the units
+        m = {}
+        for k, v in zip(h, r):
+            try:
+                m[k] = float(v.replace(",", ""))
+            except ValueError:
+                m[k] = v
+        out.append((m.get("Kernel Name", "?"), m))
+    return out
+
+
+def ncu_traffic_kernels(specs):
+    """Per-kernel DRAM traffic from small ncu captures of a one-frame forward.
+
+    Each spec is RAW_CSV:KERNEL:SKIP - an `ncu -i ... --page raw --csv` export of a
+    capture of launches SKIP+1 .. SKIP+N of KERNEL (as scb_profile_kernels names it).
+    The captured launches are matched to the same occurrences of that kernel in a
+    profiled forward of the same configuration (their algorithmic bytes); writes
+    profiles/traffic.json and prints the table."""
     import torch
     scb = importlib.import_module("scunet-rs_b200")
-    ls = read_ncu_csv(path)
     be = scb.B200(scb.Weights.seeded(3, 0), device=0)
     fr = torch.from_numpy(scb.synth.frames(4000, 1, H, W)).cuda()
     y = torch.empty((1, C, H, W), dtype=torch.float32, device="cuda")
@@ -286,35 +324,36 @@ def ncu_traffic(path):
     be.set_profiling(True)
     be.forward_dev(fr.data_ptr(), scb.SCB_U8, 1, C, H, W, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
     torch.cuda.synchronize()
-    prof = be.profile()
+    prof, kern = be.profile(), be.profile_kernels()
     be.close()
-    mine = ("gemm_tc_kernel", "head_tc_kernel", "io_kernel", "mlp_fused_kernel", "trans32_ws_kernel", "trans64_ws_kernel",
-            "window_attn_kernel")
-    ls = [l for l in ls if any(k in l[0] for k in mine)]
-    if len(ls) < len(prof):
-        raise SystemExit(f"{len(ls)} captured launches of this library, {len(prof)} ops in a forward")
-    ls = ls[-len(prof):]  # the capture ends with a whole forward; earlier launches are dropped
-    cls = {}
-    for (name, m), (c, fl, nb, ms) in zip(ls, prof):
-        e = cls.setdefault(c, {"launches": 0, "dram_bytes": 0.0, "algorithmic_bytes": 0.0, "flops": 0.0,
-                               "ncu_ms": 0.0, "kernels": set()})
-        e["launches"] += 1
-        e["dram_bytes"] += m["dram__bytes_read.sum"] + m["dram__bytes_write.sum"]
-        e["algorithmic_bytes"] += nb
-        e["flops"] += fl
-        e["ncu_ms"] += m["gpu__time_duration.sum"] / 1e6
-        e["kernels"].add(name.split("(")[0].split("<")[0].replace("void ", ""))
-    for e in cls.values():
-        e["kernels"] = sorted(e["kernels"])
-    out = {"workload": "one 1920x1080 frame per call (padded 1920x1088), config-4 frame, seeded weights",
-           "frames_per_call": 1, "classes": cls}
-    (ROOT / "profiles" / "traffic.json").write_text(json.dumps(out, indent=1) + "\n")
-    lines = ["| class | launches | kernels | DRAM bytes / algorithmic | DRAM MB per launch | ncu ms (serialised) |",
+    out = {}
+    for spec in specs:
+        path, kname, skip = spec.rsplit(":", 2)
+        rows = read_ncu_raw(path)
+        occ = [i for i, k in enumerate(kern) if k == kname][int(skip):int(skip) + len(rows)]
+        if len(occ) != len(rows):
+            raise SystemExit(f"{path}: {len(rows)} captured launches, {len(occ)} matching ops of {kname}")
+        e = out.setdefault(kname, {"captured_launches": 0, "dram_bytes": 0.0, "algorithmic_bytes": 0.0,
+                                   "ncu_us": 0.0, "classes": set(), "source": []})
+        for (name, m), i in zip(rows, occ):
+            e["captured_launches"] += 1
+            e["dram_bytes"] += m["dram__bytes_read.sum"] + m["dram__bytes_write.sum"]
+            e["algorithmic_bytes"] += prof[i][2]
+            e["ncu_us"] += m["gpu__time_duration.sum"] / 1e3
+            e["classes"].add(prof[i][0])
+        e["source"].append(Path(path).name)
+    for e in out.values():
+        e["classes"] = sorted(e["classes"])
+    res = {"workload": "one 1920x1080 frame per call (padded 1920x1088), seeded config-4 frame and weights; "
+                       "DRAM bytes from per-kernel ncu captures of 1-3 launches each",
+           "kernels": out}
+    (ROOT / "profiles" / "traffic.json").write_text(json.dumps(res, indent=1) + "\n")
+    lines = ["| kernel | classes | captured launches | DRAM MB per launch | algorithmic MB per launch | DRAM / algorithmic |",
              "|---|---|---|---|---|---|"]
-    for c, e in sorted(cls.items(), key=lambda kv: -kv[1]["ncu_ms"]):
-        lines.append(f"| {c} | {e['launches']} | {', '.join(e['kernels'])} | "
-                     f"{e['dram_bytes'] / max(e['algorithmic_bytes'], 1):.2f} | "
-                     f"{e['dram_bytes'] / e['launches'] / 1e6:.1f} | {e['ncu_ms']:.3f} |")
+    for k, e in sorted(out.items(), key=lambda kv: -kv[1]["dram_bytes"] / kv[1]["captured_launches"]):
+        n = e["captured_launches"]
+        lines.append(f"| `{k}` | {', '.join(e['classes'])} | {n} | {e['dram_bytes'] / n / 1e6:.1f} | "
+                     f"{e['algorithmic_bytes'] / n / 1e6:.1f} | {e['dram_bytes'] / e['algorithmic_bytes']:.2f} |")
     print("\n".join(lines))
 
 
@@ -419,7 +458,7 @@ def frames_workload(a, job, scb):
     be.set_profiling(True)
     be.forward_dev(x_dev[0].data_ptr(), scb.SCB_U8, micro, C, H, W, y_dev[0].data_ptr(), scb.SCB_F32, sp)
     torch.cuda.synchronize()
-    roofline = roofline_from_profile(be.profile(), micro)
+    roofline = roofline_from_profile(be.profile(), be.profile_kernels())
     be.set_profiling(False)
 
     # ---- end to end through the host-pointer C ABI ----
@@ -516,8 +555,7 @@ def band_workload(a, job, scb):
     be.set_profiling(True)
     step()
     torch.cuda.synchronize()
-    roofline = roofline_from_profile(be.profile(), 1)
-    roofline["traffic"] = None  # traffic.json is a frame capture, not a band
+    roofline = roofline_from_profile(be.profile(), be.profile_kernels())
     be.set_profiling(False)
     job.barrier()
 
@@ -569,8 +607,8 @@ def main():
     if a.ncu_launches:
         print(ncu_launch_summary(a.ncu_launches))
         return
-    if a.ncu_traffic:
-        ncu_traffic(a.ncu_traffic)
+    if a.ncu_traffic_kernels:
+        ncu_traffic_kernels(a.ncu_traffic_kernels)
         return
     rank, world, local = dist_env()
     if a.impl == "reference":

@@ -267,6 +267,12 @@ int scb_profile_read(scb_ctx* ctx, int* tags, double* flops, float* ms, int max)
  * counterpart in the reference, whose profile reports times only. */
 int scb_profile_bytes(const scb_ctx* ctx, double* bytes, int max);
 
+/* For the same launches: the kernel each one ran, as profilers name it (e.g.
+ * "gemm_tc_kernel<64, 64, 0, 1>"), one per line, so a per-kernel profiler capture
+ * can be matched to the op list. Writes at most cap - 1 bytes and a NUL (buf may be
+ * NULL to size it); returns the full length. */
+int scb_profile_kernels(const scb_ctx* ctx, char* buf, size_t cap);
+
 /* `Backend::profile_report` (src/backend.rs:33-38; `Cuda::profile_report`,
  * src/cuda.rs:1875-1886): the last profiled forward's device time per op class,
  * most expensive first, as text (one line per class: ms, share, launches, achieved

@@ -31,7 +31,7 @@ SYMBOLS = [
     "scb_set_profiling", "scb_profile_read", "scb_set_option", "scb_forward_dev_noalloc",
     "scb_forward_bands", "scb_band_unique_id", "scb_band_init", "scb_forward_band", "scb_profile_bytes", "scb_probe_mlp",
     "scb_band_sync", "scb_probe_head", "scb_probe_tail", "scb_probe_wait_timeout", "scb_mem_report",
-    "scb_profile_report", "scb_check_admission",
+    "scb_profile_report", "scb_check_admission", "scb_profile_kernels",
 ]
 SCB_OPT_FUSE_TRANS = 1
 SCB_OPT_RESIDUAL32 = 2
@@ -80,6 +80,7 @@ def load_library(path=None):
     lib.scb_probe_wait_timeout.argtypes = [vp, i]
     lib.scb_mem_report.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_profile_report.argtypes = [vp, ctypes.c_char_p, sz]
+    lib.scb_profile_kernels.argtypes = [vp, ctypes.c_char_p, sz]
     lib.scb_check_admission.argtypes = [vp, i, i, i, ctypes.POINTER(sz), ctypes.POINTER(sz)]
     lib.scb_probe_mlp.argtypes = [vp, i, i, vp, vp, i]
     lib.scb_need_bytes.argtypes = [i, i, i, i, ctypes.POINTER(sz)]
@@ -263,6 +264,13 @@ class B200:
         n = self.lib.scb_profile_read(self.ctx, tags, flops, ms, max_ops)
         self.lib.scb_profile_bytes(self.ctx, nbytes, max_ops)
         return [(OP_CLASSES[tags[k]], flops[k], nbytes[k], ms[k]) for k in range(n)]
+
+    def profile_kernels(self):
+        """The kernel each launch of the last profiled forward ran (profiler names)."""
+        n = self.lib.scb_profile_kernels(self.ctx, None, 0)
+        buf = ctypes.create_string_buffer(max(n, 0) + 1)
+        self.lib.scb_profile_kernels(self.ctx, buf, n + 1)
+        return buf.value.decode().splitlines()
 
     def last_launch_count(self):
         return self.lib.scb_last_launch_count(self.ctx)

@@ -744,6 +744,7 @@ struct scb_ctx {
   std::vector<int> prof_tags;
   std::vector<double> prof_flops;
   std::vector<double> prof_bytes;
+  std::string prof_kernels;  // the kernel of each launch, one name per line
   std::vector<float> prof_ms;
 };
 
@@ -1110,6 +1111,25 @@ double op_bytes(const Arena& A, const Op& op, const Io& io) {
   return 0;
 }
 
+// The kernel a launch of `op` runs, as profilers print it.
+std::string op_kernel_name(const Op& op) {
+  switch (op.kind) {
+    case Op::GEMM: {
+      const GemmOp& g = op.gemm;
+      return "gemm_tc_kernel<" + std::to_string(g.bn) + ", " + std::to_string(g.bk) + ", " + std::to_string(g.geo) +
+             ", " + (g.tma_epi ? "1" : "0") + ">";
+    }
+    case Op::ATTN: return "window_attn_kernel";
+    case Op::HEAD: return "head_tc_kernel";
+    case Op::TAIL: return "tail_tc_kernel";
+    case Op::TRANS: return op.trans_t == 32 ? "trans32_ws_kernel" : "trans64_ws_kernel";
+    case Op::MLP: return "mlp_fused_kernel<" + std::to_string(op.mlp_t) + ">";
+    case Op::XCHG: return "(halo exchange)";
+    case Op::ZERO: return "(memset)";
+  }
+  return "?";
+}
+
 int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, int c, int h, int w,
             cudaStream_t st, bool allow_profile = true) {
   // (a banded arena here is one rank of a NCCL band group)
@@ -1140,10 +1160,13 @@ int run_ops(scb_ctx* ctx, Arena& A, const void* x, int x_u8, void* y, int y_u8, 
     ctx->prof_tags.clear();
     ctx->prof_flops.clear();
     ctx->prof_bytes.clear();
+    ctx->prof_kernels.clear();
     for (const Op& op : A.ops) {
       ctx->prof_tags.push_back(op.tag);
       ctx->prof_flops.push_back(op.flops);
       ctx->prof_bytes.push_back(op_bytes(A, op, io));
+      ctx->prof_kernels += op_kernel_name(op);
+      ctx->prof_kernels += '\n';
     }
     ctx->prof_ms.assign(A.ops.size(), -1.f);  // filled by scb_profile_read after a sync
   }
@@ -2341,6 +2364,17 @@ int scb_profile_bytes(const scb_ctx* ctx, double* bytes, int max) {
   const int n = (int)std::min<size_t>(ctx->prof_bytes.size(), (size_t)std::max(max, 0));
   for (int i = 0; i < n && bytes; ++i) bytes[i] = ctx->prof_bytes[i];
   return n;
+}
+
+int scb_profile_kernels(const scb_ctx* ctx, char* buf, size_t cap) {
+  if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
+  const std::string& s = ctx->profiling ? ctx->prof_kernels : std::string();
+  if (buf && cap) {
+    const size_t m = std::min(cap - 1, s.size());
+    memcpy(buf, s.data(), m);
+    buf[m] = 0;
+  }
+  return (int)s.size();
 }
 
 const char* scb_last_error(const scb_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_error.c_str(); }
