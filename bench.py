@@ -65,6 +65,8 @@ def args_():
     ap.add_argument("--frames", type=int, default=16, help="frames per GPU per step")
     ap.add_argument("--micro", type=int, default=4, help="frames per library call")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--trans32-lanes", type=int, choices=[0, 1], default=None,
+                    help="full-resolution transformer kernel: 1 independent pair lanes, 0 warp-specialised")
     ap.add_argument("--residual32", action="store_true",
                     help="keep the in-stage residual stream in fp32 (SCB_OPT_RESIDUAL32, the reference's precision)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -290,17 +292,24 @@ def ncu_launch_summary(path):
     return "\n".join(out)
 
 
+NCU_UNITS = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "nsecond": 1.0, "ns": 1.0, "usecond": 1e3,
+             "us": 1e3, "msecond": 1e6, "ms": 1e6}
+
+
 def read_ncu_raw(path):
-    """`ncu -i <rep> --page raw --csv` output -> [(kernel name, {metric: value})]."""
+    """`ncu -i <rep> --page raw --csv` output -> [(kernel name, {metric: value})], with
+    byte metrics in bytes and durations in nanoseconds."""
     import csv
     rows = list(csv.reader(l for l in Path(path).read_text().splitlines() if l.startswith('"')))
-    h = rows[0]
+    if len(rows) < 3:
+        raise SystemExit(f"{path}: no captured launches")
+    h, units = rows[0], rows[1]
     out = []
-    for r in rows[2:]:  # row 1 holds the units
+    for r in rows[2:]:
         m = {}
-        for k, v in zip(h, r):
+        for k, u, v in zip(h, units, r):
             try:
-                m[k] = float(v.replace(",", ""))
+                m[k] = float(v.replace(",", "")) * NCU_UNITS.get(u, 1.0)
             except ValueError:
                 m[k] = v
         out.append((m.get("Kernel Name", "?"), m))
@@ -430,6 +439,8 @@ def frames_workload(a, job, scb):
     be = scb.B200(wt, device=local)
     if a.residual32:
         be.set_option(scb.backend.SCB_OPT_RESIDUAL32, 1)
+    if a.trans32_lanes is not None:
+        be.set_option(scb.backend.SCB_OPT_TRANS32_LANES, a.trans32_lanes)
     frames = scb.synth.frames(4000 + rank, F, H, W, distinct=min(F, 4))
     x_dev = torch.from_numpy(frames).cuda()
     y_dev = torch.empty((F, C, H, W), dtype=torch.float32, device="cuda")

@@ -247,7 +247,9 @@ int scb_last_launch_count(const scb_ctx* ctx);
  * channel a block moves through its 1x1 convs. */
 /* SCB_OPT_HOST_CHUNK (default 0 = automatic): images per compute call of
  * scb_forward_host's pipeline. */
-enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3 };
+/* SCB_OPT_TRANS32_LANES: the full-resolution transformer half (trans width 32) on the
+ * kernel with independent pair lanes (1) or on the warp-specialised one (0). */
+enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3, SCB_OPT_TRANS32_LANES = 4 };
 int scb_set_option(scb_ctx* ctx, int option, int value);
 
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,

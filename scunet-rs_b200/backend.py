@@ -36,6 +36,7 @@ SYMBOLS = [
 SCB_OPT_FUSE_TRANS = 1
 SCB_OPT_RESIDUAL32 = 2
 SCB_OPT_HOST_CHUNK = 3
+SCB_OPT_TRANS32_LANES = 4
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
               "trans_fused", "halo", "mlp"]
 

@@ -36,6 +36,7 @@
 #include "io_kernels.cuh"
 #include "trans.cuh"
 #include "trans32ws.cuh"
+#include "trans32mp.cuh"
 #include "trans64ws.cuh"
 #include "mlp.cuh"
 
@@ -564,6 +565,7 @@ struct Op {
   size_t zero_bytes = 0;
   TransGeom trans{};
   int trans_t = 0;
+  bool trans_lanes = false;  // t = 32: the independent-lane kernel instead of the warp-specialised one
   int tag = 0;
   double flops = 0;  // algorithmic FLOPs of this launch (2 per multiply-add)
   GemmOp gemm;
@@ -715,6 +717,7 @@ struct scb_ctx {
   int last_launches = 0;
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
   bool residual32 = false; // SCB_OPT_RESIDUAL32
+  bool trans32_lanes = false;  // SCB_OPT_TRANS32_LANES
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
   // context's device (looked up by scb_create, which loads the device code and
   // with it the array) and the plan laid out in it.
@@ -911,8 +914,25 @@ cudaError_t launch_mlp(const Op& op, int sms, cudaStream_t st) {
   return cudaErrorInvalidConfiguration;
 }
 
+cudaError_t launch_trans32mp(const Op& op, int sms, cudaStream_t st) {
+  using L = T32M;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(trans32_mp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const long pairs = (op.trans.win.n_windows + 1) / 2;
+  const long ctas = (pairs + L::LANES - 1) / L::LANES;
+  const int grid = (int)std::max(1L, std::min(ctas, (long)sms));  // one CTA per SM, persistent over pairs
+  trans32_mp_kernel<<<grid, L::THREADS, L::SMEM, st>>>(op.trans);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
-  if (op.trans_t == 32) return launch_trans32(op, sms, st);
+  if (op.trans_t == 32) return op.trans_lanes ? launch_trans32mp(op, sms, st) : launch_trans32(op, sms, st);
   if (op.trans_t == 64) return launch_trans64(op, sms, st);
   return cudaErrorInvalidConfiguration;
 }
@@ -1122,7 +1142,8 @@ std::string op_kernel_name(const Op& op) {
     case Op::ATTN: return "window_attn_kernel";
     case Op::HEAD: return "head_tc_kernel";
     case Op::TAIL: return "tail_tc_kernel";
-    case Op::TRANS: return op.trans_t == 32 ? "trans32_ws_kernel" : "trans64_ws_kernel";
+    case Op::TRANS:
+      return op.trans_t == 64 ? "trans64_ws_kernel" : op.trans_lanes ? "trans32_mp_kernel" : "trans32_ws_kernel";
     case Op::MLP: return "mlp_fused_kernel<" + std::to_string(op.mlp_t) + ">";
     case Op::XCHG: return "(halo exchange)";
     case Op::ZERO: return "(memset)";
@@ -1322,6 +1343,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
     Op tr{};
     tr.kind = Op::TRANS;
     tr.trans_t = t;
+    tr.trans_lanes = t == 32 && ctx->trans32_lanes;
     tr.tag = TAG_TRANS;
     tr.flops = 2.0 * P * (3.0 * t * t + 2.0 * 64 * t + t * t + 8.0 * t * t);
     TransGeom& tg = tr.trans;
@@ -1727,7 +1749,8 @@ cudaError_t preload_kernels() {
   const void* others[] = {(const void*)window_attn_kernel,     (const void*)trans32_ws_kernel,
                           (const void*)trans64_ws_kernel,      (const void*)mlp_fused_kernel<128>,
                           (const void*)mlp_fused_kernel<256>,  (const void*)head_tc_kernel,
-                          (const void*)tail_tc_kernel,         (const void*)wait_probe_kernel};
+                          (const void*)tail_tc_kernel,         (const void*)wait_probe_kernel,
+                          (const void*)trans32_mp_kernel};
   for (const void* f : others)
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
   return e;
@@ -2324,6 +2347,16 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     (option == SCB_OPT_FUSE_TRANS ? ctx->fuse_trans : ctx->residual32) = value != 0;
     ctx->arena.ops.clear();
     ctx->arena.n = 0;  // re-plan on the next forward
+    ctx->noalloc.ops.clear();
+    ctx->noalloc.n = 0;
+    ctx->band_arena.ops.clear();
+    for (Arena& A : ctx->vbands) A.ops.clear();
+    return SCB_OK;
+  }
+  if (option == SCB_OPT_TRANS32_LANES) {
+    ctx->trans32_lanes = value != 0;
+    ctx->arena.ops.clear();
+    ctx->arena.n = 0;
     ctx->noalloc.ops.clear();
     ctx->noalloc.n = 0;
     ctx->band_arena.ops.clear();
