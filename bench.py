@@ -72,6 +72,8 @@ def args_():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-traffic-kernels", metavar="RAW_CSV:KERNEL:SKIP", nargs="+",
                     help="write profiles/traffic.json from per-kernel ncu captures of a 1-frame forward and exit")
+    ap.add_argument("--traffic-out", default=str(ROOT / "profiles" / "traffic.json"),
+                    help="where --ncu-traffic-kernels writes its JSON")
     ap.add_argument("--ncu-launches", metavar="CSV", help="print a per-kernel launch table of an ncu capture and exit")
     return ap.parse_args()
 
@@ -316,7 +318,7 @@ def read_ncu_raw(path):
     return out
 
 
-def ncu_traffic_kernels(specs):
+def ncu_traffic_kernels(specs, out_path):
     """Per-kernel DRAM traffic from small ncu captures of a one-frame forward.
 
     Each spec is RAW_CSV:KERNEL:SKIP - an `ncu -i ... --page raw --csv` export of a
@@ -356,7 +358,7 @@ def ncu_traffic_kernels(specs):
     res = {"workload": "one 1920x1080 frame per call (padded 1920x1088), seeded config-4 frame and weights; "
                        "DRAM bytes from per-kernel ncu captures of 1-3 launches each",
            "kernels": out}
-    (ROOT / "profiles" / "traffic.json").write_text(json.dumps(res, indent=1) + "\n")
+    Path(out_path).write_text(json.dumps(res, indent=1) + "\n")
     lines = ["| kernel | classes | captured launches | DRAM MB per launch | algorithmic MB per launch | DRAM / algorithmic |",
              "|---|---|---|---|---|---|"]
     for k, e in sorted(out.items(), key=lambda kv: -kv[1]["dram_bytes"] / kv[1]["captured_launches"]):
@@ -619,7 +621,7 @@ def main():
         print(ncu_launch_summary(a.ncu_launches))
         return
     if a.ncu_traffic_kernels:
-        ncu_traffic_kernels(a.ncu_traffic_kernels)
+        ncu_traffic_kernels(a.ncu_traffic_kernels, a.traffic_out)
         return
     rank, world, local = dist_env()
     if a.impl == "reference":
