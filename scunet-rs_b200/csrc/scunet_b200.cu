@@ -739,6 +739,7 @@ struct scb_ctx {
   // on this GPU (virtual bands, in lockstep)
   ncclComm_t nccl = nullptr;
   int band_rank = 0, band_nranks = 1;
+  bool band_ready = false;  // scb_band_init has run and the group has not been aborted
   Arena band_arena;
   std::vector<Arena> vbands;
   // SCUNET_PROFILE equivalent (src/cuda.rs:106-135): events around every launch
@@ -2198,6 +2199,7 @@ int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks) {
   const NcclApi* nc = nccl_api(err);
   if (!nc) return fail(ctx, SCB_EINVAL, err);
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  ctx->band_ready = false;
   if (ctx->nccl) {
     nc->CommDestroy(ctx->nccl);
     ctx->nccl = nullptr;
@@ -2211,6 +2213,7 @@ int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks) {
   }
   ctx->band_rank = rank;
   ctx->band_nranks = nranks;
+  ctx->band_ready = true;
   free_arena(ctx->band_arena);
   ctx->err.clear();
   return SCB_OK;
@@ -2221,7 +2224,8 @@ int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   if (!x || !y) return fail(ctx, SCB_EINVAL, "NULL image pointer");
   if (!geom_ok(ctx, 1, c, h, w)) return SCB_EINVAL;
-  if (ctx->band_nranks > 1 && !ctx->nccl) return fail(ctx, SCB_EINVAL, "scb_band_init has not run");
+  if (!ctx->band_ready || (ctx->band_nranks > 1 && !ctx->nccl))
+    return fail(ctx, SCB_EINVAL, "no band group: scb_band_init has not run, or the group was aborted");
   const int hp = (h + 63) / 64 * 64, wp = (w + 63) / 64 * 64;
   CKC(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
   std::string err;
@@ -2287,6 +2291,7 @@ int scb_band_sync(scb_ctx* ctx, void* stream, int timeout_ms) {
     nc->CommAbort(ctx->nccl);
     ctx->nccl = nullptr;
   }
+  ctx->band_ready = false;
   return fail(ctx, SCB_ECUDA, why + "; the band group was aborted (call scb_band_init again)");
 }
 

@@ -181,3 +181,35 @@ def test_two_gpu_bands_at_8192(scb):
     for rank, finite, d in res:
         print(f"8192^2, 2 GPUs, rank {rank}: max |band - whole| {d}")
         assert finite and isinstance(d, float) and d <= TOL, (rank, finite, d)
+
+
+def test_band_sync_deadline_aborts_group(scb, be3):
+    """scb_band_sync's deadline on one GPU: a one-rank band group (no peer, so no NCCL
+    kernel ever waits), a forward of a 2048x2048 image, and a wait with a 0 ms
+    deadline that the forward cannot meet. The call returns SCB_ECUDA naming the
+    deadline, the group is aborted (the next banded forward refuses until scb_band_init
+    runs again), the forward itself completes, and a re-initialised group works.
+    The other failure - a peer rank that dies while its memory is mapped by this
+    one - is not run on a GPU (see the design notes); its host logic is tested on CPU."""
+    torch = _torch()
+    x = scb.synth.noisy_image_device(72, 3, 2048, 2048, 25 / 255, device="cuda")
+    be = scb.B200(be3.weights)
+    try:
+        be.band_init(scb.band_unique_id(), 0, 1)
+        y = torch.empty((1, 3, 2048, 2048), dtype=torch.float32, device="cuda")
+        s = torch.cuda.Stream()
+        torch.cuda.synchronize()
+        be.forward_band(x.data_ptr(), scb.SCB_U8, 3, 2048, 2048, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
+        rc = be.lib.scb_band_sync(be.ctx, s.cuda_stream, 0)
+        msg = be.lib.scb_last_error(be.ctx).decode()
+        s.synchronize()
+        assert rc == -3 and "did not finish within 0 ms" in msg and "aborted" in msg, (rc, msg)
+        rc = be.lib.scb_forward_band(be.ctx, x.data_ptr(), scb.SCB_U8, 3, 2048, 2048, y.data_ptr(), scb.SCB_F32,
+                                     s.cuda_stream)
+        assert rc == -1, "a banded forward ran on an aborted group"
+        be.band_init(scb.band_unique_id(), 0, 1)
+        be.forward_band(x.data_ptr(), scb.SCB_U8, 3, 2048, 2048, y.data_ptr(), scb.SCB_F32, s.cuda_stream)
+        be.band_sync(120000, s.cuda_stream)
+        assert bool(torch.isfinite(y).all())
+    finally:
+        be.close()
