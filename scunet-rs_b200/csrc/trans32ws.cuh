@@ -101,14 +101,13 @@ __device__ __forceinline__ void named_bar(int id, int n) {
 
 
 // Bounded mbarrier wait that also gives up when another group raised `abort_flag`;
-// a timeout records `code` and raises the flag. The first ~2 K polls do not suspend
-// the thread: a UMMA round trip completes within a few hundred cycles, and a
-// suspended waiter takes ~100 cycles longer to resume (measured on the transformer
-// kernels' group leaders); only longer waits sleep in hardware.
+// a timeout records `code` and raises the flag. (Polling without the suspend hint
+// before sleeping was measured: the leader resumes ~100 cycles sooner per round trip,
+// but the polling takes issue slots from the working warps of the SM, and the
+// full-resolution and half-resolution kernels got 3-40 % slower.)
 __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                                     unsigned code) {
-  for (int i = 0; i < 2048; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {
     // sleeps in hardware (no issue slots taken from the SMSP's other warps) until
