@@ -249,7 +249,13 @@ int scb_last_launch_count(const scb_ctx* ctx);
  * scb_forward_host's pipeline. */
 /* SCB_OPT_TRANS32_LANES: the full-resolution transformer half (trans width 32) on the
  * kernel with independent pair lanes (1) or on the warp-specialised one (0). */
-enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3, SCB_OPT_TRANS32_LANES = 4 };
+/* SCB_OPT_FUSE_PAIR (default 1): at 64 and 128 channels, run each block boundary
+ * inside a stage (block i's conv1_2 and block i + 1's conv1_1) as one kernel, so
+ * conv1_1 reads the updated residual stream from the chip instead of from HBM; 0 runs
+ * them as two GEMM launches (the reference's op sequence). Needs the fp16 residual
+ * stream and the fused transformer halves; ignored otherwise. */
+enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3, SCB_OPT_TRANS32_LANES = 4,
+       SCB_OPT_FUSE_PAIR = 5 };
 int scb_set_option(scb_ctx* ctx, int option, int value);
 
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,

@@ -39,6 +39,7 @@
 #include "trans32mp.cuh"
 #include "trans64ws.cuh"
 #include "mlp.cuh"
+#include "convpair.cuh"
 
 using namespace scb;
 
@@ -553,7 +554,7 @@ enum OpTag : int {
 };
 
 struct Op {
-  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS, XCHG, ZERO, MLP } kind;
+  enum Kind { GEMM, ATTN, HEAD, TAIL, TRANS, XCHG, ZERO, MLP, PAIR } kind;
   // XCHG (row bands): swap kHalo boundary rows of a stored plane with the
   // neighbouring bands; xchg_base is the plane, xchg_row the bytes of one row
   char* xchg_base = nullptr;
@@ -582,6 +583,13 @@ struct Op {
   // TAIL: the (y + x1) shadow as a TMA load map (one 128-pixel row segment per box)
   CUtensorMap tail_map;
   TailGeom tail{};
+  // PAIR: conv1_2 of a block and conv1_1 of the next in one kernel (convpair.cuh): Z
+  // and the residual plane as [64 x 128] SW128 boxes, the two Y planes as [32 x 128]
+  // SW64 store boxes
+  int pair_c = 0;
+  CUtensorMap pair_mz, pair_mx, pair_myc, pair_myt;
+  const __half *pair_w12 = nullptr, *pair_w11 = nullptr;
+  PairGeom pair{};
 };
 
 // A row band of one image (config 5): full-resolution rows [R0, R0 + rows) of the
@@ -718,6 +726,7 @@ struct scb_ctx {
   bool fuse_trans = true;  // SCB_OPT_FUSE_TRANS
   bool residual32 = false; // SCB_OPT_RESIDUAL32
   bool trans32_lanes = false;  // SCB_OPT_TRANS32_LANES
+  bool fuse_pair = true;       // SCB_OPT_FUSE_PAIR
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
   // context's device (looked up by scb_create, which loads the device code and
   // with it the array) and the plan laid out in it.
@@ -932,6 +941,36 @@ cudaError_t launch_trans32mp(const Op& op, int sms, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// TMA ring depth and CTAs per SM of the block-boundary kernel: at 64 channels two
+// CTAs per SM (eight epilogue warps) with a two-stage ring each; at 128 channels the
+// resident weights and staging leave room for one CTA with three stages.
+template <int C>
+cudaError_t launch_pair_t(const Op& op, int sms, cudaStream_t st) {
+  using L = PairSmem<C>;
+  constexpr int stages = C == 64 ? 2 : 3, ctas = C == 64 ? 2 : 1;
+  static bool attr_set[16] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 16 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(conv_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::smem(stages));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  PairGeom g = op.pair;
+  g.stages = stages;
+  const int grid = std::max(1, std::min(g.tiles, sms * ctas));
+  conv_pair_kernel<C><<<grid, 192, L::smem(stages), st>>>(op.pair_mz, op.pair_mx, op.pair_myc, op.pair_myt,
+                                                             op.pair_w12, op.pair_w11, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pair(const Op& op, int sms, cudaStream_t st) {
+  if (op.pair_c == 64) return launch_pair_t<64>(op, sms, st);
+  if (op.pair_c == 128) return launch_pair_t<128>(op, sms, st);
+  return cudaErrorInvalidConfiguration;
+}
+
 cudaError_t launch_trans(const Op& op, int sms, cudaStream_t st) {
   if (op.trans_t == 32) return op.trans_lanes ? launch_trans32mp(op, sms, st) : launch_trans32(op, sms, st);
   if (op.trans_t == 64) return launch_trans64(op, sms, st);
@@ -1072,6 +1111,8 @@ cudaError_t exec_op(scb_ctx* ctx, Arena& A, const Op& op, const Io& io, cudaStre
       return launch_trans(op, ctx->sms, st);
     case Op::MLP:
       return launch_mlp(op, ctx->sms, st);
+    case Op::PAIR:
+      return launch_pair(op, ctx->sms, st);
     case Op::XCHG:
       return cudaSuccess;  // handled by the caller (it needs the other bands)
     case Op::ZERO:
@@ -1120,6 +1161,8 @@ double op_bytes(const Arena& A, const Op& op, const Io& io) {
       return 64.0 * op.attn.win.n_windows * (3.0 * op.attn.t + op.attn.t) * 2;
     case Op::MLP:  // a in, x1 in, z out; both weight matrices
       return (double)op.mlp.M * op.mlp_t * 2 * 3 + 16.0 * op.mlp_t * op.mlp_t;
+    case Op::PAIR:  // Z and x in, x' and Y out; both weight matrices
+      return (double)op.pair.M * op.pair_c * 2 * 4 + 4.0 * op.pair_c * op.pair_c;
     case Op::HEAD: {
       const Region R = region_of(A, 0);
       return (double)R.px() * (io.c * (io.x_u8 ? 1 : 4) + 64 * (4 + 2));
@@ -1146,6 +1189,7 @@ std::string op_kernel_name(const Op& op) {
     case Op::TRANS:
       return op.trans_t == 64 ? "trans64_ws_kernel" : op.trans_lanes ? "trans32_mp_kernel" : "trans32_ws_kernel";
     case Op::MLP: return "mlp_fused_kernel<" + std::to_string(op.mlp_t) + ">";
+    case Op::PAIR: return "conv_pair_kernel<" + std::to_string(op.pair_c) + ">";
     case Op::XCHG: return "(halo exchange)";
     case Op::ZERO: return "(memset)";
   }
@@ -1266,8 +1310,12 @@ bool mlp_op(Op& mo, const BlockW& bw, const __half* a, __half* z, long z_ld, lon
          encode_map(&mo.mlp_w2, bw.w2, 2, d2, s2, b2b, 2, 128, err);
 }
 
+// `next`: the following block of the same stage, whose conv1_1 then runs in this
+// block's conv1_2 kernel (one PAIR op); `conv11_done`: this block's conv1_1 already
+// ran that way in the previous block's op.
 bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena& A, const Region& R,
-               const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err) {
+               const float* xin, float* xout, __half* xs, const float* skip, bool shifted, std::string& err,
+               const BlockW* next = nullptr, bool conv11_done = false) {
   const int c = bw.c, t = c / 2, cc = c / 2, heads = t / 32;
   const int n = R.n, H = R.H, W = R.W;
   const long P = R.px();
@@ -1276,7 +1324,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   Op op{};
   op.kind = Op::GEMM;
   // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
-  {
+  if (!conv11_done) {
     GemmOp g{};
     if (!mk.flat(g, xs + R.off(c), P, c, c, bw.w11, c, GEO_FLAT, fused ? 0 : t)) return false;
     g.e.bias = bw.b11;
@@ -1447,7 +1495,33 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   //    x is `xin` (fp32) when given, else the fp16 plane xs itself, updated in place
   //    (every tile reads its residual slab before storing that slab); fp32 x is
   //    written only when `xout` is given.
-  {
+  if (next) {
+    // x' = x + conv1_2(z) + b12 -> xs, and the next block's Y = conv1_1(x') + b11
+    if ((c != 64 && c != 128) || xin || xout || skip || next->c != c) {
+      err = "a block boundary kernel needs 64 or 128 channels and the fp16 residual stream";
+      return false;
+    }
+    Op po{};
+    po.kind = Op::PAIR;
+    po.tag = TAG_CONV1X1;
+    po.flops = 2.0 * 2.0 * P * c * c;
+    po.pair_c = c;
+    po.pair_w12 = bw.w12;
+    po.pair_w11 = next->w11;
+    po.pair.M = (int)P;
+    po.pair.tiles = (int)((P + 127) / 128);
+    po.pair.b12 = bw.b12;
+    po.pair.b11 = next->b11;
+    const uint64_t dz[2] = {(uint64_t)c, (uint64_t)P}, sz[1] = {(uint64_t)c * 2};
+    const uint64_t dy[2] = {(uint64_t)cc, (uint64_t)P}, sy[1] = {(uint64_t)cc * 2};
+    const uint32_t bz[2] = {64, 128}, by[2] = {32, 128};
+    if (!encode_map(&po.pair_mz, A.z + R.off(c), 2, dz, sz, bz, 2, 128, err) ||
+        !encode_map(&po.pair_mx, xs + R.off(c), 2, dz, sz, bz, 2, 128, err) ||
+        !encode_map(&po.pair_myc, A.y + R.off(cc), 2, dy, sy, by, 2, 64, err) ||
+        !encode_map(&po.pair_myt, A.yt + R.off(t), 2, dy, sy, by, 2, 64, err))
+      return false;
+    ops.push_back(po);
+  } else {
     GemmOp g{};
     if (!mk.flat(g, A.z + R.off(c), P, c, c, bw.w12, c)) return false;
     g.e.bias = bw.b12;
@@ -1538,6 +1612,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       ops.push_back(op);
     }
     const int nb = ctx->config[s];
+    bool prev_pair = false;
     for (int i = 0; i < nb; ++i) {
       // the residual stream: fp16 in xs (default; a down stage's first block reads the
       // skip plane's fp16 shadow, which the head / down conv wrote into xs), or fp32
@@ -1551,8 +1626,15 @@ int build_plan(scb_ctx* ctx, Arena& A) {
         skip = A.skip[lvl];
         xout = nullptr;
       }
-      if (!block_ops(ctx, ops, ctx->blocks[s][i], A, R, xin, xout, A.xs[lvl], skip, (i % 2) == 1, err))
+      // a boundary between two blocks of the stage at 64 or 128 channels runs as one
+      // kernel (this block's conv1_2 with the next block's conv1_1), when the residual
+      // stream is fp16 and the next block's transformer half normalises its own input
+      const bool pair = ctx->fuse_pair && !ctx->residual32 && ctx->fuse_trans && !skip && i + 1 < nb &&
+                        (c == 64 || c == 128);
+      if (!block_ops(ctx, ops, ctx->blocks[s][i], A, R, xin, xout, A.xs[lvl], skip, (i % 2) == 1, err,
+                     pair ? &ctx->blocks[s][i + 1] : nullptr, prev_pair))
         return fail(ctx, SCB_EINVAL, err);
+      prev_pair = pair;
     }
     if (s < 3) {
       // m_down{k}.4 : 2x2 stride-2 conv -> the next level's skip (fp32) + shadow
@@ -1751,7 +1833,8 @@ cudaError_t preload_kernels() {
                           (const void*)trans64_ws_kernel,      (const void*)mlp_fused_kernel<128>,
                           (const void*)mlp_fused_kernel<256>,  (const void*)head_tc_kernel,
                           (const void*)tail_tc_kernel,         (const void*)wait_probe_kernel,
-                          (const void*)trans32_mp_kernel};
+                          (const void*)trans32_mp_kernel,      (const void*)conv_pair_kernel<64>,
+                          (const void*)conv_pair_kernel<128>};
   for (const void* f : others)
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
   return e;
@@ -2358,8 +2441,8 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     for (Arena& A : ctx->vbands) A.ops.clear();
     return SCB_OK;
   }
-  if (option == SCB_OPT_TRANS32_LANES) {
-    ctx->trans32_lanes = value != 0;
+  if (option == SCB_OPT_TRANS32_LANES || option == SCB_OPT_FUSE_PAIR) {
+    (option == SCB_OPT_TRANS32_LANES ? ctx->trans32_lanes : ctx->fuse_pair) = value != 0;
     ctx->arena.ops.clear();
     ctx->arena.n = 0;
     ctx->noalloc.ops.clear();
@@ -2606,6 +2689,7 @@ int scb_probe_block(scb_ctx* ctx, int stage, int index, const float* x32, int n,
       case Op::TRANS: e = launch_trans(op, ctx->sms, ctx->stream); break;
       case Op::ATTN: e = launch_attn(op, ctx->stream); break;
       case Op::MLP: e = launch_mlp(op, ctx->sms, ctx->stream); break;
+      case Op::PAIR: e = launch_pair(op, ctx->sms, ctx->stream); break;
       default: e = cudaErrorInvalidValue;  // a block builds none of the other kinds
     }
     if (e != cudaSuccess) break;

@@ -107,3 +107,22 @@ def test_footprint_and_release(scb, be3):
     assert wb > 30e6 and sb > 0
     be3.release_scratch()
     assert be3.footprint()[1] == 0
+
+
+@pytest.mark.parametrize("stem,h,w", [("c64", 256, 192), ("c64b", 72, 136), ("c64c", 200, 328)])
+def test_block_boundary_kernel_is_bit_identical(scb, be3, stem, h, w):
+    """The block-boundary kernel (block i's conv1_2 and block i+1's conv1_1 in one
+    launch, SCB_OPT_FUSE_PAIR = 1, the default) computes the same fp16 values as the
+    two separate GEMM launches: the whole forward is bit-identical either way."""
+    _gpu()
+    x = scb.synth.noisy_image(len(stem) + h, 3, h, w, 25 / 255)[None]
+    fused = be3.forward_host(x)
+    n_fused = be3.last_launch_count()
+    be3.set_option(scb.backend.SCB_OPT_FUSE_PAIR, 0)
+    try:
+        sep = be3.forward_host(x)
+        n_sep = be3.last_launch_count()
+    finally:
+        be3.set_option(scb.backend.SCB_OPT_FUSE_PAIR, 1)
+    assert n_sep - n_fused == 12, (n_sep, n_fused)  # 3 boundaries x 4 stages at 64 / 128 channels
+    assert np.array_equal(fused, sep), f"max |diff| {np.abs(fused - sep).max():.3e}"
