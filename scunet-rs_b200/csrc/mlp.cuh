@@ -224,10 +224,19 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       hc += L::NCH;
       // ---- z = acc + b2 + x1, in place ----
-      if (!ok || !(ok = mbar_wait(acc_full, t & 1, SCB_ERR_WAIT_ACC))) break;
-      tc_fence_after();
+      // this thread's x1 columns are loaded before the wait for the accumulator, so
+      // their latency overlaps the last chunk's UMMAs
+      if (!ok) break;
       const long p = (long)tile * 128 + r;
-#pragma unroll 1
+      uint4 xv[T / 16];
+      if (p < g.M) {
+        const uint4* zp = reinterpret_cast<const uint4*>(g.z + p * g.z_ld + hf * (T / 2));
+#pragma unroll
+        for (int i = 0; i < T / 16; ++i) xv[i] = zp[i];
+      }
+      if (!(ok = mbar_wait(acc_full, t & 1, SCB_ERR_WAIT_ACC))) break;
+      tc_fence_after();
+#pragma unroll
       for (int cc = hf * (T / 2); cc < (hf + 1) * (T / 2); cc += 32) {
         float v[32];
         tmem_ld16x2(trow + 256 + cc, v, trow + 256 + cc + 16, v + 16);
@@ -236,7 +245,7 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const float4* b4 = reinterpret_cast<const float4*>(g.b2 + cc);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint4 u = zp[i];
+            const uint4 u = xv[(cc - hf * (T / 2)) / 8 + i];
             const __half2* hp = reinterpret_cast<const __half2*>(&u);
             const float4 ba = __ldg(b4 + 2 * i), bb = __ldg(b4 + 2 * i + 1);
             const float bs[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
