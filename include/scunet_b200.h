@@ -125,7 +125,12 @@ int scb_forward_bands(scb_ctx* ctx, int nbands, const void* x, int x_dtype, int 
  * rank calls scb_forward_band with the FULL image x (device, on its own GPU); it
  * computes its band and writes that band's rows of y (device [1][c][h][w] on its
  * own GPU). Halo rows travel with NCCL send/recv over NVLink on the compute
- * stream. scb_band_init with nranks = 1 runs the whole image as one band. */
+ * stream. scb_band_init with nranks = 1 runs the whole image as one band.
+ * Of x, scb_forward_band reads only the input rows [lo, hi) of its band
+ * [R0, R0 + rows): lo = min(max(R0 - 1, 0), h - 1), hi = max(lo + 1, min(R0 + rows
+ * + 1, h)) (the head's 3x3 conv reads one row above and below; padded rows at or
+ * past h read row h - 1), so a caller holding the image on the host copies only
+ * those rows to each rank; the other rows of x may hold anything. */
 int scb_band_unique_id(void* id_out);
 int scb_band_init(scb_ctx* ctx, const void* id, int rank, int nranks);
 int scb_forward_band(scb_ctx* ctx, const void* x, int x_dtype, int c, int h, int w, void* y, int y_dtype,

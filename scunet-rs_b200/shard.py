@@ -25,6 +25,18 @@ def band_rows(hp, rank, world):
     return 64 * b0, 64 * (b1 - b0)
 
 
+def band_input_rows(h, hp, rank, world):
+    """[lo, hi) of the input image's h rows that this rank's band reads. The head's
+    3x3 conv of band rows [R0, R0 + rows) reads one row above and one below, and a
+    padded row at or past h reads row h - 1 (the replicate pad), so a caller holding
+    the image on the host copies only these rows to the rank's GPU."""
+    if h < 1 or hp < h:
+        raise ValueError(f"image of {h} rows, padded to {hp}")
+    r0, rows = band_rows(hp, rank, world)
+    lo = min(max(r0 - 1, 0), h - 1)
+    return lo, max(lo + 1, min(r0 + rows + 1, h))
+
+
 def max_over_ranks(value, group=None):
     """The largest value over the ranks of the default (or given) process group;
     the value itself when torch.distributed is not initialised."""

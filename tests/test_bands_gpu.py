@@ -90,7 +90,12 @@ def _band_worker(rank, nranks, uid, x, q):
     be = scb.B200(scb.Weights.seeded(3, 0), device=rank)
     be.band_init(uid, rank, nranks)
     c, h, w = x.shape[1:]
-    xd = torch.from_numpy(x).cuda()
+    # Only the input rows the band reads hold the image; the others hold its negative,
+    # which must not reach this rank's output.
+    lo, hi = scb.shard.band_input_rows(h, -(-h // 64) * 64, rank, nranks)
+    xs = 255 - x
+    xs[:, :, lo:hi] = x[:, :, lo:hi]
+    xd = torch.from_numpy(xs).cuda()
     y = torch.full((1, c, h, w), float("nan"), dtype=torch.float32, device="cuda")
     s = torch.cuda.Stream()
     torch.cuda.synchronize()
@@ -102,6 +107,8 @@ def _band_worker(rank, nranks, uid, x, q):
 
 
 def test_two_gpu_bands_over_nccl(scb, be3):
+    """Two processes, one GPU and one band each, halo rows over NCCL; each rank's
+    input holds the image only on the rows `shard.band_input_rows` names."""
     torch = _torch()
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

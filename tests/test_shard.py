@@ -24,6 +24,22 @@ def test_band_rows_cover_image(scb):
         scb.shard.band_rows(128, 0, 3)
 
 
+def test_band_input_rows_are_the_rows_the_head_reads(scb):
+    """The input rows a band reads, against the head conv's read pattern written out:
+    rows y - 1, y, y + 1 of every band row y inside the padded image, clamped to
+    h - 1 by the replicate pad (io_kernels.cuh, head_tc_kernel's im2col)."""
+    for h, world in [(8192, 8), (1080, 3), (1000, 2), (65, 2), (130, 3), (1, 1), (64, 1)]:
+        hp = -(-h // 64) * 64
+        for r in range(world):
+            r0, rows = scb.shard.band_rows(hp, r, world)
+            read = {min(yy, h - 1) for y in range(r0, r0 + rows) for yy in (y - 1, y, y + 1) if 0 <= yy < hp}
+            lo, hi = scb.shard.band_input_rows(h, hp, r, world)
+            assert (lo, hi) == (min(read), max(read) + 1), (h, world, r)
+            assert read == set(range(lo, hi))
+    with pytest.raises(ValueError):
+        scb.shard.band_input_rows(100, 64, 0, 1)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
