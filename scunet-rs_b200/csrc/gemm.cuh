@@ -37,7 +37,11 @@
 //                   (the first before the accumulator wait); outputs are written to
 //                   swizzled smem staging and leave through TMA bulk tensor stores,
 //                   double-buffered. Every global byte moves in full lines through
-//                   the TMA unit.
+//                   the TMA unit. PAIRS = true (flat GEMMs without residual slabs):
+//                   two slabs per round, one in each staging buffer, so a tile pays
+//                   half the rounds of barriers, proxy fences and store issues that
+//                   bound these epilogues (measured: the level-2 qkv linear 154 ->
+//                   118 us per 4-frame launch).
 //   TMAEPI = false: per-thread vector loads/stores, for the variants without a TMA
 //                   one (and the LayerNorm of non-flat GEMMs).
 #pragma once
@@ -287,7 +291,7 @@ __device__ __forceinline__ void epi_slab_store(const CUtensorMap* m, const void*
 // Named barrier over the four epilogue warps only.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int BN, int BK, int GEO, bool TMAEPI>
+template <int BN, int BK, int GEO, bool TMAEPI, bool PAIRS = false>
 __global__ void __launch_bounds__(192, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmGeom g,
                const GemmEpi e, const __grid_constant__ EpiMaps em) {
@@ -295,6 +299,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(BK == 64 || BK == 32, "BK is one 128B or 64B swizzle row of fp16");
   static_assert(!TMAEPI || BN % 32 == 0, "TMA epilogue works in 32-column slabs");
+  static_assert(!PAIRS || (TMAEPI && BN % 64 == 0), "paired slabs: TMA epilogue, 64-column rounds");
   constexpr uint32_t ROWB = BK * 2;
   constexpr uint32_t SWZ = (BK == 64) ? SW_128B : SW_64B;
   constexpr uint32_t IDESC = make_idesc_f16(128, BN);
@@ -571,6 +576,102 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         ln_mean = shift + md;
         ln_rstd = rsqrtf(fmaxf(s2 * inv_n - md * md, 0.f) + 1e-5f);
       }
+      if constexpr (PAIRS) {
+        // Two 32-column slabs per round, one in each staging buffer: half the barrier,
+        // fence and store rounds of the slab loop below (no residual slabs here: the
+        // host picks this form only without them)
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64, os += 2) {
+          float v[64];
+          {
+            uint32_t rr[4][16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) tmem_ld16_issue(tbase + c + 16 * q4, rr[q4]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              tmem_fence16(rr[q4]);
+              u32_to_f32_16(rr[q4], v + 16 * q4);
+            }
+          }
+          const int n = n0 + c;
+          if (e.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(e.bias + n);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float4 bb = __ldg(b4 + j);
+              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+            }
+          }
+          if (e.act == ACT_RELU) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = fmaxf(v[j], 0.f);
+          } else if (e.act == ACT_GELU) {
+#pragma unroll
+            for (int j = 0; j < 64; j += 2) {
+              const __half2 gv = gelu_tanh_h2(__floats2half2_rn(v[j], v[j + 1]));
+              const float2 f = __half22float2(gv);
+              v[j] = f.x;
+              v[j + 1] = f.y;
+            }
+          }
+          // both staging buffers were last read by the previous round's stores
+          if (elected) bulk_wait_group_read<0>();
+          epi_bar();
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint8_t* ob = out_stage + hh * e.st_out_bytes;
+            const float* vh = v + 32 * hh;
+            const int nh = n + 32 * hh;
+            if (e.st_out32 >= 0) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<float4*>(ob + e.st_out32 + swz_off(r, j, 128)) =
+                    make_float4(vh[4 * j], vh[4 * j + 1], vh[4 * j + 2], vh[4 * j + 3]);
+            }
+            if (do_ln && nh >= e.ln_lo && nh < e.ln_lo + e.ln_n) {
+              const float* lg = e.ln_g + (nh - e.ln_lo);
+              const float* lb = e.ln_b + (nh - e.ln_lo);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  o[i] = (vh[8 * j + i] - ln_mean) * ln_rstd * __ldg(lg + 8 * j + i) + __ldg(lb + 8 * j + i);
+                *reinterpret_cast<uint4*>(ob + e.st_ln + swz_off(r, j, 64)) =
+                    make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]),
+                               pack_half2(o[6], o[7]));
+              }
+            }
+            if (e.st_out16 >= 0) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(ob + e.st_out16 + swz_off(r, j, 64)) =
+                    make_uint4(pack_half2(vh[8 * j], vh[8 * j + 1]), pack_half2(vh[8 * j + 2], vh[8 * j + 3]),
+                               pack_half2(vh[8 * j + 4], vh[8 * j + 5]), pack_half2(vh[8 * j + 6], vh[8 * j + 7]));
+            }
+          }
+          fence_proxy_async_smem();
+          epi_bar();  // both halves staged
+          if (elected) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint8_t* ob = out_stage + hh * e.st_out_bytes;
+              const int nh = n + 32 * hh;
+              if (e.st_out32 >= 0) epi_slab_store<GEO>(&em.out32, ob + e.st_out32, nh, mt, g);
+              if (e.st_out16 >= 0) {
+                if (e.out16b && nh >= e.out16_split)
+                  epi_slab_store<GEO>(&em.out16b, ob + e.st_out16, nh - e.out16_split, mt, g);
+                else
+                  epi_slab_store<GEO>(&em.out16, ob + e.st_out16, nh, mt, g);
+              }
+              if (do_ln && nh >= e.ln_lo && nh < e.ln_lo + e.ln_n)
+                epi_slab_store<GEO>(&em.lnout, ob + e.st_ln, nh - e.ln_lo, mt, g);
+            }
+            bulk_commit_group();
+          }
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32, ++os) {
         // buffer (rs + NRES - 1) % NRES held slab rs - 1, which every thread finished
@@ -682,6 +783,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (ln_slab) epi_slab_store<GEO>(&em.lnout, ob + e.st_ln, n - e.ln_lo, mt, g);
           bulk_commit_group();
         }
+      }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);

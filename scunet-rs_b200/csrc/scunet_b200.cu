@@ -121,6 +121,7 @@ constexpr int kSmemPerSm = 227 * 1024;
 struct GemmOp {
   int geo = GEO_FLAT, bn = 64, bk = 64;
   bool tma_epi = false;
+  bool pairs = false;  // TMA epilogue in 64-column rounds (flat GEMMs without residual slabs)
   CUtensorMap ta, tb;
   GemmGeom g{};
   GemmEpi e{};
@@ -162,10 +163,10 @@ constexpr int kResBufs = 2;
 #endif
 constexpr bool kResidualMma = SCB_RESIDUAL_MMA != 0;
 
-template <int BN, int BK, int GEO, bool TMAEPI>
+template <int BN, int BK, int GEO, bool TMAEPI, bool PAIRS = false>
 cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   using L = GemmSmem<BN, BK, GEO>;
-  auto kfn = gemm_tc_kernel<BN, BK, GEO, TMAEPI>;
+  auto kfn = gemm_tc_kernel<BN, BK, GEO, TMAEPI, PAIRS>;
   static bool attr_set[16] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -193,11 +194,16 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   if (op.bn == BN && op.bk == BK && op.geo == GEO && !op.tma_epi)                      \
     return launch_t<BN, BK, GEO, false>(op, sms, st);
 #define SCB_GEMM_TCASE(BN, BK, GEO)                                                    \
-  if (op.bn == BN && op.bk == BK && op.geo == GEO && op.tma_epi)                       \
+  if (op.bn == BN && op.bk == BK && op.geo == GEO && op.tma_epi && !op.pairs)          \
     return launch_t<BN, BK, GEO, true>(op, sms, st);
+#define SCB_GEMM_PCASE(BN, BK, GEO)                                                    \
+  if (op.bn == BN && op.bk == BK && op.geo == GEO && op.tma_epi && op.pairs)           \
+    return launch_t<BN, BK, GEO, true, true>(op, sms, st);
 
-// Every compiled GEMM variant: T = with the TMA epilogue, D = direct epilogue.
-#define SCB_GEMM_VARIANTS(T, D)                                                                              \
+// Every compiled GEMM variant: T = with the TMA epilogue, D = direct epilogue, P = TMA
+// epilogue in paired slabs (flat GEMMs whose tile is a multiple of 64 columns).
+#define SCB_GEMM_VARIANTS(T, D, P)                                                                           \
+  P(64, 64, GEO_FLAT) P(128, 64, GEO_FLAT) P(192, 64, GEO_FLAT) P(256, 64, GEO_FLAT) P(128, 32, GEO_FLAT)   \
   T(64, 64, GEO_FLAT) T(128, 64, GEO_FLAT) T(192, 64, GEO_FLAT) T(256, 64, GEO_FLAT) T(128, 32, GEO_FLAT)   \
   T(32, 32, GEO_CONV3X) T(32, 32, GEO_CONV3W) T(64, 64, GEO_CONV3X) T(128, 64, GEO_CONV3X)                  \
   T(256, 64, GEO_CONV3) T(128, 64, GEO_DOWN2) T(256, 64, GEO_DOWN2) T(64, 64, GEO_UP2) T(128, 64, GEO_UP2)  \
@@ -208,7 +214,7 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   D(128, 64, GEO_DOWN2) D(256, 64, GEO_DOWN2)
 
 cudaError_t launch_gemm(const GemmOp& op, int sms, cudaStream_t st) {
-  SCB_GEMM_VARIANTS(SCB_GEMM_TCASE, SCB_GEMM_CASE)
+  SCB_GEMM_VARIANTS(SCB_GEMM_TCASE, SCB_GEMM_CASE, SCB_GEMM_PCASE)
   return cudaErrorInvalidConfiguration;
 }
 
@@ -267,6 +273,7 @@ void pick_tile(int W, int& TW, int& TH) {
 
 struct Maker {
   std::string* err;
+  bool pairs_enabled = true;  // SCB_OPT_GEMM_PAIRS
   bool ok = true;
 
   bool mapB(GemmOp& op, const __half* w, int N, int K) {
@@ -503,6 +510,7 @@ struct Maker {
     }
     e.st_out_bytes = off;
     op.tma_epi = true;
+    op.pairs = op.geo == GEO_FLAT && op.bn % 64 == 0 && e.st_res_bytes == 0 && pairs_enabled;
     return true;
   }
 
@@ -727,6 +735,7 @@ struct scb_ctx {
   bool residual32 = false; // SCB_OPT_RESIDUAL32
   bool trans32_lanes = false;  // SCB_OPT_TRANS32_LANES
   bool fuse_pair = true;       // SCB_OPT_FUSE_PAIR
+  bool gemm_pairs = true;      // SCB_OPT_GEMM_PAIRS
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
   // context's device (looked up by scb_create, which loads the device code and
   // with it the array) and the plan laid out in it.
@@ -1181,7 +1190,7 @@ std::string op_kernel_name(const Op& op) {
     case Op::GEMM: {
       const GemmOp& g = op.gemm;
       return "gemm_tc_kernel<" + std::to_string(g.bn) + ", " + std::to_string(g.bk) + ", " + std::to_string(g.geo) +
-             ", " + (g.tma_epi ? "1" : "0") + ">";
+             ", " + (g.tma_epi ? "1" : "0") + (g.pairs ? ", 1" : "") + ">";
     }
     case Op::ATTN: return "window_attn_kernel";
     case Op::HEAD: return "head_tc_kernel";
@@ -1320,7 +1329,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   const int n = R.n, H = R.H, W = R.W;
   const long P = R.px();
   const bool fused = ctx->fuse_trans && (t == 32 || t == 64);
-  Maker mk{&err};
+  Maker mk{&err, ctx->gemm_pairs};
   Op op{};
   op.kind = Op::GEMM;
   // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
@@ -1597,7 +1606,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
-      Maker mk{&err};
+      Maker mk{&err, ctx->gemm_pairs};
       GemmOp g{};
       if (!mk.up2(g, A.xs[lvl + 1] + Rn.off(2 * c), Rn.n, Rn.rows, Rn.W, 2 * c, ctx->wup[s - 4], c))
         return fail(ctx, SCB_EINVAL, err);
@@ -1641,7 +1650,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
-      Maker mk{&err};
+      Maker mk{&err, ctx->gemm_pairs};
       GemmOp g{};
       if (!mk.down2(g, A.xs[lvl] + R.off(c), R.n, R.rows, R.W, c, ctx->wdown[s], 2 * c))
         return fail(ctx, SCB_EINVAL, err);
@@ -1826,9 +1835,12 @@ cudaError_t preload_kernels() {
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, BK, GEO, true>);
 #define SCB_PRELOAD_D(BN, BK, GEO) \
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, BK, GEO, false>);
-  SCB_GEMM_VARIANTS(SCB_PRELOAD_T, SCB_PRELOAD_D)
+#define SCB_PRELOAD_P(BN, BK, GEO) \
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, BK, GEO, true, true>);
+  SCB_GEMM_VARIANTS(SCB_PRELOAD_T, SCB_PRELOAD_D, SCB_PRELOAD_P)
 #undef SCB_PRELOAD_T
 #undef SCB_PRELOAD_D
+#undef SCB_PRELOAD_P
   const void* others[] = {(const void*)window_attn_kernel,     (const void*)trans32_ws_kernel,
                           (const void*)trans64_ws_kernel,      (const void*)mlp_fused_kernel<128>,
                           (const void*)mlp_fused_kernel<256>,  (const void*)head_tc_kernel,
@@ -2441,8 +2453,10 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     for (Arena& A : ctx->vbands) A.ops.clear();
     return SCB_OK;
   }
-  if (option == SCB_OPT_TRANS32_LANES || option == SCB_OPT_FUSE_PAIR) {
-    (option == SCB_OPT_TRANS32_LANES ? ctx->trans32_lanes : ctx->fuse_pair) = value != 0;
+  if (option == SCB_OPT_TRANS32_LANES || option == SCB_OPT_FUSE_PAIR || option == SCB_OPT_GEMM_PAIRS) {
+    (option == SCB_OPT_TRANS32_LANES ? ctx->trans32_lanes
+     : option == SCB_OPT_FUSE_PAIR   ? ctx->fuse_pair
+                                     : ctx->gemm_pairs) = value != 0;
     ctx->arena.ops.clear();
     ctx->arena.n = 0;
     ctx->noalloc.ops.clear();
@@ -2538,7 +2552,7 @@ int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16,
                    const void* res16, void* out16, float* out32) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err};
+  Maker mk{&err, ctx->gemm_pairs};
   GemmOp g{};
   if (!mk.flat(g, static_cast<const __half*>(a16), M, K, K, static_cast<const __half*>(b16), N))
     return fail(ctx, SCB_EINVAL, err);
@@ -2560,7 +2574,7 @@ int scb_probe_conv3x3(scb_ctx* ctx, const void* x16, int n, int H, int W, int ci
                       const void* res16, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err};
+  Maker mk{&err, ctx->gemm_pairs};
   GemmOp g{};
   if (!mk.conv3(g, static_cast<const __half*>(x16), n, H, W, cin, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);
@@ -2577,7 +2591,7 @@ int scb_probe_down2(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin,
                     float* out32, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err};
+  Maker mk{&err, ctx->gemm_pairs};
   GemmOp g{};
   if (!mk.down2(g, static_cast<const __half*>(x16), n, H, W, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);
@@ -2593,7 +2607,7 @@ int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, c
                   float* out32, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err};
+  Maker mk{&err, ctx->gemm_pairs};
   GemmOp g{};
   if (!mk.up2(g, static_cast<const __half*>(x16), n, h, w, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);

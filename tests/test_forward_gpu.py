@@ -1,6 +1,8 @@
 """End to end on the device: the golden fixtures (upstream torch FP32 on seeded
 weights), batched vs single, and bit-identical repeats (the reference's race
 detector, tests/cuda_ops.rs:217-251)."""
+import re
+
 import numpy as np
 import pytest
 
@@ -126,3 +128,28 @@ def test_block_boundary_kernel_is_bit_identical(scb, be3, stem, h, w):
         be3.set_option(scb.backend.SCB_OPT_FUSE_PAIR, 1)
     assert n_sep - n_fused == 12, (n_sep, n_fused)  # 3 boundaries x 4 stages at 64 / 128 channels
     assert np.array_equal(fused, sep), f"max |diff| {np.abs(fused - sep).max():.3e}"
+
+
+def test_paired_slab_epilogue_is_bit_identical(scb, be3):
+    """The flat GEMMs' 64-column epilogue rounds (SCB_OPT_GEMM_PAIRS = 1, the default:
+    qkv and the LayerNorm-fused conv1_1 at 1/4 and 1/8 resolution, among others) store
+    the same fp16 / fp32 values as the 32-column slab loop: the forward is bit-identical,
+    and the paired variants are the ones that ran."""
+    _gpu()
+    x = scb.synth.noisy_image(91, 3, 136, 200, 25 / 255)[None]
+    be3.set_profiling(True)
+    try:
+        paired = be3.forward_host(x)
+        k_on = be3.profile_kernels()
+        be3.set_option(scb.backend.SCB_OPT_GEMM_PAIRS, 0)
+        try:
+            slabs = be3.forward_host(x)
+            k_off = be3.profile_kernels()
+        finally:
+            be3.set_option(scb.backend.SCB_OPT_GEMM_PAIRS, 1)
+    finally:
+        be3.set_profiling(False)
+    paired_name = re.compile(r"gemm_tc_kernel<\d+, \d+, \d+, 1, 1>")  # <BN, BK, geometry, TMA, paired>
+    assert any(paired_name.fullmatch(k) for k in k_on) and not any(paired_name.fullmatch(k) for k in k_off)
+    assert len(k_on) == len(k_off)
+    assert np.array_equal(paired, slabs), f"max |diff| {np.abs(paired - slabs).max():.3e}"
