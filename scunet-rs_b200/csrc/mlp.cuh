@@ -12,9 +12,10 @@
 //
 // Warp 0 streams the tile's a (once) and the weights' 64-wide K blocks through a
 // ring of shared-memory stages with TMA; warp 1 issues the UMMAs, H_{j+1} before
-// acc += Hs_j, so the tensor pipe computes the next chunk while warps 2-9 evaluate
-// GELU of this one (two warps per TMEM lane quarter, each half of the columns);
-// warps 2-9 finally write z = acc + b2 + x1 in place over x1.
+// acc += Hs_j, so the tensor pipe computes the next chunk while the 16 epilogue warps
+// evaluate GELU of this one (four warps per TMEM lane quarter, each a quarter of the
+// columns; 8 warps measured 4 % slower at T = 128) and finally write z = acc + b2 + x1
+// in place over x1.
 // HBM traffic per token: a (2T bytes) in, x1 (2T) in, z (2T) out; the weights
 // (16 T^2 bytes) stream from L2.
 #pragma once
@@ -47,7 +48,8 @@ struct MlpLayout {
   static constexpr int TMEM_COLS = 512;                     // H: [0, 128) and [128, 256); acc: [256, 256 + T)
 };
 
-constexpr int MLP_THREADS = 320;  // producer, UMMA issuer, 8 epilogue warps
+constexpr int MLP_EPI_WARPS = 16;
+constexpr int MLP_THREADS = 64 + 32 * MLP_EPI_WARPS;  // producer, UMMA issuer, epilogue warps
 
 template <int T>
 __global__ void __launch_bounds__(MLP_THREADS, 1)
@@ -78,12 +80,12 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     mbar_init(a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&h_full[b], 1);
-      mbar_init(&h_empty[b], 256);
-      mbar_init(&hs_full[b], 256);
+      mbar_init(&h_empty[b], 32 * MLP_EPI_WARPS);
+      mbar_init(&hs_full[b], 32 * MLP_EPI_WARPS);
       mbar_init(&hs_empty[b], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 256);
+    mbar_init(acc_empty, 32 * MLP_EPI_WARPS);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW0);
@@ -181,9 +183,10 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..9, thread = (token row, column half) ----------------
+    // ---------------- epilogue: warps 2.., thread = (token row, column share) ----------------
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int hf = (warp - 2) >> 2;    // which half of the columns
+    const int hf = (warp - 2) >> 2;    // which share of the columns
+    constexpr int NSH = MLP_EPI_WARPS / 4, HC = 128 / NSH, ZC = T / NSH;  // shares; columns per share
     const int r = q * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t t = 0, hc = 0;
@@ -197,7 +200,7 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         tc_fence_after();
         uint8_t* hs = sm + L::HS + b * L::HS_BYTES;
 #pragma unroll 1
-        for (int cc = 64 * hf; cc < 64 * hf + 64; cc += 32) {
+        for (int cc = HC * hf; cc < HC * hf + HC; cc += 32) {
           float v[32];
           tmem_ld16x2(trow + 128 * b + cc, v, trow + 128 * b + cc + 16, v + 16);
           const float4* b4 = reinterpret_cast<const float4*>(g.b0 + j * 128 + cc);
@@ -228,16 +231,16 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // their latency overlaps the last chunk's UMMAs
       if (!ok) break;
       const long p = (long)tile * 128 + r;
-      uint4 xv[T / 16];
+      uint4 xv[ZC / 8];
       if (p < g.M) {
-        const uint4* zp = reinterpret_cast<const uint4*>(g.z + p * g.z_ld + hf * (T / 2));
+        const uint4* zp = reinterpret_cast<const uint4*>(g.z + p * g.z_ld + hf * ZC);
 #pragma unroll
-        for (int i = 0; i < T / 16; ++i) xv[i] = zp[i];
+        for (int i = 0; i < ZC / 8; ++i) xv[i] = zp[i];
       }
       if (!(ok = mbar_wait(acc_full, t & 1, SCB_ERR_WAIT_ACC))) break;
       tc_fence_after();
 #pragma unroll
-      for (int cc = hf * (T / 2); cc < (hf + 1) * (T / 2); cc += 32) {
+      for (int cc = hf * ZC; cc < (hf + 1) * ZC; cc += 32) {
         float v[32];
         tmem_ld16x2(trow + 256 + cc, v, trow + 256 + cc + 16, v + 16);
         if (p < g.M) {
@@ -245,7 +248,7 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const float4* b4 = reinterpret_cast<const float4*>(g.b2 + cc);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint4 u = xv[(cc - hf * (T / 2)) / 8 + i];
+            const uint4 u = xv[(cc - hf * ZC) / 8 + i];
             const __half2* hp = reinterpret_cast<const __half2*>(&u);
             const float4 ba = __ldg(b4 + 2 * i), bb = __ldg(b4 + 2 * i + 1);
             const float bs[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
