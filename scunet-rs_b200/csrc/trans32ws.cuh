@@ -13,8 +13,9 @@
 //      b_proj] -> LN2(x1) -> A2 -> [hid = A2.W0'^T + b0'] for the next pair while G4
 //      works on this one, in two 64-column chunks with their own TMEM buffers;
 //      z = acc + b2 -> Z
-//   G4 (8 warps, two threads per row, 32 columns of a chunk each): per chunk,
-//      2 GELU(hid) -> H -> [acc += H.(W2/2)^T]
+//   G4 (4 warps, one thread per row, the chunk's 64 columns in two halves): per
+//      chunk, 2 GELU(hid) -> H -> [acc += H.(W2/2)^T] (8 warps, two threads per row,
+//      measured 2.5 % slower: the SM's issue slots are shared by all groups)
 //
 //   x  = y_t;  x1 = x + proj(WMSA(LN1(x)));  z = x1 + mlp2(GELU(mlp0(LN2(x1))))
 //   (tools/network_scunet.py:128-136; WMSA as tools/network_scunet.py:69-102)
@@ -91,7 +92,7 @@ struct T32 {
   static constexpr uint32_t C_ACC = 320;  // 2 x 32: x1, then x1 + mlp2 (z)
   static constexpr uint32_t C_HID = 384;  // hidden accumulator (128); GELU(hidden) (A of
                                           // mlp2) overwrites the first 32 of each half
-  static constexpr int G1_WARPS = 4, G2_WARPS = 8, G3_WARPS = 4, G4_WARPS = 8;
+  static constexpr int G1_WARPS = 4, G2_WARPS = 8, G3_WARPS = 4, G4_WARPS = 4;
   static constexpr int THREADS = 32 * (G1_WARPS + G2_WARPS + G3_WARPS + G4_WARPS);
 };
 
@@ -581,10 +582,9 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       mbar_wait(drain + 2, 0, SCB_ERR_WAIT_ATTN);
     }
   } else {
-    // ====== G4 (two threads per row): per hidden chunk, 2 GELU -> H -> [acc += H.(W2/2)^T] ======
+    // ====== G4 (one thread per row): per hidden chunk, 2 GELU -> H -> [acc += H.(W2/2)^T] ======
     GroupSync gs{4, 32 * L::G4_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + L::G3_WARPS + 3), status + 6,
                  abort_flag, 0u};
-    const int hf = (warp - L::G1_WARPS - L::G2_WARPS - L::G3_WARPS) >> 2;
     for (int li = 0; li < n_local; ++li) {
       bool ok = true;
 #pragma unroll 1
@@ -594,19 +594,22 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
           break;
         }
         tc_fence_after();
-        // this thread's 32 hidden columns [32 hf, 32 hf + 32) of chunk c; the packed
-        // result (A of mlp2) goes to the first 16 of them, after they have been read
-        const uint32_t col = L::C_HID + c * 64 + hf * 32;
-        float hv[32];
-        tmem_ld16x2(trow + col, hv, trow + col + 16, hv + 16);
-        uint32_t pk[16];
+        // the row's 64 hidden columns of chunk c in two halves hf; the packed result
+        // of a half (A of mlp2) goes to its first 16 columns, after they have been read
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          __half2 a = __floats2half2_rn(hv[2 * j], hv[2 * j + 1]);
-          a = gelu2_tanh_h2(a);
-          pk[j] = *reinterpret_cast<uint32_t*>(&a);
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t col = L::C_HID + c * 64 + hf * 32;
+          float hv[32];
+          tmem_ld16x2(trow + col, hv, trow + col + 16, hv + 16);
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            __half2 a = __floats2half2_rn(hv[2 * j], hv[2 * j + 1]);
+            a = gelu2_tanh_h2(a);
+            pk[j] = *reinterpret_cast<uint32_t*>(&a);
+          }
+          tmem_st16u(trow + col, pk);
         }
-        tmem_st16u(trow + col, pk);
         tmem_wait_st();
         tc_fence_before();
         gs.sync();

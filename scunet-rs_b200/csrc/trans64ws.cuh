@@ -1,6 +1,6 @@
 // The transformer half of a half-resolution ConvTransBlock (trans width T = 64, two
 // heads of 32), warp-specialised like trans32ws.cuh (whose helpers it uses): one
-// 640-thread CTA per SM streams pairs of 8x8 windows (128 tokens, one UMMA M tile)
+// 512-thread CTA per SM streams pairs of 8x8 windows (128 tokens, one UMMA M tile)
 // through four warp groups working on different pairs ([..] = a UMMA):
 //
 //   G1 (4 warps, one thread per token row): y_t row by cp.async (a pair ahead) ->
@@ -13,7 +13,7 @@
 //      [hid_c = A2.W0'_c^T + b0'_c] for four 64-wide hidden chunks c, two TMEM
 //      buffers, each refilled as soon as its chunk's mlp2 K steps have completed;
 //      z = acc + b2 -> Z
-//   G4 (8 warps, two threads per row, 32 columns of a chunk each): per chunk,
+//   G4 (4 warps, one thread per row, a chunk's 64 columns in two halves): per chunk,
 //      2 GELU(hid_c) -> H_c (over the chunk's own columns) -> [acc += H_c.(W2_c/2)^T]
 //
 //   x  = y_t;  x1 = x + proj(WMSA(LN1(x)));  z = x1 + mlp2(GELU(mlp0(LN2(x1))))
@@ -65,7 +65,7 @@ struct T64 {
   static constexpr uint32_t C_A2 = 288;   // LN2 output (32)
   static constexpr uint32_t C_ACC = 320;  // x1, then z (64)
   static constexpr uint32_t C_HID = 384;  // two 64-column hidden chunk buffers; 2 GELU overwrites the first 32
-  static constexpr int G1_WARPS = 4, G2_WARPS = 4, G3_WARPS = 4, G4_WARPS = 8;
+  static constexpr int G1_WARPS = 4, G2_WARPS = 4, G3_WARPS = 4, G4_WARPS = 4;
   static constexpr int THREADS = 32 * (G1_WARPS + G2_WARPS + G3_WARPS + G4_WARPS);
 };
 
@@ -519,10 +519,9 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
       mbar_wait(drain + 2, 0, SCB_ERR_WAIT_ATTN);
     }
   } else {
-    // ====== G4 (two threads per row): per hidden chunk, 2 GELU -> H -> [acc += H.(W2/2)^T] ======
+    // ====== G4 (one thread per row): per hidden chunk, 2 GELU -> H -> [acc += H.(W2/2)^T] ======
     GroupSync gs{4, 32 * L::G4_WARPS, tid == 32 * (L::G1_WARPS + L::G2_WARPS + L::G3_WARPS + 3), status + 6,
                  abort_flag, 0u};
-    const int hf = (warp - L::G1_WARPS - L::G2_WARPS - L::G3_WARPS) >> 2;  // which 32 of the chunk's columns
     for (int li = 0; li < n_local; ++li) {
       bool ok = true;
 #pragma unroll 1
@@ -534,9 +533,10 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         }
         tc_fence_after();
         const uint32_t col = L::C_HID + b * 64;
-        // this thread's 32 hidden columns [32 hf, 32 hf + 32) of chunk c; the packed
-        // result goes to the first 16 of them (hidden 32 hf + 2j, + 1 at column 32 hf + j)
-        {
+        // the row's 64 hidden columns of chunk c in two halves hf; the packed result of
+        // a half goes to its first 16 columns (hidden 32 hf + 2j, + 1 at column 32 hf + j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
           float hv[32];
           tmem_ld16x2(trow + col + 32 * hf, hv, trow + col + 32 * hf + 16, hv + 16);
           uint32_t pk[16];
