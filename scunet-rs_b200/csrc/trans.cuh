@@ -34,6 +34,29 @@ struct TransGeom {
   const float *bqkv_f, *b0_f;
 };
 
+// LayerNorm of N fp32 values (no affine map: the kernels fold it into the next
+// weights) as packed fp16 pairs (x - mu) rstd, in fp32x2 arithmetic (half the FP32
+// instructions; the same sums and roundings as two scalar accumulators of the even and
+// odd elements).
+template <int N>
+__device__ __forceinline__ void ln_pack_f32x2(const float* x, uint32_t* a) {
+  float2 s = make_float2(0.f, 0.f), q = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < N; j += 2) {
+    const float2 v = make_float2(x[j], x[j + 1]);
+    s = __fadd2_rn(s, v);
+    q = __ffma2_rn(v, v, q);
+  }
+  const float mu = (s.x + s.y) * (1.f / N);
+  const float rstd = rsqrtf(fmaxf((q.x + q.y) * (1.f / N) - mu * mu, 0.f) + 1e-5f);
+  const float2 r2 = make_float2(rstd, rstd), n2 = make_float2(-mu * rstd, -mu * rstd);
+#pragma unroll
+  for (int j = 0; j < N / 2; ++j) {
+    const float2 o = __ffma2_rn(make_float2(x[2 * j], x[2 * j + 1]), r2, n2);
+    a[j] = pack_half2(o.x, o.y);
+  }
+}
+
 // Copy a row-major fp16 [R][K] matrix into K-major swizzled tiles: K split into
 // blocks of `kblk` elements (kblk*2 = row bytes = swizzle span), block b at
 // dst + b * R * kblk * 2.

@@ -306,20 +306,8 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         float x[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) unpack8(*reinterpret_cast<const uint4*>(yb + swz_off(row, c, 64)), x + 8 * c);
-        float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          s0 += x[j];
-          s1 += x[j + 1];
-          q0 = fmaf(x[j], x[j], q0);
-          q1 = fmaf(x[j + 1], x[j + 1], q1);
-        }
-        const float mu = (s0 + s1) * (1.f / T);
-        const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
-        const float nmr = -mu * rstd;
         uint32_t a[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+        ln_pack_f32x2<T>(x, a);
         tmem_st16u(trow + L::C_A1, a);  // (pair li - 1's qkv UMMA has completed)
         tmem_wait_st();
       }
@@ -403,10 +391,12 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 bb = *reinterpret_cast<const float4*>(rb + ((hf * 8 + ((c ^ tok) & 7)) << 2));
-            s[4 * c] += bb.x;
-            s[4 * c + 1] += bb.y;
-            s[4 * c + 2] += bb.z;
-            s[4 * c + 3] += bb.w;
+            const float2 lo = __fadd2_rn(make_float2(s[4 * c], s[4 * c + 1]), make_float2(bb.x, bb.y));
+            const float2 hi = __fadd2_rn(make_float2(s[4 * c + 2], s[4 * c + 3]), make_float2(bb.z, bb.w));
+            s[4 * c] = lo.x;
+            s[4 * c + 1] = lo.y;
+            s[4 * c + 2] = hi.x;
+            s[4 * c + 3] = hi.y;
           }
         }
         if (last_row || last_col) {  // warp-uniform: a warp's 32 tokens share one window
@@ -437,7 +427,10 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         // the row sum comes from the same fp16 values (the ones row of V^T)
         uint32_t p[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) p[j] = ex2_approx_h2(pack_half2(s[2 * j] - mx, s[2 * j + 1] - mx));
+        for (int j = 0; j < 16; ++j) {
+          const float2 d = __fadd2_rn(make_float2(s[2 * j], s[2 * j + 1]), make_float2(-mx, -mx));
+          p[j] = ex2_approx_h2(pack_half2(d.x, d.y));
+        }
         tmem_st16u(trow + sbuf + hf * 16, p);
         tmem_wait_st();
       }
@@ -474,20 +467,8 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       tc_fence_after();
       float x[32];
       tmem_ld16x2(trow + L::C_ACC + b * T, x, trow + L::C_ACC + b * T + 16, x + 16);
-      float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        s0 += x[j];
-        s1 += x[j + 1];
-        q0 = fmaf(x[j], x[j], q0);
-        q1 = fmaf(x[j + 1], x[j + 1], q1);
-      }
-      const float mu = (s0 + s1) * (1.f / T);
-      const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
-      const float nmr = -mu * rstd;
       uint32_t a[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+      ln_pack_f32x2<T>(x, a);
       tmem_st16u(trow + L::C_A2, a);
       tmem_wait_st();
       tc_fence_before();
@@ -517,7 +498,10 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       mbar_arrive(so_free + b);  // score buffer b may take pair li + 2's qkv
       uint32_t po[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) po[j] = pack_half2(o[2 * j] * inv, o[2 * j + 1] * inv);
+      for (int j = 0; j < 16; ++j) {
+        const float2 v = __fmul2_rn(make_float2(o[2 * j], o[2 * j + 1]), make_float2(inv, inv));
+        po[j] = pack_half2(v.x, v.y);
+      }
       tmem_st16u(trow + L::C_O, po);
       tmem_wait_st();
       tc_fence_before();
@@ -567,10 +551,12 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 bb = b24[q];
-          z[4 * q] += bb.x;
-          z[4 * q + 1] += bb.y;
-          z[4 * q + 2] += bb.z;
-          z[4 * q + 3] += bb.w;
+          const float2 lo = __fadd2_rn(make_float2(z[4 * q], z[4 * q + 1]), make_float2(bb.x, bb.y));
+          const float2 hi = __fadd2_rn(make_float2(z[4 * q + 2], z[4 * q + 3]), make_float2(bb.z, bb.w));
+          z[4 * q] = lo.x;
+          z[4 * q + 1] = lo.y;
+          z[4 * q + 2] = hi.x;
+          z[4 * q + 3] = hi.y;
         }
         uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
 #pragma unroll

@@ -202,19 +202,7 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         float x[64];
 #pragma unroll
         for (int c = 0; c < 8; ++c) unpack8(*reinterpret_cast<const uint4*>(sm + L::Y + swz_off(row, c, 128)), x + 8 * c);
-        float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 64; j += 2) {
-          s0 += x[j];
-          s1 += x[j + 1];
-          q0 = fmaf(x[j], x[j], q0);
-          q1 = fmaf(x[j + 1], x[j + 1], q1);
-        }
-        const float mu = (s0 + s1) * (1.f / T);
-        const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
-        const float nmr = -mu * rstd;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+        ln_pack_f32x2<T>(x, a);
       }
       if (li + 1 < n_local) {  // the row was read: fetch the next pair's
         cur.advance(g.win, win_step);
@@ -308,7 +296,11 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
             float bb[8];
             unpack8(*reinterpret_cast<const uint4*>(rb + ((c ^ (tok & 7)) << 4)), bb);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s[8 * c + e] += bb[e];
+            for (int e = 0; e < 8; e += 2) {
+              const float2 v = __fadd2_rn(make_float2(s[8 * c + e], s[8 * c + e + 1]), make_float2(bb[e], bb[e + 1]));
+              s[8 * c + e] = v.x;
+              s[8 * c + e + 1] = v.y;
+            }
           }
         }
         if (last_row || last_col) {  // warp-uniform: a warp's 32 tokens share one window
@@ -334,7 +326,10 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         // P'_h = 2^(s - max) as packed fp16 over this row's own S columns (read above)
         uint32_t p[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) p[j] = ex2_approx_h2(pack_half2(s[2 * j] - mx, s[2 * j + 1] - mx));
+        for (int j = 0; j < 32; ++j) {
+          const float2 d = __fadd2_rn(make_float2(s[2 * j], s[2 * j + 1]), make_float2(-mx, -mx));
+          p[j] = ex2_approx_h2(pack_half2(d.x, d.y));
+        }
         tmem_st32u(trow + hb, p);
       }
       tmem_wait_st();
@@ -377,7 +372,10 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         const float inv = __fdividef(1.f, tmem_ld1(trow + hb + 96));
         uint32_t po[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) po[j] = pack_half2(o[2 * j] * inv, o[2 * j + 1] * inv);
+        for (int j = 0; j < 16; ++j) {
+          const float2 v = __fmul2_rn(make_float2(o[2 * j], o[2 * j + 1]), make_float2(inv, inv));
+          po[j] = pack_half2(v.x, v.y);
+        }
         tmem_st16u(trow + hb + 112, po);
       }
       tmem_wait_st();
@@ -415,26 +413,18 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         float yy[8];
         unpack8(yreg[c], yy);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[8 * c + e] += yy[e];
+        for (int e = 0; e < 8; e += 2) {
+          const float2 v = __fadd2_rn(make_float2(x[8 * c + e], x[8 * c + e + 1]), make_float2(yy[e], yy[e + 1]));
+          x[8 * c + e] = v.x;
+          x[8 * c + e + 1] = v.y;
+        }
       }
       tmem_st16(trow + L::C_ACC, x);
       tmem_st16(trow + L::C_ACC + 16, x + 16);
       tmem_st16(trow + L::C_ACC + 32, x + 32);
       tmem_st16(trow + L::C_ACC + 48, x + 48);
-      float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 64; j += 2) {
-        s0 += x[j];
-        s1 += x[j + 1];
-        q0 = fmaf(x[j], x[j], q0);
-        q1 = fmaf(x[j + 1], x[j + 1], q1);
-      }
-      const float mu = (s0 + s1) * (1.f / T);
-      const float rstd = rsqrtf(fmaxf((q0 + q1) * (1.f / T) - mu * mu, 0.f) + 1e-5f);
-      const float nmr = -mu * rstd;
       uint32_t a[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) a[j] = pack_half2(fmaf(x[2 * j], rstd, nmr), fmaf(x[2 * j + 1], rstd, nmr));
+      ln_pack_f32x2<T>(x, a);
       tmem_st32u(trow + L::C_A2, a);
       tmem_wait_st();
       tc_fence_before();
@@ -492,10 +482,12 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             const float4 bb = b24[q];
-            z[4 * q] += bb.x;
-            z[4 * q + 1] += bb.y;
-            z[4 * q + 2] += bb.z;
-            z[4 * q + 3] += bb.w;
+            const float2 lo = __fadd2_rn(make_float2(z[4 * q], z[4 * q + 1]), make_float2(bb.x, bb.y));
+            const float2 hi = __fadd2_rn(make_float2(z[4 * q + 2], z[4 * q + 3]), make_float2(bb.z, bb.w));
+            z[4 * q] = lo.x;
+            z[4 * q + 1] = lo.y;
+            z[4 * q + 2] = hi.x;
+            z[4 * q + 3] = hi.y;
           }
           uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
 #pragma unroll
