@@ -166,9 +166,10 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
         const __half2* hb = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 b = __half22float2(hb[e]);
-          s[8 * c + 2 * e] = fmaf(s[8 * c + 2 * e], kScaleLog2e, b.x);
-          s[8 * c + 2 * e + 1] = fmaf(s[8 * c + 2 * e + 1], kScaleLog2e, b.y);
+          const float2 r = __ffma2_rn(make_float2(s[8 * c + 2 * e], s[8 * c + 2 * e + 1]),
+                                      make_float2(kScaleLog2e, kScaleLog2e), __half22float2(hb[e]));
+          s[8 * c + 2 * e] = r.x;
+          s[8 * c + 2 * e + 1] = r.y;
         }
       }
       if (last_row || last_col) {  // warp-uniform: the warp's tokens share a window
@@ -192,7 +193,10 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
       // row sum comes from the same fp16 values (the ones column of V)
       uint32_t p[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) p[j] = ex2_approx_h2(pack_half2(s[2 * j] - mx, s[2 * j + 1] - mx));
+      for (int j = 0; j < 32; ++j) {
+        const float2 d = __fadd2_rn(make_float2(s[2 * j], s[2 * j + 1]), make_float2(-mx, -mx));
+        p[j] = ex2_approx_h2(pack_half2(d.x, d.y));
+      }
       tmem_st32u(trow, p);
       tmem_wait_st();
     }

@@ -215,7 +215,7 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap mZ, const __grid_constant__
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 bb = __ldg(b4 + j);
-          v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+          add4_f32x2(v + 4 * j, bb);
         }
         uint8_t* blk = xp + (c >> 6) * 16384;
 #pragma unroll
@@ -258,7 +258,7 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap mZ, const __grid_constant__
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 bb = __ldg(b4 + j);
-          v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+          add4_f32x2(v + 4 * j, bb);
         }
         uint8_t* slab = sm + L::YS + (c >> 5) * 8192;
 #pragma unroll

@@ -546,7 +546,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const float4 bb = __ldg(b4 + j);
-              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+              add4_f32x2(v + 4 * j, bb);
             }
           }
           if (e.res16 && g.res_kb == 0 && p < g.M) {  // (else already in the accumulator)
@@ -558,8 +558,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float2 f = __half22float2(hp[i]);
-                v[8 * h + 2 * i] += f.x;
-                v[8 * h + 2 * i + 1] += f.y;
+                add2_f32x2(v + 8 * h + 2 * i, f.x, f.y);
               }
             }
           }
@@ -600,7 +599,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const float4 bb = __ldg(b4 + j);
-              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+              add4_f32x2(v + 4 * j, bb);
             }
           }
           if (e.act == ACT_RELU) {
@@ -685,7 +684,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 bb = __ldg(b4 + j);
-            v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+            add4_f32x2(v + 4 * j, bb);
           }
         }
         if (e.act == ACT_RELU) {
@@ -714,8 +713,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float2 f = __half22float2(hp[i]);
-                v[8 * j + 2 * i] += f.x;
-                v[8 * j + 2 * i + 1] += f.y;
+                add2_f32x2(v + 8 * j + 2 * i, f.x, f.y);
               }
             }
           }
@@ -723,7 +721,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const float4 f = *reinterpret_cast<const float4*>(base + e.st_res32 + swz_off(r, j, 128));
-              v[4 * j] += f.x; v[4 * j + 1] += f.y; v[4 * j + 2] += f.z; v[4 * j + 3] += f.w;
+              add4_f32x2(v + 4 * j, f);
             }
           }
           if (e.st_skip >= 0) {
@@ -762,7 +760,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (e.st_out16 >= 0) {
           if (e.st_skip >= 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += sk[j];
+            for (int j = 0; j < 32; j += 2) add2_f32x2(v + j, sk[j], sk[j + 1]);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -821,7 +819,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float4 bb = __ldg(b4 + j);
-            v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+            add4_f32x2(v + 4 * j, bb);
           }
         }
         if (e.act == ACT_RELU) {
@@ -910,7 +908,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float4 bb = __ldg(b4 + j);
-              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+              add4_f32x2(v + 4 * j, bb);
             }
           }
           if (p >= 0) {

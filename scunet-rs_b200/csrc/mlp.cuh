@@ -208,8 +208,10 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 bb = __ldg(b4 + i);
-            __half2 a0 = gelu_tanh_h2(__floats2half2_rn(v[4 * i] + bb.x, v[4 * i + 1] + bb.y));
-            __half2 a1 = gelu_tanh_h2(__floats2half2_rn(v[4 * i + 2] + bb.z, v[4 * i + 3] + bb.w));
+            const float2 h0 = __fadd2_rn(make_float2(v[4 * i], v[4 * i + 1]), make_float2(bb.x, bb.y));
+            const float2 h1 = __fadd2_rn(make_float2(v[4 * i + 2], v[4 * i + 3]), make_float2(bb.z, bb.w));
+            __half2 a0 = gelu_tanh_h2(__floats2half2_rn(h0.x, h0.y));
+            __half2 a1 = gelu_tanh_h2(__floats2half2_rn(h1.x, h1.y));
             pk[2 * i] = *reinterpret_cast<uint32_t*>(&a0);
             pk[2 * i + 1] = *reinterpret_cast<uint32_t*>(&a1);
           }
@@ -255,9 +257,11 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             float o[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(hp[e]);
-              o[2 * e] = v[8 * i + 2 * e] + bs[2 * e] + f.x;
-              o[2 * e + 1] = v[8 * i + 2 * e + 1] + bs[2 * e + 1] + f.y;
+              const float2 t = __fadd2_rn(make_float2(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]),
+                                          make_float2(bs[2 * e], bs[2 * e + 1]));
+              const float2 r = __fadd2_rn(t, __half22float2(hp[e]));
+              o[2 * e] = r.x;
+              o[2 * e + 1] = r.y;
             }
             zp[i] = make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]),
                                pack_half2(o[6], o[7]));

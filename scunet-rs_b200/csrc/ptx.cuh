@@ -575,6 +575,18 @@ struct WinCursor {
   }
 };
 
+// v[0..1] += (a, b) / v[0..3] += b as fp32x2 adds (Blackwell's paired FP32 pipe: half
+// the instructions, the same roundings as scalar adds).
+__device__ __forceinline__ void add2_f32x2(float* v, float a, float b) {
+  const float2 r = __fadd2_rn(make_float2(v[0], v[1]), make_float2(a, b));
+  v[0] = r.x;
+  v[1] = r.y;
+}
+__device__ __forceinline__ void add4_f32x2(float* v, float4 b) {
+  add2_f32x2(v, b.x, b.y);
+  add2_f32x2(v + 2, b.z, b.w);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
