@@ -180,15 +180,7 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
           s[j] = m ? -INFINITY : s[j];
         }
       }
-      float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
-#pragma unroll
-      for (int j = 4; j < 64; j += 4) {
-        m0 = fmaxf(m0, s[j]);
-        m1 = fmaxf(m1, s[j + 1]);
-        m2 = fmaxf(m2, s[j + 2]);
-        m3 = fmaxf(m3, s[j + 3]);
-      }
-      const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+      const float mx = row_max<64>(s);
       // P' = 2^(s - max) as packed fp16, the precision the P.V operand has anyway; the
       // row sum comes from the same fp16 values (the ones column of V)
       uint32_t p[32];

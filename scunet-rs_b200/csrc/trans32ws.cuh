@@ -408,15 +408,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
 #pragma unroll
           for (int j = 0; j < 32; ++j) s[j] = (rmask || (last_col && (qleft != ((j & 7) < 4)))) ? -INFINITY : s[j];
         }
-        float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
-#pragma unroll
-        for (int j = 4; j < 32; j += 4) {
-          m0 = fmaxf(m0, s[j]);
-          m1 = fmaxf(m1, s[j + 1]);
-          m2 = fmaxf(m2, s[j + 2]);
-          m3 = fmaxf(m3, s[j + 3]);
-        }
-        float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        float mx = row_max<32>(s);
         red[hf * 128 + row] = mx;
         tmem_wait_ld();
         tc_fence_before();

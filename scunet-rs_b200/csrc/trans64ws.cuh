@@ -314,15 +314,7 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
             s[j] = m ? -INFINITY : s[j];
           }
         }
-        float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
-#pragma unroll
-        for (int j = 4; j < 64; j += 4) {
-          m0 = fmaxf(m0, s[j]);
-          m1 = fmaxf(m1, s[j + 1]);
-          m2 = fmaxf(m2, s[j + 2]);
-          m3 = fmaxf(m3, s[j + 3]);
-        }
-        const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        const float mx = row_max<64>(s);
         // P'_h = 2^(s - max) as packed fp16 over this row's own S columns (read above)
         uint32_t p[32];
 #pragma unroll
