@@ -262,8 +262,11 @@ int scb_last_launch_count(const scb_ctx* ctx);
 /* SCB_OPT_GEMM_PAIRS (default 1): the 1x1 convs and linears whose epilogue has no
  * residual to stream in write their output tile in 64-column rounds (two 32-column
  * slabs per barrier / store round); 0 keeps 32-column rounds. Same results. */
+/* SCB_OPT_CONV3_TWIN (default 1): the 128-channel 3x3 convs (1/4 resolution) load each
+ * weight stage once for two pixel tiles, halving the weight bytes through shared
+ * memory, which bounds them; 0 loads it per tile. Same results. */
 enum { SCB_OPT_FUSE_TRANS = 1, SCB_OPT_RESIDUAL32 = 2, SCB_OPT_HOST_CHUNK = 3, SCB_OPT_TRANS32_LANES = 4,
-       SCB_OPT_FUSE_PAIR = 5, SCB_OPT_GEMM_PAIRS = 6 };
+       SCB_OPT_FUSE_PAIR = 5, SCB_OPT_GEMM_PAIRS = 6, SCB_OPT_CONV3_TWIN = 7 };
 int scb_set_option(scb_ctx* ctx, int option, int value);
 
 /* Per-launch device timing (the reference's SCUNET_PROFILE, src/cuda.rs:106-135,

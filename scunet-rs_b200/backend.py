@@ -39,6 +39,7 @@ SCB_OPT_HOST_CHUNK = 3
 SCB_OPT_TRANS32_LANES = 4
 SCB_OPT_FUSE_PAIR = 5
 SCB_OPT_GEMM_PAIRS = 6
+SCB_OPT_CONV3_TWIN = 7
 OP_CLASSES = ["head", "tail", "conv1x1", "conv3x3", "qkv", "attention", "proj", "mlp0", "mlp2", "down", "up",
               "trans_fused", "halo", "mlp"]
 

@@ -95,6 +95,10 @@ struct GemmGeom {
   // [j BK, + BK) by UMMAs of N = 32 against slices of a 32 x 32 identity B (built
   // in shared memory). Exact: fp16 x 1 summed in fp32.
   int res_kb;
+  // GEO_CONV3X, 128-wide, one N tile: 1 = two M tiles per pipeline stage (the CTA's
+  // tiles i and i + grid, one A box each) share the stage's B, halving the weight
+  // bytes each tile pulls through shared memory, the bound of these convs
+  int twin;
 };
 
 struct GemmEpi {
@@ -175,19 +179,25 @@ struct GemmSmem {
   static constexpr int A_BYTES = (A_TX + 1023) / 1024 * 1024;      // its slot: stages stay 1024-aligned
   static constexpr int B_BYTES = B_TAPS * BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // layout: stages (A, or A + B) | resident B (num_kb x B_BYTES, when b_res) | barriers | staging
-  __host__ __device__ static constexpr int stage_bytes(bool b_res) { return b_res ? A_BYTES : STAGE_BYTES; }
+  // layout: stages (A, or A + B, or A0 + A1 + B for twin tiles) | resident B (num_kb x
+  // B_BYTES, when b_res) | barriers | staging
+  __host__ __device__ static constexpr int stage_bytes(bool b_res, bool twin = false) {
+    return b_res ? A_BYTES : twin ? 2 * A_BYTES + B_BYTES : STAGE_BYTES;
+  }
   // TMEM accumulator buffers: four for narrow tiles (so the loads and MMAs of the next
-  // tiles run ahead while the epilogue drains one), two otherwise
-  static constexpr int NACC = BN <= 64 ? 4 : 2;
+  // tiles run ahead while the epilogue drains one) and for the 128-wide 3x3 convs (two
+  // twin tiles in flight), two otherwise
+  static constexpr int NACC = (BN <= 64 || (GEO == GEO_CONV3X && BN == 128)) ? 4 : 2;
   static constexpr int TMEM_COLS = (NACC * BN <= 32) ? 32 : (NACC * BN <= 64) ? 64 : (NACC * BN <= 128) ? 128
                                    : (NACC * BN <= 256) ? 256 : 512;
-  __host__ __device__ static constexpr int bres_off(int stages, bool b_res) { return stages * stage_bytes(b_res); }
-  __host__ __device__ static constexpr int bar_off(int stages, bool b_res, int num_kb) {
-    return bres_off(stages, b_res) + (b_res ? num_kb * B_BYTES : 0);
+  __host__ __device__ static constexpr int bres_off(int stages, bool b_res, bool twin = false) {
+    return stages * stage_bytes(b_res, twin);
   }
-  __host__ __device__ static constexpr int staging_off(int stages, bool b_res, int num_kb) {
-    return bar_off(stages, b_res, num_kb) + 1024;
+  __host__ __device__ static constexpr int bar_off(int stages, bool b_res, int num_kb, bool twin = false) {
+    return bres_off(stages, b_res, twin) + (b_res ? num_kb * B_BYTES : 0);
+  }
+  __host__ __device__ static constexpr int staging_off(int stages, bool b_res, int num_kb, bool twin = false) {
+    return bar_off(stages, b_res, num_kb, twin) + 1024;
   }
 };
 
@@ -305,19 +315,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   constexpr uint32_t IDESC = make_idesc_f16(128, BN);
   const int STAGES = g.stages;
   const bool b_res = g.b_res != 0;
-  const int SBYTES = L::stage_bytes(b_res);
+  // (compiled for the 128-wide conv only: at 64 channels two tiles per stage measured 15 %
+  // slower - one CTA per SM instead of two)
+  const bool twin = GEO == GEO_CONV3X && BN == 128 && g.twin != 0 && !b_res && g.n_tiles == 1;
+  const int SBYTES = L::stage_bytes(b_res, twin);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bres = smem + L::bres_off(STAGES, b_res);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES, b_res, g.num_kb));
+  uint8_t* bres = smem + L::bres_off(STAGES, b_res, twin);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off(STAGES, b_res, g.num_kb, twin));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + L::NACC;
   uint64_t* res_full = acc_empty + L::NACC;
   uint64_t* bres_full = res_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
-  uint8_t* staging = smem + L::staging_off(STAGES, b_res, g.num_kb);
+  uint8_t* staging = smem + L::staging_off(STAGES, b_res, g.num_kb, twin);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = g.m_tiles * g.n_tiles;
@@ -381,16 +394,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         mbar_arrive_expect_tx(bres_full, g.num_kb * L::B_BYTES);
         for (int kb = 0; kb < g.num_kb; ++kb) load_b(bres + kb * L::B_BYTES, bres_full, kb, 0);
       }
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      const int tstep = twin ? 2 : 1;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tstep * gridDim.x) {
         const int mt = tile / g.n_tiles, nt = tile - mt * g.n_tiles;
         const int n0 = nt * BN;
         int img, y0, x0;
         tile_origin<GEO>(g, mt, img, y0, x0);
+        // twin tiles: the CTA's next tile (one N tile, so mt1 = tile1) shares this one's stages
+        const int tile1 = tile + (int)gridDim.x;
+        const bool has1 = twin && tile1 < total_tiles;
+        int img1 = 0, y1 = 0, x1 = 0;
+        if (has1) tile_origin<GEO>(g, tile1, img1, y1, x1);
         for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
           uint8_t* sa = smem + s * SBYTES;
-          mbar_arrive_expect_tx(&full[s], b_res ? L::A_TX : L::A_TX + L::B_BYTES);
+          mbar_arrive_expect_tx(&full[s], b_res ? L::A_TX : (has1 ? 2 : 1) * L::A_TX + L::B_BYTES);
           if (GEO == GEO_UP2 && g.TW > 0) {
             tma_load_3d(sa, &tmA, &full[s], kb * BK, x0, y0);
           } else if (GEO == GEO_FLAT || GEO == GEO_UP2) {
@@ -403,6 +422,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // k block = (channel chunk, kx): one 10 x 16 box, three weight taps
             const int kx = kb % 3, ch = kb / 3;
             tma_load_4d(sa, &tmA, &full[s], ch * BK, x0 + kx - 1, y0 - 1, img);
+            if (has1) tma_load_4d(sa + L::A_BYTES, &tmA, &full[s], ch * BK, x1 + kx - 1, y1 - 1, img1);
           } else if (GEO == GEO_CONV3W) {
             // k block = channel chunk: one 20 x 10 box, all nine weight taps
             tma_load_4d(sa, &tmA, &full[s], kb * BK, x0 - 1, y0 - 1, img);
@@ -410,17 +430,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int tap = kb / g.kb_per_tap, ch = kb - tap * g.kb_per_tap;
             tma_load_5d(sa, &tmA, &full[s], ch * BK, tap & 1, x0, tap >> 1, y0);
           }
-          if (!b_res) load_b(sa + L::A_BYTES, &full[s], kb, n0);
+          if (!b_res) load_b(sa + (twin ? 2 : 1) * L::A_BYTES, &full[s], kb, n0);
         }
         if (RES_MMA) {
           for (int j = 0; j < g.res_kb && ok; ++j, ++it) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
             if (!mbar_wait(&empty[s], ph ^ 1, SCB_ERR_WAIT_EMPTY)) { ok = false; break; }
-            mbar_arrive_expect_tx(&full[s], 128 * BK * 2);
+            mbar_arrive_expect_tx(&full[s], (has1 ? 2 : 1) * 128 * BK * 2);
             if (GEO == GEO_FLAT)
               tma_load_2d(smem + s * SBYTES, &em.resA, &full[s], n0 + j * BK, mt * 128);
             else
               tma_load_4d(smem + s * SBYTES, &em.resA, &full[s], n0 + j * BK, x0, y0, img);
+            if (has1) tma_load_4d(smem + s * SBYTES + L::A_BYTES, &em.resA, &full[s], n0 + j * BK, x1, y1, img1);
           }
         }
       }
@@ -434,18 +455,33 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         ok = mbar_wait(bres_full, 0, SCB_ERR_WAIT_FULL);
         tc_fence_after();
       }
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t) {
+      const int tstep = twin ? 2 : 1;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tstep * gridDim.x, t += tstep) {
+        // twin tiles: this tile and the CTA's next one, accumulators t and t + 1
+        const bool has1 = twin && tile + (int)gridDim.x < total_tiles;
         const uint32_t a = t % L::NACC, aph = (t / L::NACC) & 1;
+        const uint32_t a1 = (t + 1) % L::NACC, aph1 = ((t + 1) / L::NACC) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, SCB_ERR_WAIT_ACC_FREE)) break;
+        if (has1 && !mbar_wait(&acc_empty[a1], aph1 ^ 1, SCB_ERR_WAIT_ACC_FREE)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + a * BN;
+        const uint32_t d_tmem = tmem_base + a * BN, d_tmem1 = tmem_base + a1 * BN;
         for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, SCB_ERR_WAIT_FULL)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * SBYTES);
-          const uint32_t sb = b_res ? smem_u32(bres + kb * L::B_BYTES) : sa + L::A_BYTES;
-          if (GEO == GEO_CONV3X) {
+          const uint32_t sb = b_res ? smem_u32(bres + kb * L::B_BYTES) : sa + (twin ? 2 : 1) * L::A_BYTES;
+          if (GEO == GEO_CONV3X && has1) {  // twin tiles: each B view feeds both tiles' UMMAs
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t bdesc = make_sdesc(sb + ky * (BN * BK * 2) + k * 32, ROWB, SWZ);
+                umma_f16(d_tmem, make_sdesc(sa + ky * 16 * ROWB + k * 32, ROWB, SWZ), bdesc, IDESC, (kb | ky | k) != 0);
+                umma_f16(d_tmem1, make_sdesc(sa + L::A_BYTES + ky * 16 * ROWB + k * 32, ROWB, SWZ), bdesc, IDESC,
+                         (kb | ky | k) != 0);
+              }
+          } else if (GEO == GEO_CONV3X) {
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
@@ -486,10 +522,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               for (int q = 0; q < 2; ++q)
                 umma_f16(d_tmem + j * BK + h * 32, make_sdesc(sa + (2 * h + q) * 32, ROWB, SWZ),
                          make_sdesc(si + q * 32, 64, SW_64B), IDESC_R, 1);
+            if (has1) {
+#pragma unroll
+              for (int h = 0; h < BK / 32; ++h)
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                  umma_f16(d_tmem1 + j * BK + h * 32, make_sdesc(sa + L::A_BYTES + (2 * h + q) * 32, ROWB, SWZ),
+                           make_sdesc(si + q * 32, 64, SW_64B), IDESC_R, 1);
+            }
             umma_commit(&empty[s]);
           }
         }
         umma_commit(&acc_full[a]);
+        if (has1) umma_commit(&acc_full[a1]);
       }
     }
   } else if (TMAEPI) {

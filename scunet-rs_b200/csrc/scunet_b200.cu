@@ -122,6 +122,7 @@ struct GemmOp {
   int geo = GEO_FLAT, bn = 64, bk = 64;
   bool tma_epi = false;
   bool pairs = false;  // TMA epilogue in 64-column rounds (flat GEMMs without residual slabs)
+  bool twin = false;   // 3x3 conv (GEO_CONV3X): two pixel tiles per pipeline stage share its B
   CUtensorMap ta, tb;
   GemmGeom g{};
   GemmEpi e{};
@@ -132,10 +133,10 @@ struct GemmOp {
 // half of TMEM (BN <= 128) try for two CTAs per SM (more epilogue warps in
 // flight); stages fill what shared memory is left after the epilogue staging and,
 // when B is resident (`bres_bytes` > 0), after the whole of B.
-void plan_launch(int bn, int a_bytes, int b_bytes, int staging_bytes, int bres_bytes, int& stages, int& ctas,
-                 int& smem) {
+void plan_launch(int bn, int a_bytes, int b_bytes, int staging_bytes, int bres_bytes, int max_ctas, int& stages,
+                 int& ctas, int& smem) {
   const int stage_bytes = bres_bytes ? a_bytes : a_bytes + b_bytes;
-  ctas = bn <= 128 ? 2 : 1;
+  ctas = std::min(bn <= 128 ? 2 : 1, max_ctas);  // max_ctas: what the kernel's TMEM columns allow
   for (;;) {
     const int budget = kSmemPerSm / ctas - 1024 /*reserved*/ - 1024 /*align*/ - 1024 /*barriers*/ - staging_bytes -
                        bres_bytes;
@@ -181,8 +182,11 @@ cudaError_t launch_t(const GemmOp& op, int sms, cudaStream_t st) {
   GemmGeom g = op.g;
   const int bres_bytes = g.num_kb * L::B_BYTES;
   g.b_res = g.n_tiles == 1 && bres_bytes <= kMaxResidentB;
+  g.twin = op.twin && GEO == GEO_CONV3X && BN == 128 && g.n_tiles == 1 && !g.b_res;
   int stages, ctas, smem;
-  plan_launch(BN, L::A_BYTES, L::B_BYTES, staging, g.b_res ? bres_bytes : 0, stages, ctas, smem);
+  // twin tiles: each stage holds two A boxes and one B
+  plan_launch(BN, g.twin ? 2 * L::A_BYTES : L::A_BYTES, L::B_BYTES, staging, g.b_res ? bres_bytes : 0,
+              512 / L::TMEM_COLS, stages, ctas, smem);
   g.stages = stages;
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = std::max(1, std::min(tiles, sms * ctas));
@@ -274,6 +278,7 @@ void pick_tile(int W, int& TW, int& TH) {
 struct Maker {
   std::string* err;
   bool pairs_enabled = true;  // SCB_OPT_GEMM_PAIRS
+  bool twin_enabled = true;   // SCB_OPT_CONV3_TWIN
   bool ok = true;
 
   bool mapB(GemmOp& op, const __half* w, int N, int K) {
@@ -362,6 +367,7 @@ struct Maker {
     op.g.tiles_y = (rows_out + TH - 1) / TH;
     op.g.m_tiles = n * op.g.tiles_y * op.g.tiles_x;
     op.g.n_tiles = 1;
+    op.twin = op.geo == GEO_CONV3X && op.bn == 128 && twin_enabled;
     return true;
   }
 
@@ -736,6 +742,7 @@ struct scb_ctx {
   bool trans32_lanes = false;  // SCB_OPT_TRANS32_LANES
   bool fuse_pair = true;       // SCB_OPT_FUSE_PAIR
   bool gemm_pairs = true;      // SCB_OPT_GEMM_PAIRS
+  bool conv3_twin = true;      // SCB_OPT_CONV3_TWIN
   // scb_forward_dev_noalloc: the device address of g_noalloc_scratch on this
   // context's device (looked up by scb_create, which loads the device code and
   // with it the array) and the plan laid out in it.
@@ -1329,7 +1336,7 @@ bool block_ops(scb_ctx* ctx, std::vector<Op>& ops, const BlockW& bw, const Arena
   const int n = R.n, H = R.H, W = R.W;
   const long P = R.px();
   const bool fused = ctx->fuse_trans && (t == 32 || t == 64);
-  Maker mk{&err, ctx->gemm_pairs};
+  Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
   Op op{};
   op.kind = Op::GEMM;
   // 1. y = conv1_1(x) + b  -> Y (fp16, both halves); LN1 of the trans half -> A
@@ -1606,7 +1613,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
-      Maker mk{&err, ctx->gemm_pairs};
+      Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
       GemmOp g{};
       if (!mk.up2(g, A.xs[lvl + 1] + Rn.off(2 * c), Rn.n, Rn.rows, Rn.W, 2 * c, ctx->wup[s - 4], c))
         return fail(ctx, SCB_EINVAL, err);
@@ -1650,7 +1657,7 @@ int build_plan(scb_ctx* ctx, Arena& A) {
       const Region Rn = region_of(A, lvl + 1);
       Op op{};
       op.kind = Op::GEMM;
-      Maker mk{&err, ctx->gemm_pairs};
+      Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
       GemmOp g{};
       if (!mk.down2(g, A.xs[lvl] + R.off(c), R.n, R.rows, R.W, c, ctx->wdown[s], 2 * c))
         return fail(ctx, SCB_EINVAL, err);
@@ -2465,6 +2472,16 @@ int scb_set_option(scb_ctx* ctx, int option, int value) {
     for (Arena& A : ctx->vbands) A.ops.clear();
     return SCB_OK;
   }
+  if (option == SCB_OPT_CONV3_TWIN) {
+    ctx->conv3_twin = value != 0;
+    ctx->arena.ops.clear();
+    ctx->arena.n = 0;
+    ctx->noalloc.ops.clear();
+    ctx->noalloc.n = 0;
+    ctx->band_arena.ops.clear();
+    for (Arena& A : ctx->vbands) A.ops.clear();
+    return SCB_OK;
+  }
   if (option == SCB_OPT_HOST_CHUNK) {
     if (value < 0) return fail(ctx, SCB_EINVAL, "SCB_OPT_HOST_CHUNK must be >= 0");
     ctx->host_chunk = value;
@@ -2552,7 +2569,7 @@ int scb_probe_gemm(scb_ctx* ctx, const void* a16, int M, int K, const void* b16,
                    const void* res16, void* out16, float* out32) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err, ctx->gemm_pairs};
+  Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
   GemmOp g{};
   if (!mk.flat(g, static_cast<const __half*>(a16), M, K, K, static_cast<const __half*>(b16), N))
     return fail(ctx, SCB_EINVAL, err);
@@ -2574,7 +2591,7 @@ int scb_probe_conv3x3(scb_ctx* ctx, const void* x16, int n, int H, int W, int ci
                       const void* res16, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err, ctx->gemm_pairs};
+  Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
   GemmOp g{};
   if (!mk.conv3(g, static_cast<const __half*>(x16), n, H, W, cin, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);
@@ -2591,7 +2608,7 @@ int scb_probe_down2(scb_ctx* ctx, const void* x16, int n, int H, int W, int cin,
                     float* out32, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err, ctx->gemm_pairs};
+  Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
   GemmOp g{};
   if (!mk.down2(g, static_cast<const __half*>(x16), n, H, W, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);
@@ -2607,7 +2624,7 @@ int scb_probe_up2(scb_ctx* ctx, const void* x16, int n, int h, int w, int cin, c
                   float* out32, void* out16) {
   if (!ctx) return fail(nullptr, SCB_EINVAL, "ctx is NULL");
   std::string err;
-  Maker mk{&err, ctx->gemm_pairs};
+  Maker mk{&err, ctx->gemm_pairs, ctx->conv3_twin};
   GemmOp g{};
   if (!mk.up2(g, static_cast<const __half*>(x16), n, h, w, cin, static_cast<const __half*>(w16), cout))
     return fail(ctx, SCB_EINVAL, err);

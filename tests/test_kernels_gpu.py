@@ -95,6 +95,35 @@ def test_conv3x3(be3, n, H, W, cin, act, res):
     close(f"conv3x3 {n}x{H}x{W}x{cin}", ref, out.float().cpu().numpy(), 2e-3)
 
 
+@pytest.mark.parametrize("cin,act,res", [(128, 1, False), (128, 0, True)])
+def test_conv3x3_twin_tiles(scb, be3, cin, act, res):
+    """Two pixel tiles per weight stage (SCB_OPT_CONV3_TWIN, the 128-channel 3x3 convs)
+    on an image with several tiles per CTA, an odd count included: the same fp16
+    results as one tile per stage, and the float64 reference at the usual bar."""
+    torch = _torch()
+    n, H, W = 3, 72, 200  # 9 x 13 tiles per image: 351 tiles over the SMs
+    rng = np.random.default_rng(7 * cin + act)
+    x = h16(rng, (n, H, W, cin))
+    w = h16(rng, (cin, cin, 3, 3), (9 * cin) ** -0.5).astype(np.float32)
+    wk = np.ascontiguousarray(w.transpose(0, 2, 3, 1)).astype(np.float16)
+    r16 = h16(rng, (n, H, W, cin)) if res else None
+    tx, tw = torch.from_numpy(x).cuda(), torch.from_numpy(wk).cuda()
+    tr = torch.from_numpy(r16).cuda() if res else None
+    outs = []
+    try:
+        for mode in (1, 0):
+            be3.set_option(scb.backend.SCB_OPT_CONV3_TWIN, mode)
+            out = torch.empty((n, H, W, cin), dtype=torch.float16, device="cuda")
+            rc = be3.lib.scb_probe_conv3x3(be3.ctx, tx.data_ptr(), n, H, W, cin, tw.data_ptr(), cin, act,
+                                           tr.data_ptr() if res else None, out.data_ptr())
+            assert rc == 0, be3.lib.scb_last_error(be3.ctx)
+            outs.append(out.cpu().numpy())
+    finally:
+        be3.set_option(scb.backend.SCB_OPT_CONV3_TWIN, 1)
+    assert np.array_equal(outs[0], outs[1])
+    close(f"conv3x3 twin {n}x{H}x{W}x{cin}", conv3_ref(torch, x, w, act, r16), outs[0].astype(np.float32), 2e-3)
+
+
 @pytest.mark.parametrize("n,H,W,cin", [(2, 16, 32, 64), (1, 16, 16, 128), (1, 16, 16, 256), (3, 8, 24, 64)])
 def test_down2(be3, n, H, W, cin):
     torch = _torch()
