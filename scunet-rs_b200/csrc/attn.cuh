@@ -11,7 +11,7 @@
 //   (tools/network_scunet.py:49-67, cuda/scunet.cu:137-147);
 //   softmax over the 64 keys, O = P.v.
 //
-// Persistent CTAs of 128 threads (three per SM, 128 TMEM columns each) walk pairs of
+// Persistent CTAs of 128 threads (four per SM, 128 TMEM columns each) walk pairs of
 // windows (128 tokens, one UMMA M tile), one thread per token row; a CTA keeps one
 // head. Per pair:
 //   q, k  -> smem [128 x 32] fp16 K-major (64B swizzle)            (UMMA A and B)
@@ -26,8 +26,11 @@
 //                     token of window s reads columns 32 + 32 s .. + 31 and the row
 //                     sum of the fp16 P' it was multiplied with at column 96
 //   out = O / rowsum: fp16 to the output plane at the token's pixel.
-// The next pair's q, k, v are copied (cp.async) into a second operand buffer while
-// the current pair computes, so no pair waits a DRAM round trip.
+// The next pair's v is copied (cp.async) into a second operand buffer while the
+// current pair computes, and its q and k into the single Q and K buffers as soon as
+// this pair's S has been computed from them, so no pair waits a DRAM round trip; one
+// Q / K buffer instead of two keeps a CTA's shared memory small enough for four CTAs
+// per SM (three measured slower).
 #pragma once
 #include "ptx.cuh"
 
@@ -41,18 +44,19 @@ struct AttnGeom {
   long out_ld;     // elements per pixel row of out
 };
 
-// Layout per CTA (3 CTAs per SM, 128 TMEM columns each). A CTA keeps one head h for
-// its whole life, so its relative-position bias table is built once. The q, k, v rows
-// of the next pair are copied by cp.async straight into the other of two operand
-// buffers while the current pair computes.
-constexpr int ATT_Q = 0;                  // 2 x [128 x 64 B] SW64
-constexpr int ATT_K = 16384;              // 2 x [128 x 64 B] SW64
-constexpr int ATT_V = 32768;              // 2 x V, MN-major: [64 keys x 128 B] = [V_0 | V_1]
-constexpr int ATT_ONES = 49152;           // [64 keys x 128 B]: N element 64 = 1 (the row sums)
+// Layout per CTA (4 CTAs per SM, 128 TMEM columns each). A CTA keeps one head h for
+// its whole life, so its relative-position bias table is built once. The v rows of
+// the next pair are copied by cp.async straight into the other of two V buffers while
+// the current pair computes; its q and k rows into the one Q / K buffer once this
+// pair's S is done.
+constexpr int ATT_Q = 0;                  // [128 x 64 B] SW64
+constexpr int ATT_K = 8192;               // [128 x 64 B] SW64
+constexpr int ATT_V = 16384;              // 2 x V, MN-major: [64 keys x 128 B] = [V_0 | V_1]
+constexpr int ATT_ONES = 32768;           // [64 keys x 128 B]: N element 64 = 1 (the row sums)
 constexpr int ATT_BIAS = ATT_ONES + 8192; // fp16 [64 query positions][64 keys], log2 units, chunk-swizzled
 constexpr int ATT_BAR = ATT_BIAS + 8192;
 constexpr int ATT_SMEM = ATT_BAR + 64 + 1024;
-constexpr int ATT_CTAS = 3;               // per SM
+constexpr int ATT_CTAS = 4;               // per SM
 constexpr int ATT_THREADS = 128;          // one per token row of a window pair
 
 __global__ void __launch_bounds__(ATT_THREADS, ATT_CTAS)
@@ -106,15 +110,22 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     if (pr >= n_pairs || win >= g.win.n_windows) return -1;
     return win_token_pixel(g.win, win, qi, qj, lr, lc, st);
   };
-  // this token's q, k, v of head h (3 x 64 bytes) -> Q, K rows and V row tok, N
-  // elements [32 slot, +32), of operand buffer b; zeros past the last window
-  auto fetch_qkv = [&](long pix, int b) {
+  // this token's v of head h (64 bytes) -> V row tok, N elements [32 slot, +32), of V
+  // buffer b; its q and k -> the Q and K rows; zeros past the last window. One
+  // cp.async group each.
+  auto fetch_v = [&](long pix, int b) {
+    const __half* src = pix >= 0 ? qkv + pix * g.qkv_ld + h * 32 : qkv;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      cp_async16(sm + ATT_V + b * 8192 + swz_off(tok, 4 * slot + c, 128), src + 2 * g.t + 8 * c, pix >= 0);
+    cp_async_commit();
+  };
+  auto fetch_qk = [&](long pix) {
     const __half* src = pix >= 0 ? qkv + pix * g.qkv_ld + h * 32 : qkv;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      cp_async16(sm + ATT_Q + b * 8192 + swz_off(row, c, 64), src + 8 * c, pix >= 0);
-      cp_async16(sm + ATT_K + b * 8192 + swz_off(row, c, 64), src + g.t + 8 * c, pix >= 0);
-      cp_async16(sm + ATT_V + b * 8192 + swz_off(tok, 4 * slot + c, 128), src + 2 * g.t + 8 * c, pix >= 0);
+      cp_async16(sm + ATT_Q + swz_off(row, c, 64), src + 8 * c, pix >= 0);
+      cp_async16(sm + ATT_K + swz_off(row, c, 64), src + g.t + 8 * c, pix >= 0);
     }
     cp_async_commit();
   };
@@ -133,26 +144,29 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
   long pair = p0;
   bool lr, lc, st;
   long pix = locate(pair, lr, lc, st);
-  fetch_qkv(pix, 0);
+  fetch_v(pix, 0);
+  fetch_qk(pix);
   for (int u = 0; pair < n_pairs; pair += pstride, ++u) {
     const int b = u & 1;
     const bool last_row = lr, last_col = lc, store = st;
     const long pix_c = pix;
-    // the next pair's q, k, v stream into buffer b ^ 1 (its last readers, the S and
-    // P.V UMMAs of pair u - 1, have completed) while this pair computes
+    // the next pair's v streams into V buffer b ^ 1 (its last reader, the P.V UMMA of
+    // pair u - 1, has completed) while this pair computes
     pix = locate(pair + pstride, lr, lc, st);
-    fetch_qkv(pix, b ^ 1);
-    cp_async_wait_1();  // this thread's rows of pair u have landed
+    fetch_v(pix, b ^ 1);
+    cp_async_wait_1();  // this thread's rows of pair u have landed (all but the group above)
     sync_mma();
     if (tid == 0) {  // S = Q K^T -> TMEM [0, 128)
       constexpr uint32_t id = make_idesc_f16(128, 128);
 #pragma unroll
       for (int k = 0; k < 2; ++k)
-        umma_f16(tmem, make_sdesc(sb + ATT_Q + b * 8192 + k * 32, 64, SW_64B),
-                 make_sdesc(sb + ATT_K + b * 8192 + k * 32, 64, SW_64B), id, k);
+        umma_f16(tmem, make_sdesc(sb + ATT_Q + k * 32, 64, SW_64B), make_sdesc(sb + ATT_K + k * 32, 64, SW_64B), id,
+                 k);
       umma_commit(bar);
     }
     wait_mma();
+    // S has read Q and K: the next pair's q and k stream in while this pair finishes
+    fetch_qk(pix);
 
     // ---- softmax over the row's 64 in-window keys -> P' (TMEM [0, 32), fp16) ----
     {
