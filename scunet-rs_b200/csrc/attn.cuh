@@ -30,7 +30,11 @@
 // current pair computes, and its q and k into the single Q and K buffers as soon as
 // this pair's S has been computed from them, so no pair waits a DRAM round trip; one
 // Q / K buffer instead of two keeps a CTA's shared memory small enough for four CTAs
-// per SM (three measured slower).
+// per SM (three measured slower). Global loads and stores go four lanes per token
+// (a token's 64 bytes of one head in one 16-byte chunk per lane, eight tokens per
+// instruction, the pixel of each token passed by shuffle, the output staged through
+// shared memory): with one lane per token every instruction touched 32 different
+// rows, and the load/store unit's per-row work, not DRAM, set the kernel's pace.
 #pragma once
 #include "ptx.cuh"
 
@@ -110,22 +114,32 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
     if (pr >= n_pairs || win >= g.win.n_windows) return -1;
     return win_token_pixel(g.win, win, qi, qj, lr, lc, st);
   };
-  // this token's v of head h (64 bytes) -> V row tok, N elements [32 slot, +32), of V
-  // buffer b; its q and k -> the Q and K rows; zeros past the last window. One
-  // cp.async group each.
+  // The v (q, k) rows of head h of the warp's 32 tokens -> V rows tok, N elements
+  // [32 slot, +32), of V buffer b (the Q and K rows); zeros past the last window. Lane
+  // l copies 16-byte chunk l % 4 of the tokens of rows l / 4 + 8 k (k < 4), whose
+  // pixel it takes from that row's lane (`pix`: the pixel of this lane's own row), so
+  // one copy instruction covers eight whole 64-byte rows instead of one chunk of 32.
+  // One cp.async group each.
   auto fetch_v = [&](long pix, int b) {
-    const __half* src = pix >= 0 ? qkv + pix * g.qkv_ld + h * 32 : qkv;
+    const int c = lane & 3;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-      cp_async16(sm + ATT_V + b * 8192 + swz_off(tok, 4 * slot + c, 128), src + 2 * g.t + 8 * c, pix >= 0);
+    for (int k = 0; k < 4; ++k) {
+      const int sl = (lane >> 2) + 8 * k, rr = warp * 32 + sl;
+      const long pk = __shfl_sync(0xffffffffu, pix, sl);
+      const __half* src = pk >= 0 ? qkv + pk * g.qkv_ld + h * 32 : qkv;
+      cp_async16(sm + ATT_V + b * 8192 + swz_off(rr & 63, 4 * (rr >> 6) + c, 128), src + 2 * g.t + 8 * c, pk >= 0);
+    }
     cp_async_commit();
   };
   auto fetch_qk = [&](long pix) {
-    const __half* src = pix >= 0 ? qkv + pix * g.qkv_ld + h * 32 : qkv;
+    const int c = lane & 3;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      cp_async16(sm + ATT_Q + swz_off(row, c, 64), src + 8 * c, pix >= 0);
-      cp_async16(sm + ATT_K + swz_off(row, c, 64), src + g.t + 8 * c, pix >= 0);
+    for (int k = 0; k < 4; ++k) {
+      const int sl = (lane >> 2) + 8 * k, rr = warp * 32 + sl;
+      const long pk = __shfl_sync(0xffffffffu, pix, sl);
+      const __half* src = pk >= 0 ? qkv + pk * g.qkv_ld + h * 32 : qkv;
+      cp_async16(sm + ATT_Q + swz_off(rr, c, 64), src + 8 * c, pk >= 0);
+      cp_async16(sm + ATT_K + swz_off(rr, c, 64), src + g.t + 8 * c, pk >= 0);
     }
     cp_async_commit();
   };
@@ -223,14 +237,25 @@ window_attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, con
       float o[32];
       tmem_ld16x2(trow + 32 + slot * 32, o, trow + 48 + slot * 32, o + 16);  // this token's window's half of O'
       const float inv = __fdividef(1.f, tmem_ld1(trow + 96));
-      if (pix_c >= 0 && store) {
-        uint4* dst = reinterpret_cast<uint4*>(out + pix_c * g.out_ld + h * 32);
+      // the row's 64 output bytes -> the current V tile (its P.V has completed) as
+      // staging, then each lane stores chunk l % 4 of rows l / 4 + 8 k: one store
+      // instruction writes eight whole 64-byte rows
+      uint8_t* stg = sm + ATT_V + b * 8192;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          dst[c] = make_uint4(pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv),
-                              pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
-                              pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
-                              pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(stg + row * 64 + 16 * (c ^ (row & 3))) =
+            make_uint4(pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv), pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                       pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
+                       pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+      __syncwarp();
+      const long mine = (pix_c >= 0 && store) ? pix_c : -1;
+      const int c = lane & 3;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int sl = (lane >> 2) + 8 * k, rr = warp * 32 + sl;
+        const long pk = __shfl_sync(0xffffffffu, mine, sl);
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + 16 * (c ^ (rr & 3)));
+        if (pk >= 0) *reinterpret_cast<uint4*>(out + pk * g.out_ld + h * 32 + 8 * c) = v;
       }
     }
     tc_fence_before();
