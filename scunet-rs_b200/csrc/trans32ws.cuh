@@ -281,13 +281,21 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
     GroupSync gs{1, 32 * L::G1_WARPS, tid == 0, status, abort_flag, 0u};
     WinCursor cur;
     cur.init(g.win, 2 * first + slot);
-    auto fetch = [&](int li) {  // the cursor stands at pair li
+    // the cursor stands at pair li: the y_t rows of the warp's 32 tokens, lane l copying
+    // 16-byte chunk l % 4 of rows l / 4 + 8 k (pixel by shuffle from the row's lane), so
+    // that one copy instruction covers eight whole 64-byte rows
+    auto fetch = [&](int li) {
       bool lr, lc, st;
       const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
       uint8_t* dst = sm + L::Y + (li % 3) * 8192;
-      const __half* src = pix >= 0 ? g.y + pix * T : g.y;
+      const int c = lane & 3;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) cp_async16(dst + swz_off(row, c, 64), src + 8 * c, pix >= 0);
+      for (int k = 0; k < 4; ++k) {
+        const int sl = (lane >> 2) + 8 * k;
+        const long pk = __shfl_sync(0xffffffffu, pix, sl);
+        const __half* src = pk >= 0 ? g.y + pk * T : g.y;
+        cp_async16(dst + swz_off((warp & 3) * 32 + sl, c, 64), src + 8 * c, pk >= 0);
+      }
     };
     if (n_local > 0) fetch(0);
     cp_async_commit();
@@ -300,7 +308,8 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
         fetch(li + 1);
       }
       cp_async_commit();
-      cp_async_wait_1();  // this thread's row of pair li has landed
+      cp_async_wait_1();  // this thread's copies of pair li have landed,
+      __syncwarp();       // and those of the other lanes, which hold this row's chunks
       {
         const uint8_t* yb = sm + L::Y + (li % 3) * 8192;
         float x[32];
@@ -538,7 +547,7 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
       tc_fence_before();
       bool lr, lc, st;
       const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
-      if (pix >= 0 && st) {
+      {
         const float4* b24 = reinterpret_cast<const float4*>(sm + L::B2F);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -550,9 +559,11 @@ __global__ void __launch_bounds__(T32::THREADS, 1) trans32_ws_kernel(const Trans
           z[4 * q + 2] = hi.x;
           z[4 * q + 3] = hi.y;
         }
-        uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
+        if (pix >= 0 && st) {
+          uint4* dst = reinterpret_cast<uint4*>(g.z + pix * (2 * T) + T);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) dst[c] = pack8(z + 8 * c);
+          for (int c = 0; c < 4; ++c) dst[c] = pack8(z + 8 * c);
+        }
       }
     }
     if (gs.leader) {

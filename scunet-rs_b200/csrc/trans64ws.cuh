@@ -186,17 +186,26 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
     GroupSync gs{1, 32 * L::G1_WARPS, tid == 0, status, abort_flag, 0u};
     WinCursor cur;
     cur.init(g.win, 2 * first + slot);
-    auto fetch = [&]() {  // this thread's y_t row of the pair the cursor stands at
+    // the y_t rows of the warp's 32 tokens at the pair the cursor stands at, lane l
+    // copying 16-byte chunk l % 8 of rows l / 8 + 4 k (pixel by shuffle from the row's
+    // lane): one copy instruction covers four whole 128-byte rows
+    auto fetch = [&]() {
       bool lr, lc, st;
       const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
-      const __half* src = pix >= 0 ? g.y + pix * T : g.y;
+      const int c = lane & 7;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) cp_async16(sm + L::Y + swz_off(row, c, 128), src + 8 * c, pix >= 0);
+      for (int k = 0; k < 8; ++k) {
+        const int sl = (lane >> 3) + 4 * k;
+        const long pk = __shfl_sync(0xffffffffu, pix, sl);
+        const __half* src = pk >= 0 ? g.y + pk * T : g.y;
+        cp_async16(sm + L::Y + swz_off((warp & 3) * 32 + sl, c, 128), src + 8 * c, pk >= 0);
+      }
       cp_async_commit();
     };
     if (n_local > 0) fetch();
     for (int li = 0; li < n_local; ++li) {
-      cp_async_wait_all();  // this thread's row of pair li has landed
+      cp_async_wait_all();  // this thread's copies of pair li have landed,
+      __syncwarp();         // and those of the other lanes, which hold this row's chunks
       uint32_t a[32];
       {
         float x[64];
@@ -204,7 +213,8 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
         for (int c = 0; c < 8; ++c) unpack8(*reinterpret_cast<const uint4*>(sm + L::Y + swz_off(row, c, 128)), x + 8 * c);
         ln_pack_f32x2<T>(x, a);
       }
-      if (li + 1 < n_local) {  // the row was read: fetch the next pair's
+      if (li + 1 < n_local) {  // the warp's rows were read: fetch the next pair's
+        __syncwarp();
         cur.advance(g.win, win_step);
         fetch();
       }
