@@ -54,7 +54,8 @@ struct T64 {
   // [V_0 | V_1] of the head, and one shared atom whose first N element is 1
   static constexpr int V = K + 2 * 8192;             // V_0, V_1, ones atom (8 KB each)
   static constexpr int B2F = V + 3 * 8192;           // mlp2 bias, 64 floats
-  static constexpr int BAR = B2F + 256;
+  static constexpr int YS = B2F + 256;               // [128 x 128 B] y_t rows of the next x1 (G3)
+  static constexpr int BAR = YS + 128 * 128;
   static constexpr int SMEM = BAR + 256 + 1024;      // + alignment slack
   // TMEM columns (packed fp16 A operands: 8 columns per K step of 16)
   static constexpr uint32_t C_SB = 0;     // score buffer [0, 256): qkv acc [0, 192), A1 [192, 224);
@@ -395,14 +396,12 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
       return true;
     };
     auto ln2 = [&](int li) -> bool {  // x1 = acc + y_t (back into TMEM) -> LN2 -> A2; cursor at pair li
-      uint4 yreg[8];  // this row's y_t (fp16, packed; prefetched to L2 during the previous pair's MLP)
-      {
-        bool lr, lc, st;
-        const long pix = cur.pixel(g.win, qi, qj, lr, lc, st);
+      uint4 yreg[8];  // this row's y_t (fp16, packed; staged during the previous pair's MLP)
+      cp_async_wait_all();
+      __syncwarp();  // the warp's lanes copied this row's chunks
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          yreg[c] = pix >= 0 ? __ldg(reinterpret_cast<const uint4*>(g.y + pix * T) + c) : make_uint4(0u, 0u, 0u, 0u);
-      }
+      for (int c = 0; c < 8; ++c) yreg[c] = *reinterpret_cast<const uint4*>(sm + L::YS + swz_off(row, c, 128));
+      __syncwarp();  // read before the next pair's rows are staged
       if (!gs.wait(x1_done, li & 1, SCB_ERR_WAIT_ATTN)) return false;
       tc_fence_after();
       float x[64];
@@ -441,6 +440,24 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
       umma_f16(d, d64(L::ONES), d64(L::B_0 + c * 64 * 64), ID_H64, 1);
       umma_commit(bar_hid + (c & 1));
     };
+    // the y_t rows of the warp's 32 tokens at the pair cursor `cs` stands at -> YS, lane
+    // l copying 16-byte chunk l % 8 of rows l / 8 + 4 k (pixel by shuffle from the row's
+    // lane): four whole 128-byte rows per copy instruction, and ln2 reads its row from
+    // shared memory instead of waiting on 32 scattered global loads
+    auto stage_y = [&](WinCursor& cs) {
+      bool lr, lc, st;
+      const long pix = cs.pixel(g.win, qi, qj, lr, lc, st);
+      const int c = lane & 7;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int sl = (lane >> 3) + 4 * k;
+        const long pk = __shfl_sync(0xffffffffu, pix, sl);
+        const __half* src = pk >= 0 ? g.y + pk * T : g.y;
+        cp_async16(sm + L::YS + swz_off((warp & 3) * 32 + sl, c, 128), src + 8 * c, pk >= 0);
+      }
+      cp_async_commit();
+    };
+    if (n_local > 0) stage_y(cur);
     bool ok = n_local > 0 && normproj(0) && ln2(0);
     if (ok) {
       gs.sync();
@@ -452,11 +469,9 @@ __global__ void __launch_bounds__(T64::THREADS, 1) trans64_ws_kernel(const Trans
     WinCursor nxt = cur;  // one pair ahead: whose y_t is fetched during this pair's MLP
     for (int li = 0; ok && li < n_local; ++li) {
       bool fine = true;
-      if (li + 1 < n_local) {  // warm L2 with the next pair's y_t rows for its ln2
+      if (li + 1 < n_local) {  // stage the next pair's y_t rows for its ln2
         nxt.advance(g.win, win_step);
-        bool lr, lc, st;
-        const long pix = nxt.pixel(g.win, qi, qj, lr, lc, st);
-        if (pix >= 0) prefetch_l2(g.y + pix * T);
+        stage_y(nxt);
       }
       // chunk c of pair li lives in buffer c & 1; its mlp2 completing frees the
       // buffer for chunk c + 2 (buffer b's u-th use: u = 2 li + c / 2)
