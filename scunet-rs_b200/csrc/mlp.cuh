@@ -43,7 +43,11 @@ struct MlpLayout {
   static constexpr int A_OFF = 0;
   static constexpr int RING = A_OFF + A_BYTES;
   static constexpr int HS = RING + STAGES * STAGE;          // two chunk buffers
-  static constexpr int BAR = HS + 2 * HS_BYTES;
+  // T = 128: the tile's x1 rows [128 x 256 B], staged by coalesced copies at the tile's
+  // start (at T = 256 there is no room: x1 is loaded straight into registers)
+  static constexpr bool X1_STAGED = T == 128;
+  static constexpr int X1S = HS + 2 * HS_BYTES;
+  static constexpr int BAR = X1S + (X1_STAGED ? 128 * T * 2 : 0);
   static constexpr int SMEM = BAR + 256 + 1024;
   static constexpr int TMEM_COLS = 512;                     // H: [0, 128) and [128, 256); acc: [256, 256 + T)
 };
@@ -192,6 +196,21 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint32_t t = 0, hc = 0;
     bool ok = true;  // a timed-out wait (error recorded) ends the loops; the final barrier still runs
     for (int tile = blockIdx.x; tile < g.m_tiles && ok; tile += gridDim.x, ++t) {
+      if (L::X1_STAGED) {
+        // this warp's share of the tile's x1 (rows 32 q .. + 31, 16-byte chunks 4 hf .. + 3
+        // of each 256-byte row) -> X1S, lane l copying chunk 4 hf + l % 4 of rows l / 4 + 8 k:
+        // eight rows per copy instruction instead of 32 scattered ones; chunks XOR-swizzled
+        // by row % 8
+        const int ch = 4 * hf + (lane & 3);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int rr = q * 32 + (lane >> 2) + 8 * k;
+          const long pr = (long)tile * 128 + rr;
+          const __half* src = pr < g.M ? g.z + pr * g.z_ld + 8 * ch : g.z;
+          cp_async16(sm + L::X1S + rr * 256 + 16 * (ch ^ (rr & 7)), src, pr < g.M);
+        }
+        cp_async_commit();
+      }
       for (int j = 0; j < L::NCH && ok; ++j) {
         const uint32_t c = hc + j, b = c & 1, ph = (c >> 1) & 1;
         // H_j in TMEM, and the Hs buffer's previous chunk consumed by its UMMAs
@@ -234,7 +253,14 @@ mlp_fused_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       if (!ok) break;
       const long p = (long)tile * 128 + r;
       uint4 xv[ZC / 8];
-      if (p < g.M) {
+      if (L::X1_STAGED) {
+        cp_async_wait_all();
+        __syncwarp();  // the warp's lanes copied this row's chunks
+#pragma unroll
+        for (int i = 0; i < ZC / 8; ++i)
+          xv[i] = *reinterpret_cast<const uint4*>(sm + L::X1S + r * 256 + 16 * ((4 * hf + i) ^ (r & 7)));
+        __syncwarp();  // read before the next tile's rows are staged
+      } else if (p < g.M) {
         const uint4* zp = reinterpret_cast<const uint4*>(g.z + p * g.z_ld + hf * ZC);
 #pragma unroll
         for (int i = 0; i < ZC / 8; ++i) xv[i] = zp[i];
