@@ -410,10 +410,6 @@ __device__ __forceinline__ uint32_t swz_off(uint32_t row, uint32_t chunk, uint32
   return row * row_bytes + (((chunk ^ phase) & mask) << 4);
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 // 16-byte asynchronous global -> shared copy by this thread (bypassing L1); when
 // `valid` is false nothing is read and the 16 bytes are zero-filled. Completion is
 // per thread: cp_async_wait_all() makes this thread's copies visible to itself.
