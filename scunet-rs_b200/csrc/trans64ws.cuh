@@ -23,8 +23,9 @@
 // attention stage of a pair (qkv, S of both heads, P', O', O) uses one 256-column
 // score buffer, so a pair's qkv waits until the previous pair's proj has read its O;
 // there is one x1 / z accumulator (64 columns), so a pair's proj follows the previous
-// pair's z; y_t enters x1 on the CUDA cores (no shared-memory room for y_t operand
-// tiles); the rel-pos bias table is fp16. Numerics as trans32ws.cuh: LayerNorm
+// pair's z; y_t enters x1 on the CUDA cores (the G3 threads read their rows from a
+// shared-memory copy staged during the previous pair's MLP, not from a y_t operand tile
+// of an identity UMMA); the rel-pos bias table is fp16. Numerics as trans32ws.cuh: LayerNorm
 // affine maps and the attention scale folded into the weights on the host, biases
 // of qkv, proj and mlp0 through a ones K step (fp16 high + remainder), softmax row
 // sums from the fp16 P' via a ones column of the MN-major V operand, the GELU's 1/2
